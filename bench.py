@@ -1,0 +1,389 @@
+#!/usr/bin/env python
+"""Benchmark of the oblivious-tree training hot path on B200 (one JSON line on rank 0).
+
+Headline workload ("C2"): 1M rows x 54 features (Covertype-shaped
+seeded synthetic data), 255 bins, depth 6, 200 trees, lr 0.3, logistic loss.
+  value   device time (CUDA events on the library stream) of one 200-tree fit's tree
+          loop with the binned dataset resident in HBM -- the quantity the reference
+          reports as train_s (src/booster.rs:335-504).
+  e2e     the same fit through the C ABI from pinned host buffers: H2D of x/y, GPU
+          binning, the tree loop and the model D2H (rw_fit, or rw_dataset_create +
+          rw_fit_dataset per rank), timed with events on the library stream.
+Multi-GPU (torchrun): weak scaling, 1M rows per GPU; per-level histograms are summed
+with NCCL inside the library; value is the max over ranks.
+Also reported: the histogram kernel's roofline, predict rows/s (C5: 500-tree depth-6
+random model on 1e8 u8 rows per GPU), the CPU baseline (oracle port of src/cpu.rs on
+this host's cores, bounded sample), clocks during the timed region.
+
+--impl reference: times the reference's CPU trainer (its restatement, see oracle/) on
+the same workload with all host threads, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "train s/200 trees @1M×54 d6"
+WORKLOAD = ("C2: 1M rows x 54 f32 features per GPU (10 U[0,1], 34 integer 0-360, 10 binary; "
+            "one-vs-rest of a 7-class linear-argmax label), 255 quantile bins, depth 6, "
+            "200 trees, lr 0.3, logistic")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--rows", type=int, default=1_000_000, help="training rows per GPU")
+    ap.add_argument("--trees", type=int, default=200)
+    ap.add_argument("--predict-rows", type=int, default=100_000_000)
+    ap.add_argument("--cpu-trees", type=int, default=5,
+                    help="trees in the bounded CPU-baseline sample")
+    ap.add_argument("--no-cpu", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    return rank, world, local
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling in the background during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(gpu)], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.f.flush()
+        self.f.seek(0)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.f.read().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        os.unlink(self.f.name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def read_traffic():
+    """DRAM bytes per histogram launch from the committed ncu summary, if present."""
+    path = os.path.join(ROOT, "profiles", "k_hist_c2_traffic.txt")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.startswith("traffic_bytes_per_launch:"):
+            return float(line.split(":", 1)[1])
+    return None
+
+
+def hbm_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        return float(json.load(open(path))["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def c2_cfg(trees):
+    from rustwood_b200 import Config
+    return Config(n_trees=trees, depth=6, n_bins=255, learning_rate=0.3, objective="logistic")
+
+
+def cpu_baseline(x, y, cuts, base, trees_sample, total_trees):
+    import oracle
+    nt = oracle.default_threads()
+    r = oracle.train(x, y, cuts, base, n_trees=trees_sample, depth=6, n_bins=255,
+                     learning_rate=0.3, exact=False, n_threads=nt)
+    return {"value": r.loop_seconds * total_trees / trees_sample, "unit": "s", "cores": nt,
+            "kind": "port",
+            "sample": f"C2 1M x 54: tree loop of the first {trees_sample} of {total_trees} trees "
+                      f"on oracle_ref (src/cpu.rs restated, {nt} threads), extrapolated "
+                      f"x{total_trees / trees_sample:g}; binning excluded as in the GPU value"}
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    import oracle
+    from rustwood_b200 import synth
+    x, y, _, _ = synth.c2(args.rows, seed=0)
+    cuts = oracle.compute_boundaries(x, 255)
+    base = oracle.base_score(y, "logistic")
+    nt = oracle.default_threads()
+    sample = max(1, min(args.cpu_trees, args.trees))
+    times = []
+    for i in range(args.warmup + args.steps):
+        r = oracle.train(x, y, cuts, base, n_trees=sample, depth=6, n_bins=255,
+                         learning_rate=0.3, exact=False, n_threads=nt)
+        if i >= args.warmup:
+            times.append(r.loop_seconds * args.trees / sample)
+    v = statistics.mean(times)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": v * 1e3,
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded numpy, Covertype-shaped)",
+        "config": {"workload": WORKLOAD, "rows_per_gpu": args.rows},
+        "cpu_baseline": {"value": v, "unit": "s", "cores": nt, "kind": "port",
+                         "sample": f"each step: first {sample} of {args.trees} trees of C2 on the "
+                                   f"restatement of src/cpu.rs (rayon-style f32 chunked histograms, "
+                                   f"{nt} threads), extrapolated to {args.trees} trees"},
+        "e2e": {"value": v, "unit": "s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device(f"cuda:{local}"))
+    import rustwood_b200 as rb
+    from rustwood_b200 import _native as N
+    from rustwood_b200 import synth
+    from rustwood_b200.booster import Context, Dataset, fit_dataset, train_params
+
+    nccl_id = None
+    if world > 1:
+        idt = torch.zeros(128, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            idt.copy_(torch.frombuffer(bytearray(Context.nccl_unique_id()), dtype=torch.uint8))
+        dist.broadcast(idt, 0)
+        nccl_id = bytes(idt.cpu().numpy().tobytes())
+    ctx = Context(local, rank, world, nccl_id)
+    stream = torch.cuda.ExternalStream(N.lib.rw_ctx_stream(ctx.h))
+
+    # ---- data: this rank's shard of the global training set ---------------------------
+    n = args.rows
+    x, y, _, _ = synth.c2(n, seed=rank)
+    cuts = rb.compute_boundaries(x, 255)
+    base = np.float32(rb.base_score(y, "logistic"))
+    if world > 1:  # one cut table and base score for all ranks (rank 0's shard)
+        ct = torch.from_numpy(np.append(cuts, base).astype(np.float32)).cuda()
+        dist.broadcast(ct, 0)
+        arr = ct.cpu().numpy()
+        cuts, base = arr[:-1].copy(), np.float32(arr[-1])
+    cfg = c2_cfg(args.trees)
+    xd = torch.from_numpy(x).cuda()
+    yd = torch.from_numpy(y).cuda()
+    ds = Dataset.from_device(ctx, xd.data_ptr(), yd.data_ptr(), n, x.shape[1], cuts, 255,
+                             n_global=n * world, row_offset=n * rank)
+    del xd, yd
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        fit_dataset(ds, cfg, float(base))
+    barrier()
+    clocks = ClockSampler(local)
+    time.sleep(0.3)
+    fits = []
+    for i in range(args.steps):
+        with torch.cuda.stream(stream):
+            flush.fill_(i & 0xff)  # evict L2 between timed steps (outside the fit's events)
+        fits.append(fit_dataset(ds, cfg, float(base), profile=True))
+    barrier()
+    step_ms = [r.profile.total_ms for r in fits]
+    hist_ms = sum(r.profile.category_ms[2] for r in fits)
+    hist_bytes = sum(r.profile.hist_alg_bytes for r in fits)
+    hist_launches = sum(r.profile.hist_launches for r in fits)
+    launches = sum(int(r.profile.kernel_launches) for r in fits)
+    cats = {N.CATEGORIES[c]: sum(r.profile.category_ms[c] for r in fits) / args.steps
+            for c in range(7)}
+
+    # ---- e2e through the C ABI from pinned host buffers ------------------------------
+    xp = torch.from_numpy(x).pin_memory()
+    yp = torch.from_numpy(y).pin_memory()
+    cuts_c = np.ascontiguousarray(cuts, np.float32)
+    T, D, nf = args.trees, 6, x.shape[1]
+    out = dict(feat=np.zeros(T * D, np.uint32), thr=np.zeros(T * D, np.float32),
+               thr_bin=np.zeros(T * D, np.uint16), leafval=np.zeros(T << D, np.float32),
+               fi_gain=np.zeros(nf, np.float32), fi_count=np.zeros(nf, np.float32))
+    p = train_params(cfg)
+    e2e_ms = []
+    for i in range(args.warmup + args.steps):
+        with torch.cuda.stream(stream):
+            flush.fill_(i & 0xff)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        if world == 1:
+            ctx.check(N.lib.rw_fit(ctx.h, C.byref(p), C.c_void_p(xp.data_ptr()),
+                                   C.c_void_p(yp.data_ptr()), n, nf, N.ptr(cuts_c), float(base),
+                                   *(N.ptr(out[k]) for k in ("feat", "thr", "thr_bin", "leafval")),
+                                   None, N.ptr(out["fi_gain"]), N.ptr(out["fi_count"]), None))
+        else:
+            h = C.c_void_p()
+            ctx.check(N.lib.rw_dataset_create(ctx.h, C.c_void_p(xp.data_ptr()),
+                                              C.c_void_p(yp.data_ptr()), n, nf, N.ptr(cuts_c), 255,
+                                              0, n * world, n * rank, C.byref(h)))
+            ctx.check(N.lib.rw_fit_dataset(h, C.byref(p), float(base),
+                                           *(N.ptr(out[k]) for k in ("feat", "thr", "thr_bin",
+                                                                      "leafval")),
+                                           None, N.ptr(out["fi_gain"]), N.ptr(out["fi_count"]),
+                                           None))
+            N.lib.rw_dataset_destroy(h)
+        b.record(stream)
+        b.synchronize()
+        if i >= args.warmup:
+            e2e_ms.append(a.elapsed_time(b))
+    h2d = x.nbytes + y.nbytes + cuts_c.nbytes
+    d2h = sum(v.nbytes for v in out.values())
+
+    # ---- predict throughput (C5), device-resident u8 rows ------------------------------
+    pred = None
+    if args.predict_rows > 0:
+        feat, thr_bin, leafval = synth.c5_model(500, 6, 54, seed=0)
+        m = N.Model()
+        m.n_trees, m.depth, m.n_features, m.base_score = 500, 6, 54, 0.0
+        m.feat = feat.ctypes.data_as(C.POINTER(C.c_uint32))
+        m.thr = np.zeros(500 * 6, np.float32).ctypes.data_as(C.POINTER(C.c_float))
+        m.thr_bin = thr_bin.ctypes.data_as(C.POINTER(C.c_uint16))
+        m.leafval = leafval.ctypes.data_as(C.POINTER(C.c_float))
+        dm = C.c_void_p()
+        ctx.check(N.lib.rw_model_upload(ctx.h, C.byref(m), C.byref(dm)))
+        pn = args.predict_rows
+        g = torch.Generator(device="cuda").manual_seed(1 + rank)
+        bins = torch.randint(0, 256, (54, pn), dtype=torch.uint8, device="cuda", generator=g)
+        outp = torch.empty(pn, dtype=torch.float32, device="cuda")
+        kms = C.c_float()
+        ks = []
+        for i in range(args.warmup + args.steps):
+            ctx.check(N.lib.rw_predict_u8_device(ctx.h, dm, C.c_void_p(bins.data_ptr()), pn, pn,
+                                                 C.c_void_p(outp.data_ptr()), C.byref(kms)))
+            if i >= args.warmup:
+                ks.append(kms.value)
+        N.lib.rw_model_free(dm)
+        del bins, outp
+        pred = {"rows": pn, "trees": 500, "depth": 6, "features": 54,
+                "kernel_ms": statistics.mean(ks), "rows_per_s_per_gpu": pn / (statistics.mean(ks) / 1e3)}
+    barrier()
+    clk = clocks.stop()
+
+    # ---- max over ranks -----------------------------------------------------------------
+    v_s = statistics.mean(step_ms) / 1e3
+    e2e_s = statistics.mean(e2e_ms) / 1e3
+    hist_gbs = hist_bytes / (hist_ms / 1e3) / 1e9 if hist_ms > 0 else 0.0
+    pred_rps = pred["rows_per_s_per_gpu"] if pred else 0.0
+    agg = np.array([v_s, e2e_s, -hist_gbs, hist_ms], np.float64)
+    if world > 1:
+        t = torch.from_numpy(agg).cuda()
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        agg = t.cpu().numpy()
+        ps = torch.tensor([pred_rps], dtype=torch.float64, device="cuda")
+        dist.all_reduce(ps, op=dist.ReduceOp.SUM)
+        pred_total = float(ps.item())
+    else:
+        pred_total = pred_rps
+    v_s, e2e_s, hist_gbs_min = float(agg[0]), float(agg[1]), float(-agg[2])
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(x, y, cuts, float(base), max(1, min(args.cpu_trees, args.trees)),
+                           args.trees)
+
+    if rank == 0:
+        peak, peak_kind = hbm_peak()
+        per_launch_bytes = hist_bytes / max(hist_launches, 1)
+        traffic = read_traffic()
+        line = {
+            "metric": METRIC, "value": v_s, "unit": "s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": v_s * 1e3, "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int64",
+            "data": "synthetic (seeded numpy, Covertype-shaped; Covertype itself is not available)",
+            "config": {
+                "workload": WORKLOAD, "rows_per_gpu": n, "global_rows": n * world,
+                "parallelism": f"dp{world} (row shards, NCCL int64 histogram allreduce)",
+                "arithmetic": "u8 bins; exact int64 fixed-point g/h histograms; f64 gains; f32 leaves",
+                "l2": "L2 flushed (256 MiB write) between timed steps; within a step the 68 MB "
+                      "working set (bins + per-row state) stays L2-resident across levels",
+                "cut_table": "from rank 0's shard, broadcast" if world > 1 else "from the shard",
+            },
+            "roofline": {
+                "bound": "hbm", "kernel": "k_hist", "achieved": hist_gbs_min, "peak": peak,
+                "peak_kind": peak_kind, "unit": "GB/s", "frac": hist_gbs_min / peak,
+                "traffic": traffic,
+                "alg_bytes_per_launch": per_launch_bytes,
+                "avg_launch_us": hist_ms / max(hist_launches, 1) * 1e3,
+                "note": "alg bytes per level = n*F + 12n + 8*F*B*G (u8 bins); achieved above the "
+                        "HBM peak means the level's inputs were served from L2",
+            },
+            "phases_ms_per_fit": cats,
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_s, "unit": "s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h)},
+            "gpu_launches": launches,
+            "predict": None if pred is None else dict(pred, rows_per_s_total=pred_total),
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    ds.close()
+    ctx.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

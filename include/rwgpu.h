@@ -1,0 +1,202 @@
+/* rwgpu -- B200 (sm_100a) oblivious-tree boosting hot path behind a C ABI.
+ *
+ * This is the drop-in boundary for rustwood's `--device gpu` path. Every entry point
+ * takes plain pointers and sizes; no C++ or torch types cross it. The Rust host (or
+ * any FFI: ctypes, cgo, JNI) binds these symbols in place of the cuda-oxide kernel
+ * launches that rustwood's `Booster` issues today.
+ *
+ * Conventions (mirroring src/booster.rs's single-stream design):
+ *  - Every call returns RW_OK (0) or a negative RW_ERR_* code; the message for the
+ *    last failure on a context is available from rw_last_error(). No exception or
+ *    abort crosses the ABI.
+ *  - The caller owns every host buffer; outputs are written in full before return;
+ *    no caller pointer is retained after a call returns.
+ *  - A context (and the datasets/models created from it) is used by one host thread
+ *    at a time. All device work of a context runs on one CUDA stream it owns.
+ *  - Model semantics are rustwood's: for tree t and level d, slot k = t*depth + d holds
+ *    feat[k] (feature index) and thr[k] (raw cut value); a row's leaf index is built
+ *    MSB-first as leaf = 2*leaf + (x[feat[k]] > thr[k]) (src/gpu_kernels.rs:1009),
+ *    and leafval is [n_trees][2^depth] (src/booster.rs:54-69).
+ */
+#ifndef RWGPU_H
+#define RWGPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RW_OK 0
+#define RW_ERR_ARG (-1)         /* invalid argument */
+#define RW_ERR_OOM (-2)         /* device or host allocation failed */
+#define RW_ERR_CUDA (-3)        /* CUDA runtime error */
+#define RW_ERR_NCCL (-4)        /* NCCL error */
+#define RW_ERR_UNSUPPORTED (-5) /* option not implemented on this path */
+#define RW_ERR_TIMEOUT (-6)     /* collective or device wait exceeded its limit */
+
+typedef struct rw_ctx rw_ctx;         /* device, stream, optional NCCL communicator */
+typedef struct rw_dataset rw_dataset; /* device-resident binned training shard */
+typedef struct rw_dmodel rw_dmodel;   /* device-resident model for scoring */
+
+enum { RW_OBJ_LOGISTIC = 0, RW_OBJ_L2 = 1 };
+
+/* Hyperparameters on the hot path: the fields of rustwood's Config
+ * (src/config.rs:19-88) that fit_inner reads. replicas/smem_hist/f16_hist/int_hist/
+ * int_scale only select among the reference's atomic strategies; they are accepted
+ * and ignored (this library always uses exact fixed-point histograms). */
+typedef struct rw_train_params {
+  uint32_t n_trees;
+  uint32_t depth;         /* 1..12 */
+  uint32_t n_bins;        /* 2..256 */
+  float learning_rate;
+  float lambda;
+  float min_child_h;
+  float subsample;        /* < 0.999: every round(1/subsample)-th row (src/cpu.rs:172-176) */
+  float colsample;        /* < 1: per-tree feature drop (src/gpu_kernels.rs:837) */
+  const int32_t* monotone; /* nullable, n_monotone entries of -1/0/+1 */
+  uint32_t n_monotone;
+  int32_t subtract;       /* histogram subtraction (src/cpu.rs:213) */
+  float goss_top;         /* > 0 enables GOSS (src/cpu.rs:64-110) */
+  float goss_other;
+  float clamp_hessian;    /* experimental in the reference; must be 0 here */
+  int32_t pack4;          /* 4-bit bins when n_bins <= 16 */
+  int32_t pgbm;           /* leaf variances; must be 0 here */
+  int32_t objective;      /* RW_OBJ_LOGISTIC or RW_OBJ_L2 */
+  uint32_t replicas;      /* accepted, ignored */
+  int32_t smem_hist, f16_hist, int_hist; /* accepted, ignored */
+  float int_scale;        /* accepted, ignored */
+} rw_train_params;
+
+/* Per-phase device time of one fit, from CUDA events on the context stream
+ * (the reference's profile categories, src/booster.rs:42-52, plus the collective). */
+enum {
+  RW_CAT_GRADIENTS = 0,
+  RW_CAT_ZERO_HIST,
+  RW_CAT_BUILD_HIST,
+  RW_CAT_ALLREDUCE,
+  RW_CAT_SPLIT,
+  RW_CAT_APPLY,
+  RW_CAT_UPDATE_PRED,
+  RW_N_CATEGORIES
+};
+
+typedef struct rw_profile {
+  int32_t enable;                      /* in: record per-phase events (adds no syncs) */
+  double total_ms;                     /* out: tree loop, first launch to last (events) */
+  double category_ms[RW_N_CATEGORIES]; /* out: per-phase sums */
+  double hist_alg_bytes;               /* out: sum over levels of n*F*s + 12n + 8*F*B*G */
+  uint64_t hist_launches;              /* out: histogram kernel launches */
+  uint64_t kernel_launches;            /* out: all kernels this library launched */
+} rw_profile;
+
+/* A host-side model view (rustwood's Booster fields feat/thr/leafval/base_score).
+ * thr_bin (bin-space thresholds, bin > thr_bin <=> x > thr) is needed only by the
+ * u8 scorer. */
+typedef struct rw_model {
+  uint32_t n_trees, depth, n_features;
+  float base_score;
+  const uint32_t* feat;     /* [n_trees*depth] */
+  const float* thr;         /* [n_trees*depth] */
+  const uint16_t* thr_bin;  /* [n_trees*depth], nullable for f32 scoring */
+  const float* leafval;     /* [n_trees << depth] */
+} rw_model;
+
+/* ---- contexts --------------------------------------------------------------- */
+
+/* Replaces CudaContext::new(cfg.gpu) (src/booster.rs:137) and, for --serve, the
+ * resident shared context (Booster::with_ctx, src/booster.rs:159). n_gpus must be 1;
+ * multi-GPU training uses one process per GPU with rw_ctx_create_rank. */
+int rw_ctx_create(const int* gpu_ids, int n_gpus, rw_ctx** out);
+
+/* One process per GPU: rank `rank` of `world` on device gpu_id, joined by an NCCL
+ * communicator built from the 128-byte id that rank 0 obtained with
+ * rw_nccl_unique_id and broadcast out of band. With world == 1, id may be NULL. */
+int rw_ctx_create_rank(int gpu_id, int rank, int world, const void* nccl_id, rw_ctx** out);
+int rw_nccl_unique_id(void* out128);
+void rw_ctx_destroy(rw_ctx* ctx);
+const char* rw_last_error(const rw_ctx* ctx);
+/* The context's CUDA stream (a cudaStream_t), for callers that order their own work
+ * or CUDA events with the library's. */
+void* rw_ctx_stream(const rw_ctx* ctx);
+/* Bound (milliseconds) on each collective wait; 0 = wait forever. Default 60000. */
+int rw_ctx_set_timeout(rw_ctx* ctx, int64_t ms);
+
+/* ---- training ---------------------------------------------------------------- */
+
+/* Host prep of fit_inner (src/booster.rs:255-277): upload row-major x and y, bin on
+ * the GPU against the cut table cuts[nf*(n_bins-1)] (bin = #{cut < v}), optionally
+ * pack 4-bit. For a row shard, n is the local row count, n_global the total and
+ * row_offset this shard's first global row (row-index hashes and the subsample stride
+ * use global indices). Single process: n_global = n, row_offset = 0. */
+int rw_dataset_create(rw_ctx* ctx, const float* x_rowmajor, const float* y, uint64_t n,
+                      uint32_t nf, const float* cuts, uint32_t n_bins, int32_t pack4,
+                      uint64_t n_global, uint64_t row_offset, rw_dataset** out);
+/* Same, from device pointers (row-major x, y) that stay owned by the caller. */
+int rw_dataset_create_device(rw_ctx* ctx, const float* d_x_rowmajor, const float* d_y,
+                             uint64_t n, uint32_t nf, const float* cuts, uint32_t n_bins,
+                             int32_t pack4, uint64_t n_global, uint64_t row_offset,
+                             rw_dataset** out);
+void rw_dataset_destroy(rw_dataset* ds);
+/* Copy the binned matrix out, feature-major [nf][n] u8 (unpacked). */
+int rw_dataset_bins(const rw_dataset* ds, uint8_t* out);
+
+/* The tree loop of fit_inner (src/booster.rs:349-513). Outputs (caller-allocated):
+ * feat/thr/thr_bin [n_trees*depth], leafval [n_trees<<depth], fi_gain/fi_count [nf].
+ * thr_bin, leafvar and prof may be NULL; leafvar must be NULL (pgbm unsupported). */
+int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float base_score,
+                   uint32_t* feat, float* thr, uint16_t* thr_bin, float* leafval,
+                   float* leafvar, float* fi_gain, float* fi_count, rw_profile* prof);
+
+/* Whole Booster::fit_inner replacement (src/booster.rs:227-517): dataset creation
+ * from host buffers, the tree loop and the model download in one call. */
+int rw_fit(rw_ctx* ctx, const rw_train_params* p, const float* x_rowmajor, const float* y,
+           uint64_t n, uint32_t nf, const float* cuts, float base_score, uint32_t* feat,
+           float* thr, uint16_t* thr_bin, float* leafval, float* leafvar, float* fi_gain,
+           float* fi_count, rw_profile* prof);
+
+/* ---- scoring ----------------------------------------------------------------- */
+
+/* Booster::predict (src/booster.rs:531-555): raw margins of n row-major f32 rows,
+ * accumulated per row in tree order in f32 (bit-identical to predict_cpu,
+ * src/booster.rs:582-601). */
+int rw_predict_f32(rw_ctx* ctx, const rw_model* m, const float* x_rowmajor, uint64_t n,
+                   uint32_t nf, float* out);
+/* Same margins from pre-binned feature-major u8 rows bins[nf][n] and thr_bin. */
+int rw_predict_u8(rw_ctx* ctx, const rw_model* m, const uint8_t* bins_featmajor, uint64_t n,
+                  uint32_t nf, float* out);
+
+/* Device-resident model and scoring of device-resident inputs (the model is uploaded
+ * once, as bench_latency/bench_throughput do, src/booster.rs:608-698). ld is the row
+ * stride of d_bins in bytes (>= n). kernel_ms (nullable) receives the kernel time. */
+int rw_model_upload(rw_ctx* ctx, const rw_model* m, rw_dmodel** out);
+void rw_model_free(rw_dmodel* dm);
+int rw_predict_u8_device(rw_ctx* ctx, const rw_dmodel* dm, const uint8_t* d_bins, uint64_t n,
+                         uint64_t ld, float* d_out, float* kernel_ms);
+int rw_predict_f32_device(rw_ctx* ctx, const rw_dmodel* dm, const float* d_x, uint64_t n,
+                          float* d_out, float* kernel_ms);
+
+/* ---- host helpers kept from the reference host code --------------------------- */
+
+/* compute_boundaries (src/data.rs:86-146): out[nf*(n_bins-1)]. */
+void rw_compute_boundaries(const float* x_rowmajor, uint64_t n, uint32_t nf, uint32_t n_bins,
+                           uint64_t sample, int32_t unique, float* out);
+/* base_score (src/booster.rs:201-205 / 280-284). */
+float rw_base_score(const float* y, uint64_t n, int32_t objective);
+
+/* ---- test hooks ---------------------------------------------------------------- */
+
+/* Runs the production histogram kernel once on caller data: node[n] (>= 0 in-sample,
+ * < 0 excluded), g/h[n], scales 2^e_g / 2^e_h; odd_only keys odd nodes by node>>1.
+ * out: int64 [groups][nf][n_bins][2] fixed-point (g, h) sums. */
+int rw_debug_level_hist(rw_dataset* ds, const int32_t* node, const float* g, const float* h,
+                        int32_t e_g, int32_t e_h, uint32_t groups, int32_t odd_only,
+                        int64_t* out);
+/* Evaluates the device exponential on n inputs (tests compare it with the host). */
+int rw_debug_expf(rw_ctx* ctx, const float* x, uint64_t n, float* out_rw, float* out_cuda);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RWGPU_H */

@@ -1,0 +1,319 @@
+"""Booster: the host mirror of rustwood's `Booster` (src/booster.rs) over librwgpu.
+
+fit() performs fit_inner's host prep (target encoding, cut table, base score,
+src/booster.rs:246-285) and hands the tree loop to the GPU through rw_fit_dataset;
+predict() is Booster::predict (raw margins, src/booster.rs:531-555) on the GPU;
+save_model()/load_model() read and write the `.rwood` v1 format byte-compatibly
+(src/booster.rs:797-878). The CPU trainer (`--device cpu`, src/cpu.rs) is the
+reference's own code and is not reimplemented here.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import struct
+
+import numpy as np
+
+from . import _native as N
+from . import encoding
+from .config import LOGISTIC, Config
+
+
+class Context:
+    """One GPU (and optionally one NCCL rank). rw_ctx_create_rank."""
+
+    def __init__(self, gpu: int = 0, rank: int = 0, world: int = 1, nccl_id: bytes | None = None):
+        h = C.c_void_p()
+        idb = None if nccl_id is None else C.create_string_buffer(nccl_id, 128)
+        N.check(N.lib.rw_ctx_create_rank(gpu, rank, world, idb, C.byref(h)))
+        self.h = h
+        self.gpu, self.rank, self.world = gpu, rank, world
+
+    def close(self):
+        if self.h:
+            N.lib.rw_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def check(self, code: int):
+        N.check(code, self.h)
+
+    @staticmethod
+    def nccl_unique_id() -> bytes:
+        buf = C.create_string_buffer(128)
+        N.check(N.lib.rw_nccl_unique_id(buf))
+        return buf.raw
+
+
+def train_params(cfg: Config) -> N.TrainParams:
+    p = N.TrainParams()
+    p.n_trees, p.depth, p.n_bins = cfg.n_trees, cfg.depth, cfg.n_bins
+    p.learning_rate, p.lambda_, p.min_child_h = cfg.learning_rate, cfg.lambda_, cfg.min_child_h
+    p.subsample, p.colsample = cfg.subsample, cfg.colsample
+    mono = np.ascontiguousarray(cfg.monotone, dtype=np.int32)
+    p._mono_keepalive = mono  # the array must outlive the call
+    p.monotone = mono.ctypes.data_as(C.POINTER(C.c_int32)) if len(mono) else None
+    p.n_monotone = len(mono)
+    p.subtract = int(cfg.subtract)
+    p.goss_top, p.goss_other, p.clamp_hessian = cfg.goss_top, cfg.goss_other, cfg.clamp_hessian
+    p.pack4, p.pgbm = int(cfg.pack4), int(cfg.pgbm)
+    p.objective = N.RW_OBJ_LOGISTIC if cfg.objective == LOGISTIC else N.RW_OBJ_L2
+    p.replicas, p.smem_hist, p.f16_hist = cfg.replicas, int(cfg.smem_hist), int(cfg.f16_hist)
+    p.int_hist, p.int_scale = int(cfg.int_hist), cfg.int_scale
+    return p
+
+
+def compute_boundaries(x: np.ndarray, n_bins: int, sample: int = 200_000,
+                       unique: bool = False) -> np.ndarray:
+    """src/data.rs:86-146 (native)."""
+    x = N.f32c(x)
+    n, nf = x.shape
+    out = np.empty(nf * (n_bins - 1), dtype=np.float32)
+    N.lib.rw_compute_boundaries(N.ptr(x), n, nf, n_bins, sample, int(unique), N.ptr(out))
+    return out
+
+
+def base_score(y: np.ndarray, objective: str) -> float:
+    """src/booster.rs:201-205 (native)."""
+    y = N.f32c(y)
+    return float(N.lib.rw_base_score(N.ptr(y), len(y),
+                                     N.RW_OBJ_LOGISTIC if objective == LOGISTIC else N.RW_OBJ_L2))
+
+
+class Dataset:
+    """A device-resident binned training shard (rw_dataset)."""
+
+    def __init__(self, ctx: Context, x: np.ndarray, y: np.ndarray, cuts: np.ndarray, n_bins: int,
+                 pack4: bool = False, n_global: int | None = None, row_offset: int = 0):
+        x, y, cuts = N.f32c(x), N.f32c(y), N.f32c(cuts)
+        n, nf = x.shape
+        h = C.c_void_p()
+        ctx.check(N.lib.rw_dataset_create(ctx.h, N.ptr(x), N.ptr(y), n, nf, N.ptr(cuts), n_bins,
+                                          int(pack4), n if n_global is None else n_global,
+                                          row_offset, C.byref(h)))
+        self.ctx, self.h, self.n, self.nf, self.n_bins = ctx, h, n, nf, n_bins
+
+    @classmethod
+    def from_device(cls, ctx: Context, x_ptr: int, y_ptr: int, n: int, nf: int, cuts: np.ndarray,
+                    n_bins: int, pack4: bool = False, n_global: int | None = None,
+                    row_offset: int = 0) -> "Dataset":
+        self = cls.__new__(cls)
+        cuts = N.f32c(cuts)
+        h = C.c_void_p()
+        ctx.check(N.lib.rw_dataset_create_device(ctx.h, C.c_void_p(x_ptr), C.c_void_p(y_ptr), n,
+                                                 nf, N.ptr(cuts), n_bins, int(pack4),
+                                                 n if n_global is None else n_global, row_offset,
+                                                 C.byref(h)))
+        self.ctx, self.h, self.n, self.nf, self.n_bins = ctx, h, n, nf, n_bins
+        return self
+
+    def bins(self) -> np.ndarray:
+        out = np.empty((self.nf, self.n), dtype=np.uint8)
+        self.ctx.check(N.lib.rw_dataset_bins(self.h, N.ptr(out)))
+        return out
+
+    def close(self):
+        if self.h:
+            N.lib.rw_dataset_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class FitResult:
+    def __init__(self, T, D, nf):
+        self.feat = np.zeros(T * D, dtype=np.uint32)
+        self.thr = np.zeros(T * D, dtype=np.float32)
+        self.thr_bin = np.zeros(T * D, dtype=np.uint16)
+        self.leafval = np.zeros(T << D, dtype=np.float32)
+        self.fi_gain = np.zeros(nf, dtype=np.float32)
+        self.fi_count = np.zeros(nf, dtype=np.float32)
+        self.profile = N.Profile()
+
+
+def fit_dataset(ds: Dataset, cfg: Config, base: float, profile: bool = False) -> FitResult:
+    """rw_fit_dataset: the tree loop on a prepared dataset."""
+    r = FitResult(cfg.n_trees, cfg.depth, ds.nf)
+    p = train_params(cfg)
+    r.profile.enable = int(profile)
+    ds.ctx.check(N.lib.rw_fit_dataset(ds.h, C.byref(p), base, N.ptr(r.feat), N.ptr(r.thr),
+                                      N.ptr(r.thr_bin), N.ptr(r.leafval), None, N.ptr(r.fi_gain),
+                                      N.ptr(r.fi_count), C.byref(r.profile)))
+    return r
+
+
+class Booster:
+    """src/booster.rs:54-69 fields; GPU fit/predict through librwgpu."""
+
+    def __init__(self, cfg: Config, ctx: Context | None = None):
+        if cfg.device != "gpu":
+            raise NotImplementedError(
+                "this library implements the --device gpu path; the CPU trainer is src/cpu.rs")
+        self.cfg = cfg
+        self._ctx = ctx
+        self.n_features = 0
+        self.base_score = 0.0
+        self.feat = np.zeros(0, np.uint32)
+        self.thr = np.zeros(0, np.float32)
+        self.thr_bin = np.zeros(0, np.uint16)
+        self.leafval = np.zeros(0, np.float32)
+        self.encoders: list[dict] = []
+        self.gmean = 0.0
+        self.fi_gain = np.zeros(0, np.float32)
+        self.fi_count = np.zeros(0, np.float32)
+        self.cuts = np.zeros(0, np.float32)
+        self.last_profile = None
+
+    @property
+    def ctx(self) -> Context:
+        """The GPU context, created on first use (model I/O needs none)."""
+        if self._ctx is None:
+            self._ctx = Context(self.cfg.gpu)
+        return self._ctx
+
+    # -- training ----------------------------------------------------------------
+    def prepare(self, x: np.ndarray, y: np.ndarray):
+        """fit_inner's host prep (src/booster.rs:246-285): returns (x_encoded, cuts, base)."""
+        cfg = self.cfg
+        x = np.array(x, dtype=np.float32, order="C", copy=True)
+        y = N.f32c(y)
+        if cfg.categorical:
+            self.encoders, self.gmean = encoding.fit_transform_train(
+                x, y, cfg.categorical, cfg.te_smoothing, 5, cfg.cat_hash_buckets)
+        cuts = compute_boundaries(x, cfg.n_bins, cfg.bin_sample, cfg.unique_bins)
+        return x, cuts, base_score(y, cfg.objective)
+
+    def fit(self, x: np.ndarray, y: np.ndarray, profile: bool = False) -> float:
+        """Booster::fit (src/booster.rs:169-181) for the GPU device; returns the tree-loop
+        time in seconds (what the reference reports as train_s)."""
+        x, cuts, base = self.prepare(x, y)
+        self.n_features = x.shape[1]
+        self.base_score = base
+        self.cuts = cuts
+        ds = Dataset(self.ctx, x, y, cuts, self.cfg.n_bins, self.cfg.pack4)
+        try:
+            r = fit_dataset(ds, self.cfg, base, profile=profile)
+        finally:
+            ds.close()
+        self._take(r)
+        return r.profile.total_ms / 1e3
+
+    def _take(self, r: FitResult):
+        self.feat, self.thr, self.thr_bin, self.leafval = r.feat, r.thr, r.thr_bin, r.leafval
+        self.fi_gain, self.fi_count = r.fi_gain, r.fi_count
+        self.last_profile = r.profile
+
+    # -- scoring -----------------------------------------------------------------
+    def model(self) -> tuple[N.Model, list]:
+        m = N.Model()
+        m.n_trees, m.depth, m.n_features = self.cfg.n_trees, self.cfg.depth, self.n_features
+        m.base_score = self.base_score
+        keep = [np.ascontiguousarray(self.feat, np.uint32), np.ascontiguousarray(self.thr, np.float32),
+                np.ascontiguousarray(self.leafval, np.float32)]
+        m.feat = keep[0].ctypes.data_as(C.POINTER(C.c_uint32))
+        m.thr = keep[1].ctypes.data_as(C.POINTER(C.c_float))
+        m.leafval = keep[2].ctypes.data_as(C.POINTER(C.c_float))
+        if len(self.thr_bin) == len(self.feat) and len(self.feat):
+            keep.append(np.ascontiguousarray(self.thr_bin, np.uint16))
+            m.thr_bin = keep[-1].ctypes.data_as(C.POINTER(C.c_uint16))
+        return m, keep
+
+    def predict(self, x: np.ndarray) -> np.ndarray:
+        """Raw margins on the GPU (Booster::predict)."""
+        x = np.array(x, dtype=np.float32, order="C", copy=bool(self.cfg.categorical))
+        if self.cfg.categorical:
+            encoding.transform(x, self.cfg.categorical, self.encoders, self.gmean,
+                               self.cfg.cat_hash_buckets)
+        n = x.shape[0]
+        out = np.empty(n, dtype=np.float32)
+        m, _keep = self.model()
+        self.ctx.check(N.lib.rw_predict_f32(self.ctx.h, C.byref(m), N.ptr(x), n, x.shape[1],
+                                            N.ptr(out)))
+        return out
+
+    def predict_bins(self, bins_featmajor: np.ndarray) -> np.ndarray:
+        """Raw margins from pre-binned feature-major u8 rows (rw_predict_u8)."""
+        b = np.ascontiguousarray(bins_featmajor, dtype=np.uint8)
+        nf, n = b.shape
+        out = np.empty(n, dtype=np.float32)
+        m, _keep = self.model()
+        self.ctx.check(N.lib.rw_predict_u8(self.ctx.h, C.byref(m), N.ptr(b), n, nf, N.ptr(out)))
+        return out
+
+    def feature_importance(self):
+        return self.fi_gain, self.fi_count
+
+    # -- .rwood v1 (src/booster.rs:797-878) ----------------------------------------
+    def save_model(self, path: str) -> None:
+        cfg = self.cfg
+        with open(path, "wb") as f:
+            f.write(b"RWD1")
+            f.write(struct.pack("<5I", 1, self.n_features, cfg.n_trees, cfg.depth,
+                                int(cfg.objective == LOGISTIC)))
+            f.write(struct.pack("<ffQ", self.base_score, self.gmean, cfg.cat_hash_buckets))
+            f.write(struct.pack("<I", len(cfg.categorical)))
+            for c in cfg.categorical:
+                f.write(struct.pack("<I", c))
+            for arr, dt in ((self.feat, "<u4"), (self.thr, "<f4"), (self.leafval, "<f4")):
+                a = np.ascontiguousarray(arr, dtype=dt)
+                f.write(struct.pack("<I", len(a)))
+                f.write(a.tobytes())
+            f.write(struct.pack("<I", len(self.encoders)))
+            for mp in self.encoders:
+                f.write(struct.pack("<I", len(mp)))
+                for k in sorted(mp):
+                    f.write(struct.pack("<qf", k, float(mp[k])))
+
+    @classmethod
+    def load_model(cls, path: str, ctx: Context | None = None) -> "Booster":
+        with open(path, "rb") as f:
+            data = f.read()
+        if data[:4] != b"RWD1":
+            raise ValueError("not a .rwood file")
+        off = 4
+        _ver, nf, nt, depth, logistic = struct.unpack_from("<5I", data, off)
+        off += 20
+        base, gmean, hb = struct.unpack_from("<ffQ", data, off)
+        off += 16
+        (ncat,) = struct.unpack_from("<I", data, off)
+        off += 4
+        cats = list(struct.unpack_from(f"<{ncat}I", data, off))
+        off += 4 * ncat
+
+        def arr(dt):
+            nonlocal off
+            (ln,) = struct.unpack_from("<I", data, off)
+            off += 4
+            a = np.frombuffer(data, dtype=dt, count=ln, offset=off).copy()
+            off += 4 * ln
+            return a
+
+        feat, thr, leafval = arr("<u4"), arr("<f4"), arr("<f4")
+        (nenc,) = struct.unpack_from("<I", data, off)
+        off += 4
+        encs = []
+        for _ in range(nenc):
+            (ml,) = struct.unpack_from("<I", data, off)
+            off += 4
+            mp = {}
+            for _ in range(ml):
+                k, v = struct.unpack_from("<qf", data, off)
+                off += 12
+                mp[k] = np.float32(v)
+            encs.append(mp)
+        cfg = Config(n_trees=nt, depth=depth, objective=LOGISTIC if logistic == 1 else "l2",
+                     categorical=cats, cat_hash_buckets=hb)
+        b = cls(cfg, ctx)
+        b.n_features, b.base_score, b.gmean = nf, np.float32(base), np.float32(gmean)
+        b.feat, b.thr, b.leafval, b.encoders = feat, thr, leafval, encs
+        b.thr_bin = np.zeros(0, np.uint16)
+        return b

@@ -1,0 +1,138 @@
+/* Deterministic single-precision exponential shared by the GPU kernels and the
+ * exact-mode CPU restatement.
+ *
+ * rustwood's CPU trainer computes the logistic link with Rust's `f32::exp`
+ * (src/cpu.rs:185), which on linux-gnu is glibc `expf`; the reference GPU kernel
+ * uses whatever its compiler lowers `exp` to (src/gpu_kernels.rs:680). Neither
+ * is reproducible bit-for-bit on both a CPU and a GPU, so this library defines
+ * its own routine and uses the SAME code on both sides.
+ *
+ * Method (published): Cody & Waite additive range reduction (W. J. Cody and
+ * W. Waite, "Software Manual for the Elementary Functions", Prentice-Hall, 1980):
+ *   x = k*ln2 + r,  k = nearest integer to x/ln2,  |r| <= ln2/2,
+ * with ln2 split into a 32-bit head (so k*LN2_HI is exact) and a tail.
+ * e^r is the Taylor series sum_{i=0..12} r^i / i!, evaluated by Horner's rule
+ * in double precision (truncation error < 2e-16 for |r| <= 0.347), then scaled
+ * by 2^k and rounded once to float. The double-precision evaluation makes the
+ * float result the correctly rounded e^x except when e^x lies within ~1e-15
+ * relative of a rounding midpoint.
+ *
+ * Bit-reproducibility: every operation is an IEEE-754 double add/multiply with
+ * round-to-nearest. On the device they are written as __dadd_rn/__dmul_rn,
+ * which the compiler never contracts into FMAs; host code that includes this
+ * header must be compiled with -ffp-contract=off. The constants below are the
+ * mathematical values 1/i! and ln2 (head truncated to 32 bits, tail = ln2 - head),
+ * computed for this file.
+ */
+#ifndef RW_EXPF_H
+#define RW_EXPF_H
+
+#include <stdint.h>
+#include <string.h>
+
+#if defined(__CUDACC__)
+#define RW_HD __host__ __device__ __forceinline__
+#else
+#define RW_HD static inline
+#endif
+
+#if defined(__CUDA_ARCH__)
+#define RW_DADD(a, b) __dadd_rn((a), (b))
+#define RW_DMUL(a, b) __dmul_rn((a), (b))
+#define RW_RINT(a) rint(a)
+#else
+#include <math.h>
+#define RW_DADD(a, b) ((a) + (b))
+#define RW_DMUL(a, b) ((a) * (b))
+#define RW_RINT(a) nearbyint(a)
+#endif
+
+#define RW_LN2_HI 0x1.62e42fee00000p-1
+#define RW_LN2_LO 0x1.a39ef35793c76p-33
+#define RW_LOG2E 1.4426950408889634
+
+RW_HD double rw_pow2i(int k) {
+  /* 2^k for -1022 <= k <= 1023, built from its IEEE-754 bit pattern. */
+  uint64_t bits = (uint64_t)(int64_t)(k + 1023) << 52;
+  double d;
+  memcpy(&d, &bits, sizeof d);
+  return d;
+}
+
+RW_HD float rw_expf(float xf) {
+  if (xf != xf) return xf;                  /* NaN propagates */
+  if (xf > 89.0f) return (float)1e300;      /* rounds to +inf */
+  if (xf < -104.0f) return 0.0f;            /* below the smallest subnormal */
+  double x = (double)xf;
+  double kd = RW_RINT(RW_DMUL(x, RW_LOG2E));
+  double r = RW_DADD(RW_DADD(x, -RW_DMUL(kd, RW_LN2_HI)), -RW_DMUL(kd, RW_LN2_LO));
+  double p = 1.0 / 479001600.0; /* 1/12! */
+  p = RW_DADD(RW_DMUL(p, r), 1.0 / 39916800.0);
+  p = RW_DADD(RW_DMUL(p, r), 1.0 / 3628800.0);
+  p = RW_DADD(RW_DMUL(p, r), 1.0 / 362880.0);
+  p = RW_DADD(RW_DMUL(p, r), 1.0 / 40320.0);
+  p = RW_DADD(RW_DMUL(p, r), 1.0 / 5040.0);
+  p = RW_DADD(RW_DMUL(p, r), 1.0 / 720.0);
+  p = RW_DADD(RW_DMUL(p, r), 1.0 / 120.0);
+  p = RW_DADD(RW_DMUL(p, r), 1.0 / 24.0);
+  p = RW_DADD(RW_DMUL(p, r), 1.0 / 6.0);
+  p = RW_DADD(RW_DMUL(p, r), 0.5);
+  p = RW_DADD(RW_DMUL(p, r), 1.0);
+  p = RW_DADD(RW_DMUL(p, r), 1.0);
+  double y = RW_DMUL(p, rw_pow2i((int)kd));
+  return (float)y;
+}
+
+/* Logistic link and hessian exactly as src/cpu.rs:185-187 writes them, with the
+ * exponential above: pr = 1/(1+e^-p), g = pr - y, h = max(pr*(1-pr), 1e-6). The
+ * float operations are single IEEE ops (no contraction possible). */
+RW_HD void rw_logistic_grad(float p, float y, float* g, float* h) {
+  float e = rw_expf(-p);
+  float pr = 1.0f / (1.0f + e);
+  *g = pr - y;
+  float hv = pr * (1.0f - pr);
+  *h = hv > 1e-6f ? hv : 1e-6f; /* f32::max(hv, 1e-6) for non-NaN hv */
+}
+
+/* Fixed-point quantisation of gradients and hessians.
+ *
+ * Histogram sums are accumulated exactly in 64-bit integers so that they do not
+ * depend on summation order (thread scheduling, GPU count). Per boosting round,
+ * each of g and h gets a power-of-two scale 2^e chosen from the round's maximum
+ * magnitude M so that |q| = |round(x * 2^e)| <= 2^RW_QBITS:
+ *     e = RW_QBITS - E,  where 2^(E-1) <= M < 2^E (frexp exponent of M),
+ * clamped to [-126, 100] so 2^e is a normal float. M == 0 gives e = 0.
+ * The quantisation error per value is <= 2^-(e+1) <= M * 2^-(RW_QBITS+1).
+ */
+#define RW_QBITS 26
+
+RW_HD int rw_qscale_exp(uint32_t max_bits) {
+  /* max_bits: IEEE bit pattern of a non-negative float M. */
+  if ((max_bits & 0x7fffffffu) == 0u) return 0;
+  int biased = (int)((max_bits >> 23) & 0xffu);
+  int E = (biased == 0 ? 1 : biased) - 126; /* frexp exponent (subnormals: -125) */
+  int e = RW_QBITS - E;
+  if (e > 100) e = 100;
+  if (e < -126) e = -126;
+  return e;
+}
+
+RW_HD float rw_pow2f(int e) {
+  /* 2^e as float for -126 <= e <= 127. */
+  uint32_t bits = (uint32_t)(e + 127) << 23;
+  float f;
+  memcpy(&f, &bits, sizeof f);
+  return f;
+}
+
+RW_HD int32_t rw_quantize(float x, float scale) {
+  /* round-half-even of x*scale; x*scale is exact (power-of-two scale). */
+  if (x != x) return 0;
+#if defined(__CUDA_ARCH__)
+  return __float2int_rn(__fmul_rn(x, scale));
+#else
+  return (int32_t)lrintf(x * scale);
+#endif
+}
+
+#endif /* RW_EXPF_H */

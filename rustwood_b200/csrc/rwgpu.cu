@@ -1,0 +1,950 @@
+// C-ABI implementation of include/rwgpu.h: contexts, device datasets, the boosting
+// loop (the body of rustwood's Booster::fit_inner, src/booster.rs:227-517), scoring
+// and the host helpers the reference keeps on the host.
+#include <cuda_runtime.h>
+#include <nccl.h>
+#include <stdint.h>
+#include <string.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "rw_expf.h"
+#include "rw_internal.cuh"
+
+namespace {
+
+thread_local std::string g_tls_error;
+
+int fail(rw_ctx* ctx, int code, const std::string& msg) {
+  if (ctx) ctx->last_error = msg;
+  g_tls_error = msg;
+  return code;
+}
+
+int cuda_fail(rw_ctx* ctx, cudaError_t e, const char* what) {
+  return fail(ctx, e == cudaErrorMemoryAllocation ? RW_ERR_OOM : RW_ERR_CUDA,
+              std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define RW_CU(ctx, expr)                                     \
+  do {                                                       \
+    cudaError_t _e = (expr);                                 \
+    if (_e != cudaSuccess) return cuda_fail((ctx), _e, #expr); \
+  } while (0)
+
+#define RW_NC(ctx, expr)                                                        \
+  do {                                                                          \
+    ncclResult_t _r = (expr);                                                   \
+    if (_r != ncclSuccess && _r != ncclInProgress)                              \
+      return fail((ctx), RW_ERR_NCCL, std::string(#expr) + ": " + ncclGetErrorString(_r)); \
+  } while (0)
+
+// Device allocation owned by a scope.
+template <typename T>
+struct DBuf {
+  T* p = nullptr;
+  size_t n = 0;
+  DBuf() = default;
+  DBuf(const DBuf&) = delete;
+  DBuf& operator=(const DBuf&) = delete;
+  ~DBuf() {
+    if (p) cudaFree(p);
+  }
+  cudaError_t alloc(size_t count) {
+    n = count;
+    return cudaMalloc(reinterpret_cast<void**>(&p), std::max<size_t>(count, 1) * sizeof(T));
+  }
+  T* release() {
+    T* q = p;
+    p = nullptr;
+    return q;
+  }
+};
+
+// A view of a named buffer in the dataset's workspace cache (owned by the dataset).
+template <typename T>
+struct WsBuf {
+  T* p = nullptr;
+  size_t n = 0;
+  cudaError_t get(rw_dataset* ds, const char* name, size_t count) {
+    n = count;
+    const size_t bytes = std::max<size_t>(count, 1) * sizeof(T);
+    auto it = ds->ws.find(name);
+    if (it != ds->ws.end() && it->second.second >= bytes) {
+      p = static_cast<T*>(it->second.first);
+      return cudaSuccess;
+    }
+    if (it != ds->ws.end()) {
+      cudaFree(it->second.first);
+      ds->ws.erase(it);
+    }
+    void* q = nullptr;
+    cudaError_t e = cudaMalloc(&q, bytes);
+    if (e != cudaSuccess) return e;
+    ds->ws[name] = {q, bytes};
+    p = static_cast<T*>(q);
+    return cudaSuccess;
+  }
+};
+
+uint64_t round_up(uint64_t v, uint64_t m) { return (v + m - 1) / m * m; }
+
+// Wait for the context stream; with a communicator, bound the wait and abort the
+// communicator when the limit passes or NCCL reports an asynchronous error.
+int wait_stream(rw_ctx* ctx) {
+  if (!ctx->comm) {
+    RW_CU(ctx, cudaStreamSynchronize(ctx->stream));
+    return RW_OK;
+  }
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    cudaError_t q = cudaStreamQuery(ctx->stream);
+    if (q == cudaSuccess) return RW_OK;
+    if (q != cudaErrorNotReady) return cuda_fail(ctx, q, "cudaStreamQuery");
+    ncclResult_t as = ncclSuccess;
+    ncclCommGetAsyncError(ctx->comm, &as);
+    if (as != ncclSuccess && as != ncclInProgress) {
+      ncclCommAbort(ctx->comm);
+      ctx->comm = nullptr;
+      return fail(ctx, RW_ERR_NCCL, std::string("NCCL async error: ") + ncclGetErrorString(as));
+    }
+    const double ms = std::chrono::duration<double, std::milli>(
+                          std::chrono::steady_clock::now() - t0).count();
+    if (ctx->timeout_ms > 0 && ms > (double)ctx->timeout_ms) {
+      ncclCommAbort(ctx->comm);
+      ctx->comm = nullptr;
+      return fail(ctx, RW_ERR_TIMEOUT, "collective wait exceeded the context timeout");
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
+// Phase timing with consecutive CUDA events on the context stream.
+struct PhaseTimer {
+  bool on = false;
+  cudaStream_t s = nullptr;
+  std::vector<cudaEvent_t> ev;
+  std::vector<int> cat;  // category of the interval ending at ev[i] (i >= 1)
+  std::vector<int> hist_idx;
+  size_t used = 0;
+  int init(bool enable, cudaStream_t stream, size_t cap) {
+    on = enable;
+    s = stream;
+    if (!on) return 0;
+    ev.resize(cap);
+    cat.assign(cap, -1);
+    for (auto& e : ev)
+      if (cudaEventCreate(&e) != cudaSuccess) return -1;
+    return 0;
+  }
+  void mark(int category) {
+    if (!on || used >= ev.size()) return;
+    cat[used] = category;
+    cudaEventRecord(ev[used], s);
+    if (category == RW_CAT_BUILD_HIST) hist_idx.push_back((int)used);
+    used++;
+  }
+  ~PhaseTimer() {
+    for (auto& e : ev) cudaEventDestroy(e);
+  }
+};
+
+int check_params(rw_ctx* ctx, const rw_train_params* p, uint32_t n_bins) {
+  if (!p) return fail(ctx, RW_ERR_ARG, "params is NULL");
+  if (p->depth < 1 || p->depth > 12) return fail(ctx, RW_ERR_ARG, "depth must be in 1..=12");
+  if (p->n_bins < 2 || p->n_bins > 256) return fail(ctx, RW_ERR_ARG, "n_bins must be in 2..=256");
+  if (p->n_bins != n_bins)
+    return fail(ctx, RW_ERR_ARG, "params n_bins differs from the dataset's n_bins");
+  if (p->objective != RW_OBJ_LOGISTIC && p->objective != RW_OBJ_L2)
+    return fail(ctx, RW_ERR_ARG, "unknown objective");
+  if (p->pgbm) return fail(ctx, RW_ERR_UNSUPPORTED, "pgbm leaf variances are not supported");
+  if (p->clamp_hessian != 0.0f)
+    return fail(ctx, RW_ERR_UNSUPPORTED, "clamp_hessian is not supported");
+  return RW_OK;
+}
+
+}  // namespace
+
+// =================================================================================
+// contexts
+
+extern "C" int rw_ctx_create(const int* gpu_ids, int n_gpus, rw_ctx** out) {
+  if (!out) return fail(nullptr, RW_ERR_ARG, "out is NULL");
+  *out = nullptr;
+  if (n_gpus != 1)
+    return fail(nullptr, RW_ERR_UNSUPPORTED,
+                "rw_ctx_create takes one GPU; use rw_ctx_create_rank per process");
+  return rw_ctx_create_rank(gpu_ids ? gpu_ids[0] : 0, 0, 1, nullptr, out);
+}
+
+extern "C" int rw_nccl_unique_id(void* out128) {
+  if (!out128) return fail(nullptr, RW_ERR_ARG, "out is NULL");
+  ncclUniqueId id;
+  ncclResult_t r = ncclGetUniqueId(&id);
+  if (r != ncclSuccess)
+    return fail(nullptr, RW_ERR_NCCL, std::string("ncclGetUniqueId: ") + ncclGetErrorString(r));
+  static_assert(sizeof(ncclUniqueId) == 128, "NCCL unique id is 128 bytes");
+  memcpy(out128, &id, sizeof id);
+  return RW_OK;
+}
+
+extern "C" int rw_ctx_create_rank(int gpu_id, int rank, int world, const void* nccl_id,
+                                  rw_ctx** out) {
+  if (!out) return fail(nullptr, RW_ERR_ARG, "out is NULL");
+  *out = nullptr;
+  if (world < 1 || rank < 0 || rank >= world) return fail(nullptr, RW_ERR_ARG, "bad rank/world");
+  if (world > 1 && !nccl_id) return fail(nullptr, RW_ERR_ARG, "nccl_id required for world > 1");
+  int ndev = 0;
+  cudaError_t e = cudaGetDeviceCount(&ndev);
+  if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaGetDeviceCount");
+  if (gpu_id < 0 || gpu_id >= ndev) return fail(nullptr, RW_ERR_ARG, "gpu id out of range");
+  rw_ctx* ctx = new rw_ctx();
+  ctx->device = gpu_id;
+  ctx->rank = rank;
+  ctx->world = world;
+  e = cudaSetDevice(gpu_id);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+  if (e != cudaSuccess) {
+    int rc = cuda_fail(nullptr, e, "context setup");
+    delete ctx;
+    return rc;
+  }
+  if (world > 1) {
+    ncclUniqueId id;
+    memcpy(&id, nccl_id, sizeof id);
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    ncclResult_t r = ncclCommInitRankConfig(&ctx->comm, world, id, rank, &cfg);
+    const auto t0 = std::chrono::steady_clock::now();
+    while (r == ncclInProgress || r == ncclSuccess) {
+      ncclResult_t st = ncclInProgress;
+      ncclCommGetAsyncError(ctx->comm, &st);
+      if (st == ncclSuccess) {
+        r = ncclSuccess;
+        break;
+      }
+      if (st != ncclInProgress) {
+        r = st;
+        break;
+      }
+      const double ms = std::chrono::duration<double, std::milli>(
+                            std::chrono::steady_clock::now() - t0).count();
+      if (ms > (double)ctx->timeout_ms) {
+        r = ncclInternalError;
+        break;
+      }
+      std::this_thread::sleep_for(std::chrono::milliseconds(1));
+    }
+    if (r != ncclSuccess) {
+      if (ctx->comm) ncclCommAbort(ctx->comm);
+      cudaStreamDestroy(ctx->stream);
+      delete ctx;
+      return fail(nullptr, RW_ERR_NCCL,
+                  std::string("NCCL communicator init failed: ") + ncclGetErrorString(r));
+    }
+  }
+  *out = ctx;
+  return RW_OK;
+}
+
+extern "C" void rw_ctx_destroy(rw_ctx* ctx) {
+  if (!ctx) return;
+  cudaSetDevice(ctx->device);
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  if (ctx->comm) ncclCommDestroy(ctx->comm);
+  if (ctx->stream) cudaStreamDestroy(ctx->stream);
+  delete ctx;
+}
+
+extern "C" const char* rw_last_error(const rw_ctx* ctx) {
+  return ctx ? ctx->last_error.c_str() : g_tls_error.c_str();
+}
+
+extern "C" void* rw_ctx_stream(const rw_ctx* ctx) { return ctx ? (void*)ctx->stream : nullptr; }
+
+extern "C" int rw_ctx_set_timeout(rw_ctx* ctx, int64_t ms) {
+  if (!ctx || ms < 0) return fail(ctx, RW_ERR_ARG, "bad timeout");
+  ctx->timeout_ms = ms;
+  return RW_OK;
+}
+
+// =================================================================================
+// datasets
+
+static int dataset_build(rw_ctx* ctx, const float* d_x, const float* y, bool y_on_device,
+                         uint64_t n, uint32_t nf, const float* cuts, uint32_t n_bins,
+                         int32_t pack4, uint64_t n_global, uint64_t row_offset,
+                         rw_dataset** out) {
+  int nl = 0;
+  auto* ds = new rw_dataset();
+  ds->ctx = ctx;
+  ds->n = n;
+  ds->n_pad = round_up(n, 64);
+  ds->n_global = n_global;
+  ds->row_offset = row_offset;
+  ds->nf = nf;
+  ds->n_bins = n_bins;
+  ds->packed = (pack4 && n_bins <= 16) ? 1 : 0;
+  ds->cuts.assign(cuts, cuts + (size_t)nf * (n_bins - 1));
+  cudaStream_t s = ctx->stream;
+  DBuf<uint8_t> bins;
+  DBuf<float> dy, dc;
+  cudaError_t e = bins.alloc((size_t)nf * ds->n_pad);
+  if (e == cudaSuccess) e = dy.alloc(ds->n_pad);
+  if (e == cudaSuccess) e = dc.alloc(ds->cuts.size());
+  if (e == cudaSuccess) e = cudaMemsetAsync(bins.p, 0, (size_t)nf * ds->n_pad, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(dy.p, 0, ds->n_pad * sizeof(float), s);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(dc.p, ds->cuts.data(), ds->cuts.size() * sizeof(float),
+                        cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(dy.p, y, n * sizeof(float),
+                        y_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = launch_bin(d_x, n, nf, dc.p, n_bins, bins.p, ds->n_pad, s, &nl);
+  if (e == cudaSuccess && ds->packed) {
+    DBuf<uint8_t> packed;
+    e = packed.alloc((size_t)nf * ds->n_pad / 2);
+    if (e == cudaSuccess) e = launch_pack4(bins.p, ds->n_pad, nf, packed.p, s, &nl);
+    if (e == cudaSuccess) {
+      ds->d_bins_u8 = bins.release();
+      ds->d_bins = packed.release();
+      ds->ld = ds->n_pad / 2;
+    }
+  } else if (e == cudaSuccess) {
+    ds->d_bins = bins.release();
+    ds->ld = ds->n_pad;
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  ctx->launches += nl;
+  if (e != cudaSuccess) {
+    int rc = cuda_fail(ctx, e, "dataset upload/binning");
+    if (ds->d_bins) cudaFree(ds->d_bins);
+    if (ds->d_bins_u8) cudaFree(ds->d_bins_u8);
+    delete ds;
+    return rc;
+  }
+  ds->d_y = dy.release();
+  ds->d_cuts = dc.release();
+  *out = ds;
+  return RW_OK;
+}
+
+static int dataset_args_ok(rw_ctx* ctx, const void* x, const void* y, uint64_t n, uint32_t nf,
+                           const float* cuts, uint32_t n_bins, uint64_t n_global,
+                           uint64_t row_offset, rw_dataset** out) {
+  if (!ctx) return fail(nullptr, RW_ERR_ARG, "ctx is NULL");
+  if (!out || !x || !y || !cuts) return fail(ctx, RW_ERR_ARG, "NULL buffer");
+  if (n == 0 || nf == 0) return fail(ctx, RW_ERR_ARG, "empty dataset");
+  if (n_bins < 2 || n_bins > 256) return fail(ctx, RW_ERR_ARG, "n_bins must be in 2..=256");
+  if (n_global < n || row_offset + n > n_global)
+    return fail(ctx, RW_ERR_ARG, "shard rows exceed n_global");
+  if (n_global > 0xffffffffull) return fail(ctx, RW_ERR_ARG, "more than 2^32 rows");
+  return RW_OK;
+}
+
+extern "C" int rw_dataset_create(rw_ctx* ctx, const float* x, const float* y, uint64_t n,
+                                 uint32_t nf, const float* cuts, uint32_t n_bins, int32_t pack4,
+                                 uint64_t n_global, uint64_t row_offset, rw_dataset** out) {
+  int rc = dataset_args_ok(ctx, x, y, n, nf, cuts, n_bins, n_global, row_offset, out);
+  if (rc) return rc;
+  *out = nullptr;
+  RW_CU(ctx, cudaSetDevice(ctx->device));
+  DBuf<float> dx;
+  RW_CU(ctx, dx.alloc((size_t)n * nf));
+  RW_CU(ctx, cudaMemcpyAsync(dx.p, x, (size_t)n * nf * sizeof(float), cudaMemcpyHostToDevice,
+                             ctx->stream));
+  return dataset_build(ctx, dx.p, y, false, n, nf, cuts, n_bins, pack4, n_global, row_offset,
+                       out);
+}
+
+extern "C" int rw_dataset_create_device(rw_ctx* ctx, const float* d_x, const float* d_y,
+                                        uint64_t n, uint32_t nf, const float* cuts,
+                                        uint32_t n_bins, int32_t pack4, uint64_t n_global,
+                                        uint64_t row_offset, rw_dataset** out) {
+  int rc = dataset_args_ok(ctx, d_x, d_y, n, nf, cuts, n_bins, n_global, row_offset, out);
+  if (rc) return rc;
+  *out = nullptr;
+  RW_CU(ctx, cudaSetDevice(ctx->device));
+  return dataset_build(ctx, d_x, d_y, true, n, nf, cuts, n_bins, pack4, n_global, row_offset,
+                       out);
+}
+
+extern "C" void rw_dataset_destroy(rw_dataset* ds) {
+  if (!ds) return;
+  cudaSetDevice(ds->ctx->device);
+  cudaFree(ds->d_bins);
+  if (ds->d_bins_u8) cudaFree(ds->d_bins_u8);
+  cudaFree(ds->d_y);
+  cudaFree(ds->d_cuts);
+  for (auto& kv : ds->ws) cudaFree(kv.second.first);
+  delete ds;
+}
+
+extern "C" int rw_dataset_bins(const rw_dataset* ds, uint8_t* out) {
+  if (!ds || !out) return fail(nullptr, RW_ERR_ARG, "NULL argument");
+  rw_ctx* ctx = ds->ctx;
+  RW_CU(ctx, cudaSetDevice(ctx->device));
+  const uint8_t* src = ds->packed ? ds->d_bins_u8 : ds->d_bins;
+  RW_CU(ctx, cudaMemcpy2DAsync(out, ds->n, src, ds->n_pad, ds->n, ds->nf, cudaMemcpyDeviceToHost,
+                               ctx->stream));
+  RW_CU(ctx, cudaStreamSynchronize(ctx->stream));
+  return RW_OK;
+}
+
+// =================================================================================
+// training loop
+
+extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float base_score,
+                              uint32_t* feat, float* thr, uint16_t* thr_bin, float* leafval,
+                              float* leafvar, float* fi_gain, float* fi_count, rw_profile* prof) {
+  if (!ds) return fail(nullptr, RW_ERR_ARG, "dataset is NULL");
+  rw_ctx* ctx = ds->ctx;
+  int rc = check_params(ctx, p, ds->n_bins);
+  if (rc) return rc;
+  if (leafvar) return fail(ctx, RW_ERR_UNSUPPORTED, "leafvar output is not supported");
+  if (p->n_trees > 0 && (!feat || !thr || !leafval))
+    return fail(ctx, RW_ERR_ARG, "NULL model output");
+  if (!fi_gain || !fi_count) return fail(ctx, RW_ERR_ARG, "NULL feature-importance output");
+  RW_CU(ctx, cudaSetDevice(ctx->device));
+  cudaStream_t s = ctx->stream;
+
+  const uint32_t T = p->n_trees, D = p->depth, NL = 1u << D, nf = ds->nf, nb = ds->n_bins;
+  const uint64_t n = ds->n, n_pad = ds->n_pad;
+  const bool subtract = p->subtract != 0;
+  const bool logistic = p->objective == RW_OBJ_LOGISTIC;
+  const bool goss = p->goss_top > 0.0f;
+  uint64_t stride = 1;
+  if (!goss && p->subsample < 0.999f) {
+    double sd = std::round(1.0 / (double)p->subsample);
+    if (sd < 1.0) sd = 1.0;
+    stride = sd >= 1.8446744073709552e19 ? UINT64_MAX : (uint64_t)sd;
+  }
+
+  const uint64_t cell = (uint64_t)nf * nb * 2;  // int64 words per histogram node
+  const uint64_t hb_groups = subtract ? std::max<uint64_t>(1, D >= 2 ? (1ull << (D - 2)) : 1)
+                                      : (1ull << (D - 1));
+  const uint64_t hf_nodes = 1ull << (D - 1);
+
+  // Working buffers live in the dataset's cache: repeated fits allocate nothing.
+  WsBuf<float> pred, g, h, d_leafval, d_thr, d_fi_gain, d_fi_count;
+  WsBuf<uint16_t> node, d_thr_bin;
+  WsBuf<long long> hb, hf0, hf1;
+  WsBuf<uint32_t> d_feat, maxbits, best_bin, counter, split_ft;
+  WsBuf<double> best_gain;
+  WsBuf<int32_t> d_mono;
+  WsBuf<unsigned long long> goss_counts;
+  WsBuf<uint32_t> goss_sel;
+  RW_CU(ctx, pred.get(ds, "pred", n_pad));
+  RW_CU(ctx, g.get(ds, "g", n_pad));
+  RW_CU(ctx, h.get(ds, "h", n_pad));
+  RW_CU(ctx, node.get(ds, "node", n_pad));
+  RW_CU(ctx, hb.get(ds, "hb", hb_groups * cell));
+  RW_CU(ctx, hf0.get(ds, "hf0", hf_nodes * cell));
+  RW_CU(ctx, hf1.get(ds, "hf1", hf_nodes * cell));
+  RW_CU(ctx, d_feat.get(ds, "feat", (size_t)T * D));
+  RW_CU(ctx, d_thr.get(ds, "thr", (size_t)T * D));
+  RW_CU(ctx, d_thr_bin.get(ds, "thr_bin", (size_t)T * D));
+  RW_CU(ctx, d_leafval.get(ds, "leafval", (size_t)T * NL));
+  RW_CU(ctx, d_fi_gain.get(ds, "fi_gain", nf));
+  RW_CU(ctx, d_fi_count.get(ds, "fi_count", nf));
+  RW_CU(ctx, maxbits.get(ds, "maxbits", (size_t)std::max<uint32_t>(T, 1) * 2));
+  RW_CU(ctx, best_gain.get(ds, "best_gain", nf));
+  RW_CU(ctx, best_bin.get(ds, "best_bin", nf));
+  RW_CU(ctx, counter.get(ds, "counter", 1));
+  RW_CU(ctx, split_ft.get(ds, "split_ft", 2));
+  RW_CU(ctx, cudaMemsetAsync(g.p, 0, n_pad * 4, s));
+  RW_CU(ctx, cudaMemsetAsync(h.p, 0, n_pad * 4, s));
+  RW_CU(ctx, cudaMemsetAsync(node.p, 0, n_pad * 2, s));
+  RW_CU(ctx, cudaMemsetAsync(d_fi_gain.p, 0, nf * 4, s));
+  RW_CU(ctx, cudaMemsetAsync(d_fi_count.p, 0, nf * 4, s));
+  RW_CU(ctx, cudaMemsetAsync(maxbits.p, 0, maxbits.n * 4, s));
+  RW_CU(ctx, cudaMemsetAsync(counter.p, 0, 4, s));
+  RW_CU(ctx, cudaMemsetAsync(d_leafval.p, 0, std::max<size_t>(d_leafval.n, 1) * 4, s));
+  bool any_mono = false;
+  std::vector<int32_t> mono(nf, 0);
+  for (uint32_t i = 0; i < std::min<uint32_t>(nf, p->monotone ? p->n_monotone : 0); i++) {
+    mono[i] = p->monotone[i];
+    any_mono |= mono[i] != 0;
+  }
+  if (any_mono) {
+    RW_CU(ctx, d_mono.get(ds, "mono", nf));
+    RW_CU(ctx, cudaMemcpyAsync(d_mono.p, mono.data(), nf * 4, cudaMemcpyHostToDevice, s));
+  }
+  GossState gst{nullptr, nullptr};
+  if (goss) {
+    RW_CU(ctx, goss_counts.get(ds, "goss_counts", 256));
+    RW_CU(ctx, goss_sel.get(ds, "goss_sel", 4));
+    RW_CU(ctx, cudaMemsetAsync(goss_counts.p, 0, 256 * 8, s));
+    gst.counts = goss_counts.p;
+    gst.sel = goss_sel.p;
+  }
+  int nl = 0;
+  RW_CU(ctx, launch_fill_f32(pred.p, base_score, n_pad, s, &nl));
+
+  PhaseTimer pt;
+  const bool profiling = prof && prof->enable;
+  if (pt.init(profiling, s, (size_t)T * (5 * D + 8) + 4) != 0)
+    return fail(ctx, RW_ERR_CUDA, "event creation failed");
+  cudaEvent_t ev0, ev1;
+  RW_CU(ctx, cudaEventCreate(&ev0));
+  RW_CU(ctx, cudaEventCreate(&ev1));
+  RW_CU(ctx, cudaEventRecord(ev0, s));
+  pt.mark(-1);
+
+  // GOSS constants (src/cpu.rs:72-78), over the global row count.
+  const uint64_t ng = ds->n_global;
+  const double top = (double)p->goss_top, other = (double)p->goss_other;
+  double tn = top * (double)ng;
+  uint64_t topn = tn <= 0.0 ? 0 : (uint64_t)tn;
+  topn = std::min<uint64_t>(std::max<uint64_t>(topn, 1), ng);
+  const uint64_t goss_k = std::min<uint64_t>(topn - 1, ng - 1);
+  double keep_prob = other / std::max(1.0 - top, 1e-9);
+  keep_prob = std::min(std::max(keep_prob, 0.0), 1.0);
+  const float goss_fact = (float)((1.0 - top) / std::max(other, 1e-9));
+
+  double alg_bytes = 0.0;
+  uint64_t hist_launches = 0;
+  const double bin_bytes = ds->packed ? 0.5 : 1.0;
+  const uint64_t dsz = n_pad * 4;
+  (void)dsz;
+
+  for (uint32_t t = 0; t < T; t++) {
+    uint32_t* mb = maxbits.p + 2 * (size_t)t;
+    if (goss) {
+      RW_CU(ctx, launch_grad(pred.p, ds->d_y, g.p, h.p, node.p, n, logistic, 1, 0, ds->row_offset,
+                             0, mb, s, &nl));
+      RW_CU(ctx, launch_goss_init(gst, goss_k, s, &nl));
+      for (int pass = 0; pass < 4; pass++) {
+        RW_CU(ctx, launch_goss_digit_hist(g.p, n, gst, pass, s, &nl));
+        if (ctx->comm)
+          RW_NC(ctx, ncclAllReduce(gst.counts, gst.counts, 256, ncclUint64, ncclSum, ctx->comm, s));
+        RW_CU(ctx, launch_goss_digit_select(gst, pass, s, &nl));
+      }
+      RW_CU(ctx, launch_goss_apply(g.p, h.p, n, ds->row_offset, gst, keep_prob, goss_fact,
+                                   (uint64_t)t, mb, s, &nl));
+    } else {
+      RW_CU(ctx, launch_grad(pred.p, ds->d_y, g.p, h.p, node.p, n, logistic, stride,
+                             stride > 1 ? (uint64_t)t % stride : 0, ds->row_offset, 1, mb, s,
+                             &nl));
+    }
+    if (ctx->comm) RW_NC(ctx, ncclAllReduce(mb, mb, 2, ncclUint32, ncclMax, ctx->comm, s));
+    pt.mark(RW_CAT_GRADIENTS);
+
+    const uint32_t tree_seed = t * 2654435761u + 0x455A4B41u;  // src/booster.rs:351
+    for (uint32_t d = 0; d < D; d++) {
+      const uint32_t n_nodes = 1u << d;
+      const int mode = (d == 0 || !subtract) ? 0 : 1;
+      const uint32_t groups = mode == 0 ? n_nodes : n_nodes / 2;
+      RW_CU(ctx, cudaMemsetAsync(hb.p, 0, (size_t)groups * cell * 8, s));
+      pt.mark(RW_CAT_ZERO_HIST);
+      HistLaunch hl;
+      hl.bins = ds->d_bins;
+      hl.ld = ds->ld;
+      hl.packed = ds->packed;
+      hl.node = node.p;
+      hl.g = g.p;
+      hl.h = h.p;
+      hl.n_pad = n_pad;
+      hl.nf = nf;
+      hl.nb = nb;
+      hl.groups = groups;
+      hl.odd_only = mode;
+      hl.maxbits = mb;
+      hl.e_override = nullptr;
+      hl.out = hb.p;
+      RW_CU(ctx, launch_hist(hl, s, &nl));
+      hist_launches++;
+      alg_bytes += (double)n * nf * bin_bytes + 12.0 * (double)n + 8.0 * nf * nb * groups;
+      pt.mark(RW_CAT_BUILD_HIST);
+      if (ctx->comm) {
+        RW_NC(ctx, ncclAllReduce(hb.p, hb.p, (size_t)groups * cell, ncclInt64, ncclSum, ctx->comm,
+                                 s));
+        pt.mark(RW_CAT_ALLREDUCE);
+      }
+      SplitLaunch sl;
+      sl.hb = hb.p;
+      sl.hp = (d & 1) ? hf0.p : hf1.p;
+      sl.hf = (d & 1) ? hf1.p : hf0.p;
+      sl.n_nodes = n_nodes;
+      sl.nf = nf;
+      sl.nb = nb;
+      sl.mode = mode;
+      sl.maxbits = mb;
+      sl.lambda = (double)p->lambda;
+      sl.min_child = (double)p->min_child_h;
+      sl.lr = (double)p->learning_rate;
+      sl.monotone = any_mono ? d_mono.p : nullptr;
+      sl.colsample = p->colsample;
+      sl.tree_seed = tree_seed;
+      sl.best_gain = best_gain.p;
+      sl.best_bin = best_bin.p;
+      sl.counter = counter.p;
+      sl.cuts = ds->d_cuts;
+      sl.feat = d_feat.p;
+      sl.thr = d_thr.p;
+      sl.thr_bin = d_thr_bin.p;
+      sl.split_ft = split_ft.p;
+      sl.fi_gain = d_fi_gain.p;
+      sl.fi_count = d_fi_count.p;
+      sl.slot = t * D + d;
+      sl.last_level = d == D - 1;
+      sl.leafval = d_leafval.p;
+      sl.leaf_base = t * NL;
+      RW_CU(ctx, launch_split(sl, s));
+      nl++;
+      pt.mark(RW_CAT_SPLIT);
+      RW_CU(ctx, launch_apply(ds->d_bins, ds->ld, ds->packed, node.p, split_ft.p, n_pad,
+                              d == D - 1, d_leafval.p, t * NL, pred.p, s, &nl));
+      pt.mark(d == D - 1 ? RW_CAT_UPDATE_PRED : RW_CAT_APPLY);
+    }
+  }
+  RW_CU(ctx, cudaEventRecord(ev1, s));
+  rc = wait_stream(ctx);
+  if (rc) return rc;
+  ctx->launches += nl;
+
+  if (T > 0) {
+    RW_CU(ctx, cudaMemcpy(feat, d_feat.p, (size_t)T * D * 4, cudaMemcpyDeviceToHost));
+    RW_CU(ctx, cudaMemcpy(thr, d_thr.p, (size_t)T * D * 4, cudaMemcpyDeviceToHost));
+    if (thr_bin)
+      RW_CU(ctx, cudaMemcpy(thr_bin, d_thr_bin.p, (size_t)T * D * 2, cudaMemcpyDeviceToHost));
+    RW_CU(ctx, cudaMemcpy(leafval, d_leafval.p, (size_t)T * NL * 4, cudaMemcpyDeviceToHost));
+  }
+  RW_CU(ctx, cudaMemcpy(fi_gain, d_fi_gain.p, nf * 4, cudaMemcpyDeviceToHost));
+  RW_CU(ctx, cudaMemcpy(fi_count, d_fi_count.p, nf * 4, cudaMemcpyDeviceToHost));
+
+  if (prof) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, ev0, ev1);
+    prof->total_ms = ms;
+    for (int c = 0; c < RW_N_CATEGORIES; c++) prof->category_ms[c] = 0.0;
+    if (profiling) {
+      for (size_t i = 1; i < pt.used; i++) {
+        float dt = 0.f;
+        cudaEventElapsedTime(&dt, pt.ev[i - 1], pt.ev[i]);
+        if (pt.cat[i] >= 0) prof->category_ms[pt.cat[i]] += dt;
+      }
+    }
+    prof->hist_alg_bytes = alg_bytes;
+    prof->hist_launches = hist_launches;
+    prof->kernel_launches = (uint64_t)nl;
+  }
+  cudaEventDestroy(ev0);
+  cudaEventDestroy(ev1);
+  return RW_OK;
+}
+
+extern "C" int rw_fit(rw_ctx* ctx, const rw_train_params* p, const float* x, const float* y,
+                      uint64_t n, uint32_t nf, const float* cuts, float base_score,
+                      uint32_t* feat, float* thr, uint16_t* thr_bin, float* leafval,
+                      float* leafvar, float* fi_gain, float* fi_count, rw_profile* prof) {
+  if (!p) return fail(ctx, RW_ERR_ARG, "params is NULL");
+  rw_dataset* ds = nullptr;
+  int rc = rw_dataset_create(ctx, x, y, n, nf, cuts, p->n_bins, p->pack4, n, 0, &ds);
+  if (rc) return rc;
+  rc = rw_fit_dataset(ds, p, base_score, feat, thr, thr_bin, leafval, leafvar, fi_gain, fi_count,
+                      prof);
+  rw_dataset_destroy(ds);
+  return rc;
+}
+
+// =================================================================================
+// scoring
+
+static int model_check(rw_ctx* ctx, const rw_model* m, bool need_bins) {
+  if (!ctx) return fail(nullptr, RW_ERR_ARG, "ctx is NULL");
+  if (!m) return fail(ctx, RW_ERR_ARG, "model is NULL");
+  if (m->depth < 1 || m->depth > 12) return fail(ctx, RW_ERR_ARG, "depth must be in 1..=12");
+  if (m->n_trees > 0 && (!m->feat || !m->leafval)) return fail(ctx, RW_ERR_ARG, "NULL model array");
+  if (m->n_trees > 0 && !need_bins && !m->thr) return fail(ctx, RW_ERR_ARG, "NULL thr");
+  if (m->n_trees > 0 && need_bins && !m->thr_bin)
+    return fail(ctx, RW_ERR_ARG, "u8 scoring needs thr_bin");
+  for (size_t k = 0; k < (size_t)m->n_trees * m->depth; k++) {
+    if (m->feat[k] >= m->n_features) return fail(ctx, RW_ERR_ARG, "feature index out of range");
+    if (need_bins && m->thr_bin[k] > 255) return fail(ctx, RW_ERR_ARG, "thr_bin above 255");
+  }
+  return RW_OK;
+}
+
+extern "C" int rw_model_upload(rw_ctx* ctx, const rw_model* m, rw_dmodel** out) {
+  if (!out) return fail(ctx, RW_ERR_ARG, "out is NULL");
+  *out = nullptr;
+  int rc = model_check(ctx, m, false);
+  if (rc) return rc;
+  RW_CU(ctx, cudaSetDevice(ctx->device));
+  const size_t K = (size_t)m->n_trees * m->depth, L = (size_t)m->n_trees << m->depth;
+  DBuf<uint32_t> df, ds8;
+  DBuf<float> dt, dl;
+  RW_CU(ctx, df.alloc(K));
+  RW_CU(ctx, dt.alloc(K));
+  RW_CU(ctx, dl.alloc(L));
+  RW_CU(ctx, ds8.alloc(K));
+  std::vector<uint32_t> s8(K, 0);
+  for (size_t k = 0; k < K; k++)
+    s8[k] = (m->feat[k] << 8) | (m->thr_bin ? (uint32_t)(m->thr_bin[k] & 0xff) : 0u);
+  if (K) {
+    RW_CU(ctx, cudaMemcpy(df.p, m->feat, K * 4, cudaMemcpyHostToDevice));
+    if (m->thr) RW_CU(ctx, cudaMemcpy(dt.p, m->thr, K * 4, cudaMemcpyHostToDevice));
+    RW_CU(ctx, cudaMemcpy(ds8.p, s8.data(), K * 4, cudaMemcpyHostToDevice));
+    RW_CU(ctx, cudaMemcpy(dl.p, m->leafval, L * 4, cudaMemcpyHostToDevice));
+  }
+  auto* dm = new rw_dmodel();
+  dm->ctx = ctx;
+  dm->n_trees = m->n_trees;
+  dm->depth = m->depth;
+  dm->nf = m->n_features;
+  dm->base = m->base_score;
+  dm->has_bins = m->thr_bin != nullptr;
+  dm->d_feat = df.release();
+  dm->d_thr = dt.release();
+  dm->d_split8 = ds8.release();
+  dm->d_leafval = dl.release();
+  *out = dm;
+  return RW_OK;
+}
+
+extern "C" void rw_model_free(rw_dmodel* dm) {
+  if (!dm) return;
+  cudaSetDevice(dm->ctx->device);
+  cudaFree(dm->d_feat);
+  cudaFree(dm->d_thr);
+  cudaFree(dm->d_split8);
+  cudaFree(dm->d_leafval);
+  delete dm;
+}
+
+static int predict_device_common(rw_ctx* ctx, const rw_dmodel* dm, float* d_out, uint64_t n,
+                                 float* kernel_ms, bool u8, const void* in, uint64_t ld) {
+  if (!ctx || !dm || (n > 0 && (!in || !d_out))) return fail(ctx, RW_ERR_ARG, "NULL argument");
+  if (u8 && !dm->has_bins) return fail(ctx, RW_ERR_ARG, "model uploaded without thr_bin");
+  if (u8 && ld < n) return fail(ctx, RW_ERR_ARG, "ld < n");
+  RW_CU(ctx, cudaSetDevice(ctx->device));
+  cudaEvent_t a = nullptr, b = nullptr;
+  if (kernel_ms) {
+    RW_CU(ctx, cudaEventCreate(&a));
+    RW_CU(ctx, cudaEventCreate(&b));
+    RW_CU(ctx, cudaEventRecord(a, ctx->stream));
+  }
+  cudaError_t e = cudaSuccess;
+  int nl = 0;
+  if (n > 0) {
+    if (dm->n_trees == 0) e = launch_fill_f32(d_out, dm->base, n, ctx->stream, &nl);
+    else if (u8) e = launch_predict_u8((const uint8_t*)in, n, ld, *dm, d_out, ctx->stream);
+    else e = launch_predict_f32((const float*)in, n, dm->nf, *dm, d_out, ctx->stream);
+    nl += 1;
+  }
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "predict launch");
+  ctx->launches += nl;
+  if (kernel_ms) {
+    RW_CU(ctx, cudaEventRecord(b, ctx->stream));
+    RW_CU(ctx, cudaEventSynchronize(b));
+    cudaEventElapsedTime(kernel_ms, a, b);
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+  }
+  return RW_OK;
+}
+
+extern "C" int rw_predict_u8_device(rw_ctx* ctx, const rw_dmodel* dm, const uint8_t* d_bins,
+                                    uint64_t n, uint64_t ld, float* d_out, float* kernel_ms) {
+  return predict_device_common(ctx, dm, d_out, n, kernel_ms, true, d_bins, ld);
+}
+
+extern "C" int rw_predict_f32_device(rw_ctx* ctx, const rw_dmodel* dm, const float* d_x,
+                                     uint64_t n, float* d_out, float* kernel_ms) {
+  return predict_device_common(ctx, dm, d_out, n, kernel_ms, false, d_x, 0);
+}
+
+extern "C" int rw_predict_f32(rw_ctx* ctx, const rw_model* m, const float* x, uint64_t n,
+                              uint32_t nf, float* out) {
+  int rc = model_check(ctx, m, false);
+  if (rc) return rc;
+  if (nf != m->n_features) return fail(ctx, RW_ERR_ARG, "nf differs from the model's n_features");
+  if (n == 0) return RW_OK;
+  if (!x || !out) return fail(ctx, RW_ERR_ARG, "NULL buffer");
+  rw_dmodel* dm = nullptr;
+  rc = rw_model_upload(ctx, m, &dm);
+  if (rc) return rc;
+  DBuf<float> dx, dout;
+  cudaError_t e = dx.alloc((size_t)n * nf);
+  if (e == cudaSuccess) e = dout.alloc(n);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(dx.p, x, (size_t)n * nf * 4, cudaMemcpyHostToDevice, ctx->stream);
+  if (e != cudaSuccess) {
+    rw_model_free(dm);
+    return cuda_fail(ctx, e, "predict upload");
+  }
+  rc = rw_predict_f32_device(ctx, dm, dx.p, n, dout.p, nullptr);
+  if (!rc) {
+    e = cudaMemcpyAsync(out, dout.p, n * 4, cudaMemcpyDeviceToHost, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) rc = cuda_fail(ctx, e, "predict download");
+  }
+  rw_model_free(dm);
+  return rc;
+}
+
+extern "C" int rw_predict_u8(rw_ctx* ctx, const rw_model* m, const uint8_t* bins, uint64_t n,
+                             uint32_t nf, float* out) {
+  int rc = model_check(ctx, m, true);
+  if (rc) return rc;
+  if (nf != m->n_features) return fail(ctx, RW_ERR_ARG, "nf differs from the model's n_features");
+  if (n == 0) return RW_OK;
+  if (!bins || !out) return fail(ctx, RW_ERR_ARG, "NULL buffer");
+  rw_dmodel* dm = nullptr;
+  rc = rw_model_upload(ctx, m, &dm);
+  if (rc) return rc;
+  const uint64_t ld = round_up(n, 16);
+  DBuf<uint8_t> db;
+  DBuf<float> dout;
+  cudaError_t e = db.alloc((size_t)nf * ld);
+  if (e == cudaSuccess) e = dout.alloc(n);
+  if (e == cudaSuccess) e = cudaMemsetAsync(db.p, 0, (size_t)nf * ld, ctx->stream);
+  if (e == cudaSuccess)
+    e = cudaMemcpy2DAsync(db.p, ld, bins, n, n, nf, cudaMemcpyHostToDevice, ctx->stream);
+  if (e != cudaSuccess) {
+    rw_model_free(dm);
+    return cuda_fail(ctx, e, "predict upload");
+  }
+  rc = rw_predict_u8_device(ctx, dm, db.p, n, ld, dout.p, nullptr);
+  if (!rc) {
+    e = cudaMemcpyAsync(out, dout.p, n * 4, cudaMemcpyDeviceToHost, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) rc = cuda_fail(ctx, e, "predict download");
+  }
+  rw_model_free(dm);
+  return rc;
+}
+
+// =================================================================================
+// host helpers (reference host code, restated natively)
+
+extern "C" void rw_compute_boundaries(const float* x, uint64_t n, uint32_t nf, uint32_t n_bins,
+                                      uint64_t sample, int32_t unique, float* out) {
+  // src/data.rs:86-146: strided sample, stable sort, quantile (or unique-midpoint) cuts.
+  if (!x || !out || n_bins < 2 || n == 0) return;
+  const uint32_t nbound = n_bins - 1;
+  const uint64_t stride = std::max<uint64_t>(n / std::max<uint64_t>(sample, 1), 1);
+  std::vector<float> s;
+  s.reserve(n / stride + 1);
+  for (uint32_t f = 0; f < nf; f++) {
+    s.clear();
+    for (uint64_t i = 0; i < n; i += stride) s.push_back(x[i * nf + f]);
+    std::stable_sort(s.begin(), s.end(), [](float a, float b) { return a < b; });
+    float* b = out + (size_t)f * nbound;
+    if (unique) {
+      std::vector<float> u;
+      for (float v : s)
+        if (u.empty() || u.back() != v) u.push_back(v);
+      std::vector<float> cand;
+      for (size_t i = 0; i + 1 < u.size(); i++) cand.push_back(0.5f * (u[i] + u[i + 1]));
+      for (uint32_t j = 0; j < nbound; j++) {
+        if (cand.empty()) b[j] = INFINITY;
+        else if (cand.size() <= nbound) b[j] = j < cand.size() ? cand[j] : INFINITY;
+        else {
+          size_t pos = ((size_t)(j + 1) * cand.size()) / (nbound + 1);
+          b[j] = cand[std::min(pos, cand.size() - 1)];
+        }
+      }
+    } else {
+      const size_t m = s.size();
+      for (uint32_t j = 0; j < nbound; j++) {
+        const double q = (double)(j + 1) / (double)n_bins;
+        const size_t pos = (size_t)std::round(q * (double)(m - 1));
+        b[j] = s[std::min(pos, m - 1)];
+      }
+      for (uint32_t j = 1; j < nbound; j++)
+        if (b[j] <= b[j - 1]) b[j] = b[j - 1];
+    }
+  }
+}
+
+extern "C" float rw_base_score(const float* y, uint64_t n, int32_t objective) {
+  // src/booster.rs:201-205: f32 sequential mean, clamped, logit for logistic.
+  float s = 0.0f;
+  for (uint64_t i = 0; i < n; i++) s += y[i];
+  float mean = s / (float)n;
+  mean = std::min(std::max(mean, 1e-6f), 1.0f - 1e-6f);
+  return objective == RW_OBJ_LOGISTIC ? std::log(mean / (1.0f - mean)) : mean;
+}
+
+// =================================================================================
+// test hooks
+
+extern "C" int rw_debug_level_hist(rw_dataset* ds, const int32_t* node, const float* g,
+                                   const float* h, int32_t e_g, int32_t e_h, uint32_t groups,
+                                   int32_t odd_only, int64_t* out) {
+  if (!ds || !node || !g || !h || !out || groups == 0) return fail(nullptr, RW_ERR_ARG, "NULL argument");
+  rw_ctx* ctx = ds->ctx;
+  RW_CU(ctx, cudaSetDevice(ctx->device));
+  const uint64_t n = ds->n, n_pad = ds->n_pad;
+  std::vector<uint16_t> nd(n_pad, 0);
+  std::vector<float> gg(n_pad, 0.f), hh(n_pad, 0.f);
+  for (uint64_t i = 0; i < n; i++) {
+    if (node[i] < 0) continue;
+    if (node[i] > 0xffff) return fail(ctx, RW_ERR_ARG, "node index above 65535");
+    nd[i] = (uint16_t)node[i];
+    gg[i] = g[i];
+    hh[i] = h[i];
+  }
+  const size_t words = (size_t)groups * ds->nf * ds->n_bins * 2;
+  DBuf<uint16_t> dn;
+  DBuf<float> dg, dh;
+  DBuf<long long> dout;
+  DBuf<int32_t> de;
+  RW_CU(ctx, dn.alloc(n_pad));
+  RW_CU(ctx, dg.alloc(n_pad));
+  RW_CU(ctx, dh.alloc(n_pad));
+  RW_CU(ctx, dout.alloc(words));
+  RW_CU(ctx, de.alloc(2));
+  const int32_t ev[2] = {e_g, e_h};
+  RW_CU(ctx, cudaMemcpy(dn.p, nd.data(), n_pad * 2, cudaMemcpyHostToDevice));
+  RW_CU(ctx, cudaMemcpy(dg.p, gg.data(), n_pad * 4, cudaMemcpyHostToDevice));
+  RW_CU(ctx, cudaMemcpy(dh.p, hh.data(), n_pad * 4, cudaMemcpyHostToDevice));
+  RW_CU(ctx, cudaMemcpy(de.p, ev, 8, cudaMemcpyHostToDevice));
+  RW_CU(ctx, cudaMemset(dout.p, 0, words * 8));
+  HistLaunch hl;
+  hl.bins = ds->d_bins;
+  hl.ld = ds->ld;
+  hl.packed = ds->packed;
+  hl.node = dn.p;
+  hl.g = dg.p;
+  hl.h = dh.p;
+  hl.n_pad = n_pad;
+  hl.nf = ds->nf;
+  hl.nb = ds->n_bins;
+  hl.groups = groups;
+  hl.odd_only = odd_only;
+  hl.maxbits = nullptr;
+  hl.e_override = de.p;
+  hl.out = dout.p;
+  int nl = 0;
+  RW_CU(ctx, launch_hist(hl, ctx->stream, &nl));
+  RW_CU(ctx, cudaStreamSynchronize(ctx->stream));
+  ctx->launches += nl;
+  RW_CU(ctx, cudaMemcpy(out, dout.p, words * 8, cudaMemcpyDeviceToHost));
+  return RW_OK;
+}
+
+extern "C" int rw_debug_expf(rw_ctx* ctx, const float* x, uint64_t n, float* out_rw,
+                             float* out_cuda) {
+  if (!ctx || !x || !out_rw || !out_cuda) return fail(ctx, RW_ERR_ARG, "NULL argument");
+  RW_CU(ctx, cudaSetDevice(ctx->device));
+  DBuf<float> dx, dr, dc;
+  RW_CU(ctx, dx.alloc(n));
+  RW_CU(ctx, dr.alloc(n));
+  RW_CU(ctx, dc.alloc(n));
+  RW_CU(ctx, cudaMemcpy(dx.p, x, n * 4, cudaMemcpyHostToDevice));
+  RW_CU(ctx, launch_debug_expf(dx.p, n, dr.p, dc.p, ctx->stream));
+  RW_CU(ctx, cudaStreamSynchronize(ctx->stream));
+  RW_CU(ctx, cudaMemcpy(out_rw, dr.p, n * 4, cudaMemcpyDeviceToHost));
+  RW_CU(ctx, cudaMemcpy(out_cuda, dc.p, n * 4, cudaMemcpyDeviceToHost));
+  ctx->launches += 1;
+  return RW_OK;
+}

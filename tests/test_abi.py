@@ -1,0 +1,71 @@
+"""The C-ABI library loads and exports every entry point include/rwgpu.h declares
+(no compute calls: these run without a GPU)."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+import oracle
+from rustwood_b200 import _native as N
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    hdr = open(os.path.join(ROOT, "include", "rwgpu.h")).read()
+    hdr = re.sub(r"/\*.*?\*/", "", hdr, flags=re.S)
+    return sorted(set(re.findall(r"\b(rw_[a-z0-9_]+)\s*\(", hdr)))
+
+
+def test_every_declared_symbol_is_exported():
+    syms = declared_symbols()
+    assert len(syms) >= 20
+    lib = ctypes.CDLL(N.LIB_PATH)
+    missing = [s for s in syms if not hasattr(lib, s)]
+    assert not missing, missing
+    assert sorted(N.EXPORTED) == syms
+
+
+def test_library_is_built_for_sm100a():
+    # the fatbin of an sm_100a build carries the arch string in its ELF note/section names
+    blob = open(N.LIB_PATH, "rb").read()
+    assert b"sm_100a" in blob
+
+
+def test_context_without_device_reports_an_error():
+    try:
+        import torch
+        if torch.cuda.is_available():
+            pytest.skip("a GPU is present")
+    except ImportError:
+        pass
+    h = ctypes.c_void_p()
+    rc = N.lib.rw_ctx_create_rank(0, 0, 1, None, ctypes.byref(h))
+    assert rc != 0
+    assert N.lib.rw_last_error(None)
+
+
+def test_bad_arguments_fail_cleanly():
+    h = ctypes.c_void_p()
+    assert N.lib.rw_ctx_create_rank(0, 2, 2, None, ctypes.byref(h)) == -1  # rank >= world
+    assert N.lib.rw_ctx_create(None, 2, ctypes.byref(h)) == -5  # multi-GPU per process
+    assert N.lib.rw_nccl_unique_id(None) == -1
+
+
+@pytest.mark.parametrize("seed,n,nf,nb,uniq", [
+    (0, 10_000, 5, 255, False), (1, 3_000, 3, 16, False), (2, 5_000, 4, 64, True),
+    (3, 17, 2, 255, False), (4, 900, 3, 255, True), (5, 250_000, 2, 255, False),
+])
+def test_host_boundaries_and_base_score_match_oracle(seed, n, nf, nb, uniq):
+    import rustwood_b200 as rb
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((n, nf)).astype(np.float32)
+    x[:, 0] = np.round(x[:, 0] * 3)  # ties / low cardinality
+    got = rb.compute_boundaries(x, nb, 200_000, uniq)
+    want = oracle.compute_boundaries(x, nb, 200_000, uniq)
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+    y = (rng.random(n) < 0.3).astype(np.float32)
+    for obj in ("logistic", "l2"):
+        assert np.float32(rb.base_score(y, obj)) == np.float32(oracle.base_score(y, obj))

@@ -1,0 +1,180 @@
+"""The CPU oracle against the golden fixtures, the pure-Python restatement and the
+reference's own self-checks restated as known-answer tests (CPU only)."""
+import ctypes
+import glob
+import os
+import sys
+
+import numpy as np
+import pytest
+
+import oracle
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+import pyref  # noqa: E402
+
+GOLDEN = sorted(glob.glob(os.path.join(HERE, "golden", "*.npz")))
+
+
+@pytest.mark.parametrize("path", GOLDEN, ids=[os.path.basename(p) for p in GOLDEN])
+def test_oracle_matches_golden(path):
+    z = np.load(path)
+    nb, uniq, trees, depth, lr, is_l2, exact, nt, sub = z["params"]
+    nb, trees, depth, nt = int(nb), int(trees), int(depth), int(nt)
+    cuts = oracle.compute_boundaries(z["x"], nb, unique=bool(uniq))
+    np.testing.assert_array_equal(cuts.view(np.uint32), z["cuts"].view(np.uint32))
+    obj = "l2" if is_l2 else "logistic"
+    assert np.float32(oracle.base_score(z["y"], obj)) == z["base"]
+    r = oracle.train(z["x"], z["y"], cuts, float(z["base"]), n_trees=trees, depth=depth,
+                     n_bins=nb, learning_rate=float(lr), objective=obj, exact=bool(exact),
+                     n_threads=nt, subsample=float(sub))
+    for k in ("feat", "thr_bin"):
+        np.testing.assert_array_equal(getattr(r, k), z[k])
+    for k in ("thr", "leafval", "fi_gain", "fi_count"):
+        np.testing.assert_array_equal(getattr(r, k).view(np.uint32), z[k].view(np.uint32))
+    p = oracle.predict(z["x"], r.feat, r.thr, r.leafval, float(z["base"]), trees, depth)
+    np.testing.assert_array_equal(p.view(np.uint32), z["pred"].view(np.uint32))
+
+
+@pytest.mark.parametrize("exact,nt,obj,subtract", [
+    (True, 1, "logistic", True), (False, 1, "logistic", True), (False, 4, "logistic", True),
+    (False, 3, "l2", False), (True, 2, "l2", False),
+])
+def test_oracle_matches_python_restatement(exact, nt, obj, subtract):
+    rng = np.random.default_rng(17 + nt)
+    n, nf, nb = 120, 3, 7
+    x = rng.standard_normal((n, nf)).astype(np.float32)
+    y = ((rng.random(n) < 0.5) if obj == "logistic" else rng.standard_normal(n)).astype(np.float32)
+    cuts = pyref.boundaries(x, nb)
+    base = np.float32(oracle.base_score(y, obj))
+    a = pyref.train(x, y, cuts, base, n_trees=2, depth=3, n_bins=nb, learning_rate=0.3,
+                    objective=obj, exact=exact, n_threads=nt, subtract=subtract)
+    b = oracle.train(x, y, cuts, float(base), n_trees=2, depth=3, n_bins=nb, learning_rate=0.3,
+                     objective=obj, exact=exact, n_threads=nt, subtract=subtract)
+    for k in ("feat", "thr_bin", "thr", "leafval", "fi_gain", "fi_count"):
+        np.testing.assert_array_equal(a[k].view(np.uint32), getattr(b, k).view(np.uint32))
+
+
+def test_kat_shared_memory_spike():
+    """src/main.rs:27-47: 256 rows with bins i % 16 and unit weight give 16 per bin."""
+    n = 256
+    bins = (np.arange(n) % 16).astype(np.uint8).reshape(n, 1)
+    node = np.zeros(n, np.int32)
+    g = np.ones(n, np.float32)
+    h = np.ones(n, np.float32)
+    hist = oracle.level_hist_exact(bins, node, g, h, 0, 0, 1, False, 16)
+    assert (hist[0, 0, :, 0] == 16).all() and (hist[0, 0, :, 1] == 16).all()
+
+
+def test_kat_bin_split_equivalence():
+    """src/gpu_kernels.rs:497-498: with bin = #{cut < v}, `bin > t` <=> `v > cut[t]`."""
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((5000, 3)).astype(np.float32)
+    x[:, 1] = np.round(x[:, 1])
+    cuts = oracle.compute_boundaries(x, 32)
+    bins = oracle.bin_rowmajor(x, cuts, 32)
+    c = cuts.reshape(3, 31)
+    for f in range(3):
+        for t in range(31):
+            np.testing.assert_array_equal(bins[:, f] > t, x[:, f] > c[f, t])
+
+
+def test_exact_and_faithful_modes_agree_on_clear_splits():
+    from rustwood_b200 import synth
+    x, y, xt, yt = synth.c1(20_000, 5_000, seed=2)
+    cuts = oracle.compute_boundaries(x, 255)
+    base = oracle.base_score(y)
+    a = oracle.train(x, y, cuts, base, n_trees=15, depth=6, n_bins=255, learning_rate=0.2,
+                     exact=True, n_threads=4)
+    b = oracle.train(x, y, cuts, base, n_trees=15, depth=6, n_bins=255, learning_rate=0.2,
+                     exact=False, n_threads=8)
+    np.testing.assert_array_equal(a.feat, b.feat)
+    np.testing.assert_array_equal(a.thr_bin, b.thr_bin)
+    np.testing.assert_allclose(a.leafval, b.leafval, rtol=1e-5, atol=1e-7)
+    pa = oracle.predict(xt, a.feat, a.thr, a.leafval, base, 15, 6)
+    pb = oracle.predict(xt, b.feat, b.thr, b.leafval, base, 15, 6)
+    assert abs(oracle.metric("auc", pa, yt) - oracle.metric("auc", pb, yt)) < 1e-4
+    assert abs(oracle.metric("logloss", pa, yt) - oracle.metric("logloss", pb, yt)) < 1e-4
+
+
+def test_exact_mode_is_thread_count_invariant():
+    from rustwood_b200 import synth
+    x, y, _, _ = synth.c1(8_000, seed=4)
+    cuts = oracle.compute_boundaries(x, 64)
+    base = oracle.base_score(y)
+    runs = [oracle.train(x, y, cuts, base, n_trees=6, depth=5, n_bins=64, exact=True,
+                         n_threads=nt) for nt in (1, 3, 8)]
+    for r in runs[1:]:
+        np.testing.assert_array_equal(r.leafval.view(np.uint32), runs[0].leafval.view(np.uint32))
+
+
+def _correctly_rounded_expf(v: np.float32) -> np.float32:
+    from decimal import Decimal, getcontext
+    getcontext().prec = 60
+    e = Decimal(float(v)).exp()
+    f = np.float32(float(e))
+    cands = [np.nextafter(f, np.float32(-np.inf)), f, np.nextafter(f, np.float32(np.inf))]
+    return min(cands, key=lambda c: abs(Decimal(float(c)) - e))
+
+
+def test_rw_expf_error_against_glibc():
+    """The shared exponential is within 1 ulp of glibc expf over the logistic link's
+    input range, and wherever the two differ it is the correctly rounded one (glibc's
+    expf is not correctly rounded everywhere)."""
+    libm = ctypes.CDLL("libm.so.6")
+    libm.expf.argtypes = [ctypes.c_float]
+    libm.expf.restype = ctypes.c_float
+    rng = np.random.default_rng(0)
+    xs = np.concatenate([rng.uniform(-104, 89, 20_000), rng.normal(0, 2, 20_000),
+                         np.linspace(-1e-3, 1e-3, 2_001)]).astype(np.float32)
+    worst, same = 0, 0
+    for v in xs:
+        a = np.float32(oracle.rw_expf(float(v)))
+        b = np.float32(libm.expf(float(v)))
+        if not np.isfinite(b) or b == 0:
+            assert a == b
+            continue
+        d = abs(int(a.view(np.int32)) - int(b.view(np.int32)))
+        worst = max(worst, d)
+        same += d == 0
+        if d:
+            assert a == _correctly_rounded_expf(v), float(v)
+    assert worst <= 1
+    assert same / len(xs) > 0.998
+    for v in rng.uniform(-104, 89, 300).astype(np.float32):
+        assert np.float32(oracle.rw_expf(float(v))) == _correctly_rounded_expf(v)
+    assert oracle.rw_expf(0.0) == 1.0
+
+
+def test_rw_expf_python_and_c_agree():
+    rng = np.random.default_rng(1)
+    for v in rng.uniform(-100, 88, 3000).astype(np.float32):
+        assert np.float32(oracle.rw_expf(float(v))).view(np.uint32) == \
+            pyref.rw_expf(np.float32(v)).view(np.uint32)
+
+
+def test_metrics_match_definitions():
+    rng = np.random.default_rng(3)
+    s = rng.normal(size=2000).astype(np.float32)
+    s[::10] = s[1::10]  # ties
+    y = (rng.random(2000) < 0.4).astype(np.float32)
+    from sklearn.metrics import roc_auc_score
+    assert abs(oracle.metric("auc", s, y) - roc_auc_score(y, s)) < 1e-12
+    p = np.clip(1 / (1 + np.exp(-s.astype(np.float64))), 1e-7, 1 - 1e-7)
+    ll = -np.mean(y * np.log(p) + (1 - y) * np.log(1 - p))
+    assert abs(oracle.metric("logloss", s, y) - ll) < 1e-12
+    assert abs(oracle.metric("rmse", s, y) - np.sqrt(np.mean((s - y.astype(np.float64)) ** 2))) < 1e-9
+    assert abs(oracle.metric("accuracy", s, y) - np.mean((s > 0) == (y > 0.5))) < 1e-12
+
+
+def test_target_encoding_product_matches_oracle():
+    from rustwood_b200 import encoding, synth
+    x, y, _, _ = synth.c3(5_000, seed=1)
+    cats = list(range(7, 20))
+    for hb in (0, 7):
+        xo, gmo = oracle.target_encode(x, y, cats, 10.0, 5, hb)
+        xp = x.copy()
+        _, gmp = encoding.fit_transform_train(xp, y, cats, 10.0, 5, hb)
+        assert np.float32(gmp) == np.float32(gmo)
+        np.testing.assert_array_equal(xp.view(np.uint32), xo.view(np.uint32))
