@@ -177,6 +177,25 @@ int rw_predict_u8_device(rw_ctx* ctx, const rw_dmodel* dm, const uint8_t* d_bins
 int rw_predict_f32_device(rw_ctx* ctx, const rw_dmodel* dm, const float* d_x, uint64_t n,
                           float* d_out, float* kernel_ms);
 
+/* Booster::predict from host buffers WITHOUT ANY DEVICE ALLOCATION. No counterpart in
+ * the reference: this entry point exists for callers that cannot call cudaMalloc --
+ * e.g. a serving process whose device memory belongs to another allocator (a
+ * framework's caching pool or a fixed reserved budget), or a latency-critical path
+ * where cudaMalloc/cudaFree's implicit device synchronisation would stall other work.
+ * Same margins as rw_predict_f32 (bit-identical). The model, a batch of rows and their
+ * margins are staged through one 16 MiB device array compiled into the library, which
+ * every GPU that loads the library holds until the process exits; rows are processed
+ * in batches that fit beside the model. Limits: the staged model (feat, thr and leafval,
+ * each rounded up to 256 bytes) must fit in 4 MiB, otherwise RW_ERR_ARG is returned
+ * with the size in the message. The first call on each device looks up the array's
+ * device address (cudaGetSymbolAddress, with that device current), so make the first
+ * call on a device before any CUDA stream capture. Every call on a device shares the
+ * array: calls that overlap on the GPU (from other threads or contexts on the same
+ * device) race and must be serialised by the caller. Nothing in the array has to start
+ * at zero: each call overwrites the regions it reads before reading them. */
+int rw_predict_f32_noalloc(rw_ctx* ctx, const rw_model* m, const float* x_rowmajor,
+                           uint64_t n, uint32_t nf, float* out);
+
 /* ---- host helpers kept from the reference host code --------------------------- */
 
 /* compute_boundaries (src/data.rs:86-146): out[nf*(n_bins-1)]. */

@@ -87,6 +87,7 @@ def _load() -> C.CDLL:
         "rw_model_free": (None, [vp]),
         "rw_predict_u8_device": (i32, [vp, vp, vp, u64, u64, vp, P(f32)]),
         "rw_predict_f32_device": (i32, [vp, vp, vp, u64, vp, P(f32)]),
+        "rw_predict_f32_noalloc": (i32, [vp, P(Model), vp, u64, u32, vp]),
         "rw_compute_boundaries": (None, [vp, u64, u32, u32, u64, i32, vp]),
         "rw_base_score": (f32, [vp, u64, i32]),
         "rw_debug_level_hist": (i32, [vp, vp, vp, vp, i32, i32, u32, i32, vp]),
@@ -105,7 +106,7 @@ EXPORTED = [
     "rw_last_error", "rw_ctx_set_timeout", "rw_ctx_stream", "rw_dataset_create", "rw_dataset_create_device",
     "rw_dataset_destroy", "rw_dataset_bins", "rw_fit_dataset", "rw_fit", "rw_predict_f32",
     "rw_predict_u8", "rw_model_upload", "rw_model_free", "rw_predict_u8_device",
-    "rw_predict_f32_device", "rw_compute_boundaries", "rw_base_score", "rw_debug_level_hist",
+    "rw_predict_f32_device", "rw_predict_f32_noalloc", "rw_compute_boundaries", "rw_base_score", "rw_debug_level_hist",
     "rw_debug_expf",
 ]
 
