@@ -454,10 +454,14 @@ typedef struct {
   uint32_t* best_b;
 } split_job;
 
+/* Monotone extension (gpu_kernels.rs:888-896): the child weights use the left/right
+ * (g, h) totals over all nodes. In exact mode the totals are exact integer sums of the
+ * nodes' fixed-point prefixes, converted once; in ref mode f64 sums in node order. */
 static void split_feature(uint32_t f, split_job* J, double* gain, double* pg, double* ph,
                           double* glt, double* hlt, double* grt, double* hrt) {
   uint32_t nb = J->nb, nsplit = nb - 1;
   int mono = (J->monotone && f < J->n_monotone) ? J->monotone[f] : 0;
+  int64_t* mi = mono && J->histi ? (int64_t*)calloc((size_t)nsplit * 4, sizeof(int64_t)) : NULL;
   for (uint32_t b = 0; b < nsplit; b++) {
     gain[b] = 0.0;
     glt[b] = hlt[b] = grt[b] = hrt[b] = 0.0;
@@ -473,12 +477,22 @@ static void split_feature(uint32_t f, split_job* J, double* gain, double* pg, do
         ph[b] = hl;
       }
     } else {
-      int64_t sg = 0, sh = 0;
+      int64_t sg = 0, sh = 0, tg = 0, th = 0;
+      for (uint32_t b = 0; b < nb; b++) {
+        tg += J->histi[(hb + b) * 2];
+        th += J->histi[(hb + b) * 2 + 1];
+      }
       for (uint32_t b = 0; b < nb; b++) {
         sg += J->histi[(hb + b) * 2];
         sh += J->histi[(hb + b) * 2 + 1];
         pg[b] = (double)sg * J->inv_g;
         ph[b] = (double)sh * J->inv_h;
+        if (mi && b < nsplit) {
+          mi[4 * b] += sg;
+          mi[4 * b + 1] += sh;
+          mi[4 * b + 2] += tg - sg;
+          mi[4 * b + 3] += th - sh;
+        }
       }
       gl = pg[nb - 1];
       hl = ph[nb - 1];
@@ -490,13 +504,22 @@ static void split_feature(uint32_t f, split_job* J, double* gain, double* pg, do
       double gr = gt - gl2, hr = ht - hl2;
       double valid = (double)((hl2 >= J->min_child) & (hr >= J->min_child));
       gain[b] += valid * (gl2 * gl2 / (hl2 + J->lambda) + gr * gr / (hr + J->lambda) - parent);
-      if (mono) {
+      if (mono && !mi) {
         glt[b] += gl2;
         hlt[b] += hl2;
         grt[b] += gr;
         hrt[b] += hr;
       }
     }
+  }
+  if (mi) {
+    for (uint32_t b = 0; b < nsplit; b++) {
+      glt[b] = (double)mi[4 * b] * J->inv_g;
+      hlt[b] = (double)mi[4 * b + 1] * J->inv_h;
+      grt[b] = (double)mi[4 * b + 2] * J->inv_g;
+      hrt[b] = (double)mi[4 * b + 3] * J->inv_h;
+    }
+    free(mi);
   }
   int dropped = J->colsample < 1.0f && hash01(f, J->tree_seed ^ 0x5bd1e995u) >= J->colsample;
   for (uint32_t b = 0; b < nsplit; b++) {

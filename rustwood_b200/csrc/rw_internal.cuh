@@ -57,16 +57,13 @@ struct HistLaunch {
   const uint8_t* bins;
   uint64_t ld;
   int packed;
-  const uint16_t* node;
-  const float* g;
-  const float* h;
-  uint64_t n_pad;
+  const int16_t* slot;   // per row: histogram group this level builds into, or -1
+  const int32_t* qg;     // per row: fixed-point g (rw_quantize)
+  const int32_t* qh;     // per row: fixed-point h
+  uint64_t n_pad;        // multiple of kRowAlign
   uint32_t nf, nb;
-  uint32_t groups;   // number of histogram groups written (out has `groups` slots)
-  int odd_only;      // 1: rows with odd node, keyed by node >> 1
-  const uint32_t* maxbits;  // [2]: IEEE bits of max |g|, max h (scales derive from them)
-  const int32_t* e_override;  // nullable [2]: explicit exponents (test hook)
-  long long* out;    // int64 [groups][nf][nb][2], zeroed by the caller
+  uint32_t groups;       // histogram groups written (out has `groups` slots)
+  long long* out;        // int64 [groups][nf][nb][2], zeroed by the caller
 };
 cudaError_t launch_hist(const HistLaunch& a, cudaStream_t s, int* n_launch);
 
@@ -74,6 +71,8 @@ struct SplitLaunch {
   const long long* hb;  // built histogram
   const long long* hp;  // parent level full histogram (mode 1)
   long long* hf;        // this level's full histogram (out)
+  long long* hb_next;   // built-histogram buffer of the next level, zeroed here (nullable)
+  uint64_t hb_next_words;
   uint32_t n_nodes, nf, nb;
   int mode;             // 0: hb holds every node; 1: hb holds odd nodes keyed by parent
   const uint32_t* maxbits;
@@ -98,18 +97,29 @@ struct SplitLaunch {
 };
 cudaError_t launch_split(const SplitLaunch& a, cudaStream_t s);
 
+// Rows are padded to a multiple of kRowAlign so every histogram CTA's row range is a
+// whole number of steps for every lane.
+constexpr uint64_t kRowAlign = 2048;
+
 cudaError_t launch_bin(const float* x_rowmajor, uint64_t n, uint32_t nf, const float* d_cuts,
                        uint32_t n_bins, uint8_t* d_bins, uint64_t ld, cudaStream_t s, int* nl);
 cudaError_t launch_pack4(const uint8_t* d_bins, uint64_t n_pad, uint32_t nf, uint8_t* d_packed,
                          cudaStream_t s, int* nl);
-cudaError_t launch_grad(const float* pred, const float* y, float* g, float* h, uint16_t* node,
-                        uint64_t n, int logistic, uint64_t stride, uint64_t phase,
+cudaError_t launch_grad(const float* pred, const float* y, float* g, float* h, uint64_t n,
+                        uint64_t n_pad, int logistic, uint64_t stride, uint64_t phase,
                         uint64_t row_offset, int compute_max, uint32_t* maxbits,
                         cudaStream_t s, int* nl);
+// Per round: fixed-point q, the excluded flag (bit 15 of node) and level-0 slots; also
+// zeroes the level-0 built histogram (hb0_words int64).
+cudaError_t launch_quant(const float* g, const float* h, const uint32_t* maxbits, uint64_t n_pad,
+                         int32_t* qg, int32_t* qh, uint16_t* node, int16_t* slot,
+                         long long* hb0, uint64_t hb0_words, cudaStream_t s, int* nl);
+// leaf = 2*leaf + (bin > t) keeping the excluded flag; writes the next level's build
+// slot (next_odd_only: odd children keyed by parent), or at the final level updates pred.
 cudaError_t launch_apply(const uint8_t* bins, uint64_t ld, int packed, uint16_t* node,
-                         const uint32_t* split_ft, uint64_t n_pad, int final_level,
-                         const float* leafval, uint32_t leaf_base, float* pred, cudaStream_t s,
-                         int* nl);
+                         int16_t* slot, const uint32_t* split_ft, uint64_t n_pad,
+                         int next_odd_only, int final_level, const float* leafval,
+                         uint32_t leaf_base, float* pred, cudaStream_t s, int* nl);
 cudaError_t launch_fill_f32(float* p, float v, uint64_t n, cudaStream_t s, int* nl);
 
 // GOSS: exact k-th largest |g| by radix selection (4 passes of 8-bit digits).

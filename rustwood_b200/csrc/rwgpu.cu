@@ -285,7 +285,7 @@ static int dataset_build(rw_ctx* ctx, const float* d_x, const float* y, bool y_o
   auto* ds = new rw_dataset();
   ds->ctx = ctx;
   ds->n = n;
-  ds->n_pad = round_up(n, 64);
+  ds->n_pad = round_up(n, kRowAlign);
   ds->n_global = n_global;
   ds->row_offset = row_offset;
   ds->nf = nf;
@@ -434,7 +434,9 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
   // Working buffers live in the dataset's cache: repeated fits allocate nothing.
   WsBuf<float> pred, g, h, d_leafval, d_thr, d_fi_gain, d_fi_count;
   WsBuf<uint16_t> node, d_thr_bin;
-  WsBuf<long long> hb, hf0, hf1;
+  WsBuf<int16_t> slot;
+  WsBuf<int32_t> qg, qh;
+  WsBuf<long long> hb0, hb1, hf0, hf1;
   WsBuf<uint32_t> d_feat, maxbits, best_bin, counter, split_ft;
   WsBuf<double> best_gain;
   WsBuf<int32_t> d_mono;
@@ -444,7 +446,11 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
   RW_CU(ctx, g.get(ds, "g", n_pad));
   RW_CU(ctx, h.get(ds, "h", n_pad));
   RW_CU(ctx, node.get(ds, "node", n_pad));
-  RW_CU(ctx, hb.get(ds, "hb", hb_groups * cell));
+  RW_CU(ctx, slot.get(ds, "slot", n_pad));
+  RW_CU(ctx, qg.get(ds, "qg", n_pad));
+  RW_CU(ctx, qh.get(ds, "qh", n_pad));
+  RW_CU(ctx, hb0.get(ds, "hb0", hb_groups * cell));
+  RW_CU(ctx, hb1.get(ds, "hb1", hb_groups * cell));
   RW_CU(ctx, hf0.get(ds, "hf0", hf_nodes * cell));
   RW_CU(ctx, hf1.get(ds, "hf1", hf_nodes * cell));
   RW_CU(ctx, d_feat.get(ds, "feat", (size_t)T * D));
@@ -461,6 +467,7 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
   RW_CU(ctx, cudaMemsetAsync(g.p, 0, n_pad * 4, s));
   RW_CU(ctx, cudaMemsetAsync(h.p, 0, n_pad * 4, s));
   RW_CU(ctx, cudaMemsetAsync(node.p, 0, n_pad * 2, s));
+  RW_CU(ctx, cudaMemsetAsync(slot.p, 0xff, n_pad * 2, s));
   RW_CU(ctx, cudaMemsetAsync(d_fi_gain.p, 0, nf * 4, s));
   RW_CU(ctx, cudaMemsetAsync(d_fi_count.p, 0, nf * 4, s));
   RW_CU(ctx, cudaMemsetAsync(maxbits.p, 0, maxbits.n * 4, s));
@@ -517,7 +524,7 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
   for (uint32_t t = 0; t < T; t++) {
     uint32_t* mb = maxbits.p + 2 * (size_t)t;
     if (goss) {
-      RW_CU(ctx, launch_grad(pred.p, ds->d_y, g.p, h.p, node.p, n, logistic, 1, 0, ds->row_offset,
+      RW_CU(ctx, launch_grad(pred.p, ds->d_y, g.p, h.p, n, n_pad, logistic, 1, 0, ds->row_offset,
                              0, mb, s, &nl));
       RW_CU(ctx, launch_goss_init(gst, goss_k, s, &nl));
       for (int pass = 0; pass < 4; pass++) {
@@ -529,11 +536,12 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
       RW_CU(ctx, launch_goss_apply(g.p, h.p, n, ds->row_offset, gst, keep_prob, goss_fact,
                                    (uint64_t)t, mb, s, &nl));
     } else {
-      RW_CU(ctx, launch_grad(pred.p, ds->d_y, g.p, h.p, node.p, n, logistic, stride,
+      RW_CU(ctx, launch_grad(pred.p, ds->d_y, g.p, h.p, n, n_pad, logistic, stride,
                              stride > 1 ? (uint64_t)t % stride : 0, ds->row_offset, 1, mb, s,
                              &nl));
     }
     if (ctx->comm) RW_NC(ctx, ncclAllReduce(mb, mb, 2, ncclUint32, ncclMax, ctx->comm, s));
+    RW_CU(ctx, launch_quant(g.p, h.p, mb, n_pad, qg.p, qh.p, node.p, slot.p, hb0.p, cell, s, &nl));
     pt.mark(RW_CAT_GRADIENTS);
 
     const uint32_t tree_seed = t * 2654435761u + 0x455A4B41u;  // src/booster.rs:351
@@ -541,36 +549,36 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
       const uint32_t n_nodes = 1u << d;
       const int mode = (d == 0 || !subtract) ? 0 : 1;
       const uint32_t groups = mode == 0 ? n_nodes : n_nodes / 2;
-      RW_CU(ctx, cudaMemsetAsync(hb.p, 0, (size_t)groups * cell * 8, s));
-      pt.mark(RW_CAT_ZERO_HIST);
+      long long* hb = (d & 1) ? hb1.p : hb0.p;
+      long long* hb_next = (d & 1) ? hb0.p : hb1.p;
+      const uint32_t groups_next =
+          d + 1 < D ? (subtract ? (1u << d) : (1u << (d + 1))) : 0u;
       HistLaunch hl;
       hl.bins = ds->d_bins;
       hl.ld = ds->ld;
       hl.packed = ds->packed;
-      hl.node = node.p;
-      hl.g = g.p;
-      hl.h = h.p;
+      hl.slot = slot.p;
+      hl.qg = qg.p;
+      hl.qh = qh.p;
       hl.n_pad = n_pad;
       hl.nf = nf;
       hl.nb = nb;
       hl.groups = groups;
-      hl.odd_only = mode;
-      hl.maxbits = mb;
-      hl.e_override = nullptr;
-      hl.out = hb.p;
+      hl.out = hb;
       RW_CU(ctx, launch_hist(hl, s, &nl));
       hist_launches++;
       alg_bytes += (double)n * nf * bin_bytes + 12.0 * (double)n + 8.0 * nf * nb * groups;
       pt.mark(RW_CAT_BUILD_HIST);
       if (ctx->comm) {
-        RW_NC(ctx, ncclAllReduce(hb.p, hb.p, (size_t)groups * cell, ncclInt64, ncclSum, ctx->comm,
-                                 s));
+        RW_NC(ctx, ncclAllReduce(hb, hb, (size_t)groups * cell, ncclInt64, ncclSum, ctx->comm, s));
         pt.mark(RW_CAT_ALLREDUCE);
       }
       SplitLaunch sl;
-      sl.hb = hb.p;
+      sl.hb = hb;
       sl.hp = (d & 1) ? hf0.p : hf1.p;
       sl.hf = (d & 1) ? hf1.p : hf0.p;
+      sl.hb_next = groups_next ? hb_next : nullptr;
+      sl.hb_next_words = (uint64_t)groups_next * cell;
       sl.n_nodes = n_nodes;
       sl.nf = nf;
       sl.nb = nb;
@@ -599,8 +607,8 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
       RW_CU(ctx, launch_split(sl, s));
       nl++;
       pt.mark(RW_CAT_SPLIT);
-      RW_CU(ctx, launch_apply(ds->d_bins, ds->ld, ds->packed, node.p, split_ft.p, n_pad,
-                              d == D - 1, d_leafval.p, t * NL, pred.p, s, &nl));
+      RW_CU(ctx, launch_apply(ds->d_bins, ds->ld, ds->packed, node.p, slot.p, split_ft.p, n_pad,
+                              subtract ? 1 : 0, d == D - 1, d_leafval.p, t * NL, pred.p, s, &nl));
       pt.mark(d == D - 1 ? RW_CAT_UPDATE_PRED : RW_CAT_APPLY);
     }
   }
@@ -884,45 +892,42 @@ extern "C" int rw_debug_level_hist(rw_dataset* ds, const int32_t* node, const fl
   rw_ctx* ctx = ds->ctx;
   RW_CU(ctx, cudaSetDevice(ctx->device));
   const uint64_t n = ds->n, n_pad = ds->n_pad;
-  std::vector<uint16_t> nd(n_pad, 0);
-  std::vector<float> gg(n_pad, 0.f), hh(n_pad, 0.f);
+  std::vector<int16_t> sl(n_pad, -1);
+  std::vector<int32_t> qgv(n_pad, 0), qhv(n_pad, 0);
+  const float sg = rw_pow2f(e_g), sh = rw_pow2f(e_h);
   for (uint64_t i = 0; i < n; i++) {
     if (node[i] < 0) continue;
-    if (node[i] > 0xffff) return fail(ctx, RW_ERR_ARG, "node index above 65535");
-    nd[i] = (uint16_t)node[i];
-    gg[i] = g[i];
-    hh[i] = h[i];
+    if (node[i] > 0x7fff) return fail(ctx, RW_ERR_ARG, "node index above 32767");
+    const int32_t a = rw_quantize(g[i], sg), b = rw_quantize(h[i], sh);
+    if ((a | b) == 0) continue;
+    qgv[i] = a;
+    qhv[i] = b;
+    if (odd_only) sl[i] = (node[i] & 1) ? (int16_t)(node[i] >> 1) : (int16_t)-1;
+    else sl[i] = (int16_t)node[i];
   }
   const size_t words = (size_t)groups * ds->nf * ds->n_bins * 2;
-  DBuf<uint16_t> dn;
-  DBuf<float> dg, dh;
+  DBuf<int16_t> dn;
+  DBuf<int32_t> dg, dh;
   DBuf<long long> dout;
-  DBuf<int32_t> de;
   RW_CU(ctx, dn.alloc(n_pad));
   RW_CU(ctx, dg.alloc(n_pad));
   RW_CU(ctx, dh.alloc(n_pad));
   RW_CU(ctx, dout.alloc(words));
-  RW_CU(ctx, de.alloc(2));
-  const int32_t ev[2] = {e_g, e_h};
-  RW_CU(ctx, cudaMemcpy(dn.p, nd.data(), n_pad * 2, cudaMemcpyHostToDevice));
-  RW_CU(ctx, cudaMemcpy(dg.p, gg.data(), n_pad * 4, cudaMemcpyHostToDevice));
-  RW_CU(ctx, cudaMemcpy(dh.p, hh.data(), n_pad * 4, cudaMemcpyHostToDevice));
-  RW_CU(ctx, cudaMemcpy(de.p, ev, 8, cudaMemcpyHostToDevice));
+  RW_CU(ctx, cudaMemcpy(dn.p, sl.data(), n_pad * 2, cudaMemcpyHostToDevice));
+  RW_CU(ctx, cudaMemcpy(dg.p, qgv.data(), n_pad * 4, cudaMemcpyHostToDevice));
+  RW_CU(ctx, cudaMemcpy(dh.p, qhv.data(), n_pad * 4, cudaMemcpyHostToDevice));
   RW_CU(ctx, cudaMemset(dout.p, 0, words * 8));
   HistLaunch hl;
   hl.bins = ds->d_bins;
   hl.ld = ds->ld;
   hl.packed = ds->packed;
-  hl.node = dn.p;
-  hl.g = dg.p;
-  hl.h = dh.p;
+  hl.slot = dn.p;
+  hl.qg = dg.p;
+  hl.qh = dh.p;
   hl.n_pad = n_pad;
   hl.nf = ds->nf;
   hl.nb = ds->n_bins;
   hl.groups = groups;
-  hl.odd_only = odd_only;
-  hl.maxbits = nullptr;
-  hl.e_override = de.p;
   hl.out = dout.p;
   int nl = 0;
   RW_CU(ctx, launch_hist(hl, ctx->stream, &nl));

@@ -2,13 +2,15 @@
 //
 // Per boosting round (src/booster.rs:349-501 is the reference's sequence):
 //   k_grad / GOSS           gradients, row sampling, per-round max |g| and max h
+//   [ncclAllReduce max]     multi-GPU: global maxima (the fixed-point scales)
+//   k_quant                 per-row fixed-point q(g), q(h), excluded flag, level-0 slots
 //   per level d:
 //     k_hist                exact fixed-point histogram of the built nodes
 //     [ncclAllReduce]       multi-GPU: sum of the built histograms (int64, exact)
 //     k_split               derive sibling nodes, f64 gain scan, argmax, model write,
 //                           leaf values at the last level (no separate leaf pass)
-//     k_apply               leaf = 2*leaf + (bin > t); at the last level also
-//                           pred += leafval[leaf]
+//     k_apply               leaf = 2*leaf + (bin > t) and the next level's build slot;
+//                           at the last level pred += leafval[leaf]
 //
 // Exactness: histogram cells are int64 sums of per-row fixed-point values
 // q = round(x * 2^e) (rw_expf.h). Shared memory holds the low 32 bits of each cell as
@@ -17,6 +19,7 @@
 // The result equals the int64 sum of q over the contributing rows regardless of
 // scheduling, so histograms, splits and leaf values are bit-identical run to run and
 // at every GPU count.
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -31,38 +34,46 @@ constexpr int kHistThreads = 512;
 constexpr uint32_t kBias = 0x80000000u;
 constexpr int kHistSmemBudget = 112 * 1024;  // two CTAs per SM
 constexpr int kTargetCtas = 2 * 148;
+constexpr int kMaxCluster = 8;
 
-__device__ __forceinline__ void exact_add(uint32_t* lo, uint32_t cell, int32_t q,
-                                          long long* gcell) {
-  const uint32_t uq = (uint32_t)q;
-  const uint32_t old = atomicAdd(&lo[cell], uq);
-  const int delta = (q < 0 ? -1 : 0) + ((uint32_t)(old + uq) < old ? 1 : 0);
+namespace cg = cooperative_groups;
+
+struct HistArgs {
+  const uint8_t* bins;
+  uint64_t ld;
+  const int16_t* slot;
+  const int32_t* qg;
+  const int32_t* qh;
+  uint64_t n_pad;
+  uint32_t nf, nb;
+  uint32_t gchunk;  // groups per CTA (blockIdx.z selects the chunk)
+  long long* out;
+  uint64_t rows_per_cta;
+};
+
+// Adds ±2^32 to the global cell when the 32-bit shared accumulator wrapped in the add
+// of q that returned `old` (the shared word holds the cell's low 32 bits + 2^31).
+__device__ __forceinline__ void carry_out(uint32_t old, int32_t q, long long* gcell) {
+  const uint32_t nw = old + (uint32_t)q;
+  const int delta = (nw < old ? 1 : 0) - (q < 0 ? 1 : 0);
   if (delta != 0)
     atomicAdd(reinterpret_cast<unsigned long long*>(gcell),
               (unsigned long long)((long long)delta * 4294967296LL));
 }
 
-struct HistArgs {
-  const uint8_t* bins;
-  uint64_t ld;
-  const uint16_t* node;
-  const float* g;
-  const float* h;
-  uint64_t n_pad;
-  uint32_t nf, nb;
-  uint32_t gchunk;  // groups per CTA (blockIdx.z selects the chunk)
-  uint32_t groups;
-  int odd_only;
-  const uint32_t* maxbits;
-  const int32_t* e_override;
-  long long* out;
-  uint64_t rows_per_cta;
-};
+// A wrap is only possible when the returned low word is within 2^26 (>= |q|) of the
+// 32-bit boundary, i.e. old + 2^26 (mod 2^32) < 2^27.
+__device__ __forceinline__ bool near_edge(uint32_t og, uint32_t oh) {
+  return min(og + (1u << 26), oh + (1u << 26)) < (1u << 27);
+}
 
-// One CTA: feature tile [blockIdx.y*FT, +FT) x group chunk x row range.
-// Lane (k, j): feature j of the tile for row slot k; each thread covers 4 consecutive
-// rows per step (one u32 of u8 bins, or one u16 of 4-bit bins). Shared cells are laid
-// out [group][bin][FT] so the FT lanes of one row hit FT distinct banks.
+// One CTA: feature tile [blockIdx.y*FT, +FT) x group chunk x row range, in a cluster of
+// CTAs along the row ranges. Lane (k, j) handles feature j of the tile for row slot k;
+// each thread covers 4 consecutive rows per step (one u32 of u8 bins, or one u16 of
+// 4-bit bins). Shared cells are laid out [group][bin][FT]: the FT lanes of one row hit
+// FT distinct banks. After the rows, the cluster's CTAs sum their shared histograms
+// through distributed shared memory, each CTA flushing a slice to the global int64
+// histogram, so a cell costs one global atomic per cluster rather than per CTA.
 template <int FT, bool PACKED>
 __global__ void __launch_bounds__(kHistThreads, 2) k_hist(HistArgs a) {
   extern __shared__ uint32_t smem[];
@@ -80,16 +91,7 @@ __global__ void __launch_bounds__(kHistThreads, 2) k_hist(HistArgs a) {
   const uint32_t f0 = blockIdx.y * FT;
   const uint32_t f = f0 + j;
   const bool fvalid = f < a.nf;
-  const uint32_t g0 = blockIdx.z * a.gchunk;
-  int eg, eh;
-  if (a.e_override) {
-    eg = a.e_override[0];
-    eh = a.e_override[1];
-  } else {
-    eg = rw_qscale_exp(a.maxbits[0]);
-    eh = rw_qscale_exp(a.maxbits[1]);
-  }
-  const float sg = rw_pow2f(eg), sh = rw_pow2f(eh);
+  const int g0 = (int)(blockIdx.z * a.gchunk);
   const uint8_t* col = a.bins + (size_t)(fvalid ? f : 0) * a.ld;
   long long* outf = a.out + (size_t)(fvalid ? f : 0) * nb * 2;
   const size_t gstride = (size_t)a.nf * nb * 2;
@@ -99,9 +101,9 @@ __global__ void __launch_bounds__(kHistThreads, 2) k_hist(HistArgs a) {
   if (r_end > a.n_pad) r_end = a.n_pad;
 
   for (uint64_t rb = r_begin + (uint64_t)(warp * RW + k) * 4; rb < r_end; rb += kStep) {
-    const uint2 nd2 = *reinterpret_cast<const uint2*>(a.node + rb);
-    const float4 g4 = *reinterpret_cast<const float4*>(a.g + rb);
-    const float4 h4 = *reinterpret_cast<const float4*>(a.h + rb);
+    const uint2 sl2 = *reinterpret_cast<const uint2*>(a.slot + rb);
+    const int4 qg4 = *reinterpret_cast<const int4*>(a.qg + rb);
+    const int4 qh4 = *reinterpret_cast<const int4*>(a.qh + rb);
     uint32_t b4;
     if (PACKED) {
       const uint32_t p = *reinterpret_cast<const uint16_t*>(col + (rb >> 1));
@@ -109,80 +111,106 @@ __global__ void __launch_bounds__(kHistThreads, 2) k_hist(HistArgs a) {
     } else {
       b4 = *reinterpret_cast<const uint32_t*>(col + rb);
     }
-    const uint32_t nds[4] = {nd2.x & 0xffffu, nd2.x >> 16, nd2.y & 0xffffu, nd2.y >> 16};
-    const float gs[4] = {g4.x, g4.y, g4.z, g4.w};
-    const float hs[4] = {h4.x, h4.y, h4.z, h4.w};
+    const int sl[4] = {(int)(int16_t)(sl2.x & 0xffffu), (int)(int16_t)(sl2.x >> 16),
+                       (int)(int16_t)(sl2.y & 0xffffu), (int)(int16_t)(sl2.y >> 16)};
+    const int32_t qg[4] = {qg4.x, qg4.y, qg4.z, qg4.w};
+    const int32_t qh[4] = {qh4.x, qh4.y, qh4.z, qh4.w};
+    uint32_t og[4], oh[4], cell[4];
+    bool act[4];
 #pragma unroll
     for (int s = 0; s < 4; s++) {
-      const int32_t qg = rw_quantize(gs[s], sg);
-      const int32_t qh = rw_quantize(hs[s], sh);
-      uint32_t nd = nds[s];
-      bool take = fvalid && ((qg | qh) != 0);
-      if (a.odd_only) {
-        take = take && (nd & 1u);
-        nd >>= 1;
+      const uint32_t grp = (uint32_t)(sl[s] - g0);
+      act[s] = fvalid && grp < G;
+      cell[s] = (grp * nb + ((b4 >> (8 * s)) & 0xffu)) * FT + j;
+      if (act[s]) {
+        og[s] = atomicAdd(&lo_g[cell[s]], (uint32_t)qg[s]);
+        oh[s] = atomicAdd(&lo_h[cell[s]], (uint32_t)qh[s]);
       }
-      const uint32_t grp = nd - g0;
-      take = take && grp < G;
-      if (take) {
+    }
+#pragma unroll
+    for (int s = 0; s < 4; s++) {
+      if (act[s] && near_edge(og[s], oh[s])) {
         const uint32_t bin = (b4 >> (8 * s)) & 0xffu;
-        const uint32_t cell = (grp * nb + bin) * FT + j;
-        long long* gc = outf + (size_t)(g0 + grp) * gstride + (size_t)bin * 2;
-        exact_add(lo_g, cell, qg, gc);
-        exact_add(lo_h, cell, qh, gc + 1);
+        long long* gc = outf + (size_t)sl[s] * gstride + (size_t)bin * 2;
+        carry_out(og[s], qg[s], gc);
+        carry_out(oh[s], qh[s], gc + 1);
       }
     }
   }
-  __syncthreads();
-  for (uint32_t c = threadIdx.x; c < cells; c += kHistThreads) {
+
+  cg::cluster_group cluster = cg::this_cluster();
+  cluster.sync();
+  const uint32_t cn = cluster.num_blocks(), cr = cluster.block_rank();
+  const uint32_t words = 2 * cells;
+  const uint32_t per = (words + cn - 1) / cn;
+  const uint32_t w_begin = cr * per, w_end = min(words, w_begin + per);
+  for (uint32_t w = w_begin + threadIdx.x; w < w_end; w += kHistThreads) {
+    long long v = 0;
+    for (uint32_t r = 0; r < cn; r++) {
+      const uint32_t* remote = cluster.map_shared_rank(smem, (int)r);
+      v += (long long)remote[w] - (long long)kBias;
+    }
+    if (v == 0) continue;
+    const uint32_t c = w < cells ? w : w - cells;
     const uint32_t jj = c % FT, rest = c / FT, bin = rest % nb, grp = rest / nb;
     const uint32_t ff = f0 + jj;
     if (ff >= a.nf) continue;
-    long long* gc = a.out + (size_t)(g0 + grp) * gstride + ((size_t)ff * nb + bin) * 2;
-    const long long vg = (long long)lo_g[c] - (long long)kBias;
-    const long long vh = (long long)lo_h[c] - (long long)kBias;
-    if (vg) atomicAdd(reinterpret_cast<unsigned long long*>(gc), (unsigned long long)vg);
-    if (vh) atomicAdd(reinterpret_cast<unsigned long long*>(gc + 1), (unsigned long long)vh);
+    long long* gc = a.out + (size_t)(g0 + grp) * gstride + ((size_t)ff * nb + bin) * 2 +
+                    (w < cells ? 0 : 1);
+    atomicAdd(reinterpret_cast<unsigned long long*>(gc), (unsigned long long)v);
   }
+  cluster.sync();  // keep this CTA's shared memory alive until every reader is done
 }
 
 template <int FT, bool PACKED>
-cudaError_t launch_hist_t(const HistArgs& args, dim3 grid, size_t smem, cudaStream_t s) {
+cudaError_t launch_hist_t(const HistArgs& args, dim3 grid, int cluster, size_t smem,
+                          cudaStream_t s) {
   cudaError_t e = cudaFuncSetAttribute(k_hist<FT, PACKED>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  k_hist<FT, PACKED><<<grid, kHistThreads, smem, s>>>(args);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kHistThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_hist<FT, PACKED>, args);
 }
 
 template <bool PACKED>
-cudaError_t launch_hist_ft(int ft, const HistArgs& args, dim3 grid, size_t smem,
+cudaError_t launch_hist_ft(int ft, const HistArgs& args, dim3 grid, int cluster, size_t smem,
                            cudaStream_t s) {
   switch (ft) {
-    case 32: return launch_hist_t<32, PACKED>(args, grid, smem, s);
-    case 16: return launch_hist_t<16, PACKED>(args, grid, smem, s);
-    case 8: return launch_hist_t<8, PACKED>(args, grid, smem, s);
-    case 4: return launch_hist_t<4, PACKED>(args, grid, smem, s);
-    case 2: return launch_hist_t<2, PACKED>(args, grid, smem, s);
-    default: return launch_hist_t<1, PACKED>(args, grid, smem, s);
+    case 32: return launch_hist_t<32, PACKED>(args, grid, cluster, smem, s);
+    case 16: return launch_hist_t<16, PACKED>(args, grid, cluster, smem, s);
+    case 8: return launch_hist_t<8, PACKED>(args, grid, cluster, smem, s);
+    case 4: return launch_hist_t<4, PACKED>(args, grid, cluster, smem, s);
+    case 2: return launch_hist_t<2, PACKED>(args, grid, cluster, smem, s);
+    default: return launch_hist_t<1, PACKED>(args, grid, cluster, smem, s);
   }
 }
 
 // --------------------------------------------------------------------------------
-// Split scan: one CTA per feature; warps take nodes 8 at a time, lanes take 8 bins.
+// Split scan: one CTA per feature; its 32 warps take 32 nodes at a time (one node per
+// warp), lanes take 8 consecutive bins. Per-node gain terms go to shared memory and
+// each bin's thread adds them in node order, as src/cpu.rs:242-259 does.
 
-constexpr int kSplitThreads = 256;
+constexpr int kSplitThreads = 1024;
 constexpr int kSplitWarps = kSplitThreads / 32;
 
 struct SplitSmem {
   double term[kSplitWarps][256];
-  double gl[kSplitWarps][256];
-  double hl[kSplitWarps][256];
-  double gt[kSplitWarps];
-  double ht[kSplitWarps];
+  long long mono[4][256];  // exact left/right (g, h) totals over nodes (monotone only)
   double red_g[kSplitWarps];
   uint32_t red_i[kSplitWarps];
   int last;
+  uint32_t s_f, s_b;
 };
 
 __device__ __forceinline__ long long shfl_up_ll(long long v, int d) {
@@ -206,6 +234,7 @@ __device__ __forceinline__ void argmax_merge(double& g, uint32_t& i, double g2, 
   }
 }
 
+// Block-wide argmax; the result is valid in thread 0.
 __device__ void block_argmax(double& g, uint32_t& i, SplitSmem& sm) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
@@ -243,7 +272,17 @@ __global__ void __launch_bounds__(kSplitThreads) k_split(SplitLaunch a) {
   const double lambda = a.lambda, mc = a.min_child;
   const int mono = a.monotone ? a.monotone[f] : 0;
 
-  double gain = 0.0, glt = 0.0, hlt = 0.0, grt = 0.0, hrt = 0.0;
+  // The next level's built-histogram buffer is zeroed here (this CTA's slice).
+  if (a.hb_next) {
+    const uint64_t per = (a.hb_next_words + nf - 1) / nf;
+    const uint64_t w0 = (uint64_t)f * per;
+    const uint64_t w1 = w0 + per < a.hb_next_words ? w0 + per : a.hb_next_words;
+    for (uint64_t w = w0 + threadIdx.x; w < w1; w += kSplitThreads) a.hb_next[w] = 0;
+  }
+  if (mono)
+    for (int i = threadIdx.x; i < 4 * 256; i += kSplitThreads) (&sm.mono[0][0])[i] = 0;
+
+  double gain = 0.0;
   const uint32_t b_self = threadIdx.x;
 
   for (uint32_t c = 0; c < a.n_nodes; c += kSplitWarps) {
@@ -301,32 +340,27 @@ __global__ void __launch_bounds__(kSplitThreads) k_split(SplitLaunch a) {
       for (int i = 0; i < 8; i++) {
         const uint32_t b = lane * 8 + i;
         if (b < nsplit) {
-          const double gl = (double)(vg[i] + eg) * inv_g;
-          const double hl = (double)(vh[i] + eh) * inv_h;
+          const long long pgi = vg[i] + eg, phi = vh[i] + eh;
+          const double gl = (double)pgi * inv_g;
+          const double hl = (double)phi * inv_h;
           const double gr = gt - gl, hr = ht - hl;
           const double valid = (double)((hl >= mc) & (hr >= mc));
           sm.term[warp][b] = valid * (gl * gl / (hl + lambda) + gr * gr / (hr + lambda) - parent);
-          sm.gl[warp][b] = gl;
-          sm.hl[warp][b] = hl;
+          if (mono) {
+            atomicAdd(reinterpret_cast<unsigned long long*>(&sm.mono[0][b]), (unsigned long long)pgi);
+            atomicAdd(reinterpret_cast<unsigned long long*>(&sm.mono[1][b]), (unsigned long long)phi);
+            atomicAdd(reinterpret_cast<unsigned long long*>(&sm.mono[2][b]),
+                      (unsigned long long)(totg - pgi));
+            atomicAdd(reinterpret_cast<unsigned long long*>(&sm.mono[3][b]),
+                      (unsigned long long)(toth - phi));
+          }
         }
-      }
-      if (lane == 0) {
-        sm.gt[warp] = gt;
-        sm.ht[warp] = ht;
       }
     }
     __syncthreads();
     if (b_self < nsplit) {
       const uint32_t cnt = (a.n_nodes - c) < (uint32_t)kSplitWarps ? (a.n_nodes - c) : kSplitWarps;
-      for (uint32_t w = 0; w < cnt; w++) {
-        gain += sm.term[w][b_self];
-        if (mono) {
-          glt += sm.gl[w][b_self];
-          hlt += sm.hl[w][b_self];
-          grt += sm.gt[w] - sm.gl[w][b_self];
-          hrt += sm.ht[w] - sm.hl[w][b_self];
-        }
-      }
+      for (uint32_t w = 0; w < cnt; w++) gain += sm.term[w][b_self];
     }
     __syncthreads();
   }
@@ -340,6 +374,10 @@ __global__ void __launch_bounds__(kSplitThreads) k_split(SplitLaunch a) {
     key = gain;
     if (dropped) key = -1e30;
     else if (mono) {
+      const double glt = (double)sm.mono[0][b_self] * inv_g;
+      const double hlt = (double)sm.mono[1][b_self] * inv_h;
+      const double grt = (double)sm.mono[2][b_self] * inv_g;
+      const double hrt = (double)sm.mono[3][b_self] * inv_h;
       const double wl = -glt / (hlt + lambda);
       const double wr = -grt / (hrt + lambda);
       if ((mono > 0 && wl > wr) || (mono < 0 && wl < wr)) key = -1e30;
@@ -365,12 +403,11 @@ __global__ void __launch_bounds__(kSplitThreads) k_split(SplitLaunch a) {
   for (uint32_t ff = threadIdx.x; ff < nf; ff += kSplitThreads)
     argmax_merge(bk, bf, __ldcg(a.best_gain + ff), ff);
   block_argmax(bk, bf, sm);
-  __shared__ uint32_t s_f, s_b;
   if (threadIdx.x == 0) {
     if (bk == -RW_INF) bf = 0;
     const uint32_t bb = __ldcg(a.best_bin + bf);
-    s_f = bf;
-    s_b = bb;
+    sm.s_f = bf;
+    sm.s_b = bb;
     a.feat[a.slot] = bf;
     a.thr[a.slot] = a.cuts[(size_t)bf * nsplit + bb];
     if (a.thr_bin) a.thr_bin[a.slot] = (uint16_t)bb;
@@ -382,7 +419,7 @@ __global__ void __launch_bounds__(kSplitThreads) k_split(SplitLaunch a) {
   }
   __syncthreads();
   if (a.last_level) {
-    const uint32_t fs = s_f, bs = s_b;
+    const uint32_t fs = sm.s_f, bs = sm.s_b;
     for (uint32_t nd = threadIdx.x; nd < a.n_nodes; nd += kSplitThreads) {
       long long lg = 0, lh = 0, tg = 0, th = 0;
       const long long* p = a.hf + (((size_t)nd * nf + fs) * nb) * 2;
@@ -474,15 +511,13 @@ __device__ void block_max2_atomic(uint32_t mg, uint32_t mh, uint32_t* maxbits) {
   }
 }
 
-// Gradients (src/cpu.rs:181-193), stride row sampling (src/cpu.rs:172-176, 202-204),
-// node reset, and the round's maxima over the sampled rows. Unsampled rows get
-// g = h = 0, which removes them from every histogram and leaf sum.
-// Padded rows (n <= i < n_pad) get g = h = 0 and node 0 every round, which keeps them
-// out of every sum and keeps their leaf index below 2^depth.
+// Gradients (src/cpu.rs:181-193), stride row sampling (src/cpu.rs:172-176, 202-204)
+// and the round's maxima over the sampled rows. Unsampled and padded rows
+// (n <= i < n_pad) get g = h = 0, which removes them from every histogram and leaf sum.
 __global__ void k_grad(const float* __restrict__ pred, const float* __restrict__ y,
-                       float* __restrict__ g, float* __restrict__ h, uint16_t* __restrict__ node,
-                       uint64_t n, uint64_t n_pad, int logistic, uint64_t stride, uint64_t phase,
-                       uint64_t row_offset, int compute_max, uint32_t* maxbits) {
+                       float* __restrict__ g, float* __restrict__ h, uint64_t n, uint64_t n_pad,
+                       int logistic, uint64_t stride, uint64_t phase, uint64_t row_offset,
+                       int compute_max, uint32_t* maxbits) {
   uint32_t mg = 0, mh = 0;
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_pad;
        i += (uint64_t)gridDim.x * blockDim.x) {
@@ -501,17 +536,46 @@ __global__ void k_grad(const float* __restrict__ pred, const float* __restrict__
     }
     g[i] = gv;
     h[i] = hv;
-    node[i] = 0;
     mg = max(mg, f32_bits_abs(gv));
     mh = max(mh, f32_bits_abs(hv));
   }
   if (compute_max) block_max2_atomic(mg, mh, maxbits);
 }
 
+// Per round: q = round(x * 2^e) for g and h (scales from the final maxima), the row's
+// excluded flag (node bit 15; a row whose g and h both quantise to 0 adds nothing to
+// any sum), node reset and the level-0 build slot. Also zeroes the level-0 histogram.
+constexpr uint16_t kExcluded = 0x8000;
+
+__global__ void k_quant(const float* __restrict__ g, const float* __restrict__ h,
+                        const uint32_t* __restrict__ maxbits, uint64_t n_pad,
+                        int32_t* __restrict__ qg, int32_t* __restrict__ qh,
+                        uint16_t* __restrict__ node, int16_t* __restrict__ slot,
+                        long long* __restrict__ hb0, uint64_t hb0_words) {
+  const float sg = rw_pow2f(rw_qscale_exp(maxbits[0]));
+  const float sh = rw_pow2f(rw_qscale_exp(maxbits[1]));
+  const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const uint64_t nthr = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t w = tid; w < hb0_words; w += nthr) hb0[w] = 0;
+  for (uint64_t i = tid; i < n_pad; i += nthr) {
+    const int32_t a = rw_quantize(g[i], sg), b = rw_quantize(h[i], sh);
+    const bool excl = (a | b) == 0;
+    qg[i] = a;
+    qh[i] = b;
+    node[i] = excl ? kExcluded : 0;
+    slot[i] = excl ? -1 : 0;
+  }
+}
+
+// leaf = 2*leaf + (bin[f*] > t*) (src/cpu.rs:278-281) for 4 rows per thread, keeping the
+// excluded flag; then either the next level's build slot (odd children keyed by the
+// parent when subtracting, else the node itself; -1 when excluded or not built), or, at
+// the last level, pred += leafval[leaf] (src/cpu.rs:319-320).
 __global__ void k_apply(const uint8_t* __restrict__ bins, uint64_t ld, int packed,
-                        uint16_t* __restrict__ node, const uint32_t* __restrict__ split_ft,
-                        uint64_t n4, int final_level, const float* __restrict__ leafval,
-                        uint32_t leaf_base, float* __restrict__ pred) {
+                        uint16_t* __restrict__ node, int16_t* __restrict__ slot,
+                        const uint32_t* __restrict__ split_ft, uint64_t n4, int next_odd_only,
+                        int final_level, const float* __restrict__ leafval, uint32_t leaf_base,
+                        float* __restrict__ pred) {
   const uint32_t f = split_ft[0], t = split_ft[1];
   const uint8_t* col = bins + (size_t)f * ld;
   for (uint64_t q = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; q < n4;
@@ -526,18 +590,31 @@ __global__ void k_apply(const uint8_t* __restrict__ bins, uint64_t ld, int packe
     }
     uint2 nd2 = *reinterpret_cast<const uint2*>(node + r);
     uint32_t nds[4] = {nd2.x & 0xffffu, nd2.x >> 16, nd2.y & 0xffffu, nd2.y >> 16};
+    int sl[4];
 #pragma unroll
-    for (int s = 0; s < 4; s++) nds[s] = nds[s] * 2u + (((b4 >> (8 * s)) & 0xffu) > t ? 1u : 0u);
+    for (int s = 0; s < 4; s++) {
+      const uint32_t ex = nds[s] & kExcluded;
+      const uint32_t leaf = (nds[s] & 0x7fffu) * 2u + (((b4 >> (8 * s)) & 0xffu) > t ? 1u : 0u);
+      nds[s] = ex | leaf;
+      if (ex) sl[s] = -1;
+      else if (next_odd_only) sl[s] = (leaf & 1u) ? (int)(leaf >> 1) : -1;
+      else sl[s] = (int)leaf;
+    }
     nd2.x = (nds[0] & 0xffffu) | (nds[1] << 16);
     nd2.y = (nds[2] & 0xffffu) | (nds[3] << 16);
     *reinterpret_cast<uint2*>(node + r) = nd2;
     if (final_level) {
       float4 p4 = *reinterpret_cast<const float4*>(pred + r);
-      p4.x += leafval[leaf_base + nds[0]];
-      p4.y += leafval[leaf_base + nds[1]];
-      p4.z += leafval[leaf_base + nds[2]];
-      p4.w += leafval[leaf_base + nds[3]];
+      p4.x += leafval[leaf_base + (nds[0] & 0x7fffu)];
+      p4.y += leafval[leaf_base + (nds[1] & 0x7fffu)];
+      p4.z += leafval[leaf_base + (nds[2] & 0x7fffu)];
+      p4.w += leafval[leaf_base + (nds[3] & 0x7fffu)];
       *reinterpret_cast<float4*>(pred + r) = p4;
+    } else {
+      uint2 s2;
+      s2.x = ((uint32_t)sl[0] & 0xffffu) | ((uint32_t)sl[1] << 16);
+      s2.y = ((uint32_t)sl[2] & 0xffffu) | ((uint32_t)sl[3] << 16);
+      *reinterpret_cast<uint2*>(slot + r) = s2;
     }
   }
 }
@@ -656,35 +733,38 @@ cudaError_t launch_hist(const HistLaunch& L, cudaStream_t s, int* n_launch) {
   while ((uint32_t)ft > 1 && (uint32_t)ft / 2 >= L.nf) ft >>= 1;  // no idle tile lanes
   const uint32_t ftiles = (L.nf + ft - 1) / ft;
   const uint32_t gz = (L.groups + gchunk - 1) / gchunk;
-  uint64_t rchunks = (L.n_pad + 8191) / 8192;
-  const uint64_t max_r = (uint64_t)kTargetCtas / ((uint64_t)ftiles * gz);
-  if (rchunks > (max_r < 1 ? 1 : max_r)) rchunks = max_r < 1 ? 1 : max_r;
+  // Row chunks: whole multiples of kRowAlign rows, about two CTAs per SM in total,
+  // grouped into clusters of up to kMaxCluster CTAs along the row chunks.
+  const uint64_t units = L.n_pad / kRowAlign;
+  uint64_t rchunks = (units + 3) / 4;  // >= 8192 rows per CTA
+  uint64_t max_r = (uint64_t)kTargetCtas / ((uint64_t)ftiles * gz);
+  if (max_r < 1) max_r = 1;
+  if (rchunks > max_r) rchunks = max_r;
+  if (rchunks > units) rchunks = units;
   if (rchunks < 1) rchunks = 1;
-  uint64_t rows = (L.n_pad + rchunks - 1) / rchunks;
-  rows = (rows + 3) & ~3ull;
+  const uint64_t rows = (units + rchunks - 1) / rchunks * kRowAlign;
   rchunks = (L.n_pad + rows - 1) / rows;
+  int cluster = 1;
+  while (cluster * 2 <= kMaxCluster && (uint64_t)cluster * 2 <= rchunks) cluster *= 2;
+  rchunks = (rchunks + cluster - 1) / cluster * cluster;
 
   HistArgs a;
   a.bins = L.bins;
   a.ld = L.ld;
-  a.node = L.node;
-  a.g = L.g;
-  a.h = L.h;
+  a.slot = L.slot;
+  a.qg = L.qg;
+  a.qh = L.qh;
   a.n_pad = L.n_pad;
   a.nf = L.nf;
   a.nb = L.nb;
   a.gchunk = gchunk;
-  a.groups = L.groups;
-  a.odd_only = L.odd_only;
-  a.maxbits = L.maxbits;
-  a.e_override = L.e_override;
   a.out = L.out;
   a.rows_per_cta = rows;
   const size_t smem = 8ull * gchunk * L.nb * (uint64_t)ft;
   dim3 grid((unsigned)rchunks, ftiles, gz);
   if (n_launch) (*n_launch)++;
-  return L.packed ? launch_hist_ft<true>(ft, a, grid, smem, s)
-                  : launch_hist_ft<false>(ft, a, grid, smem, s);
+  return L.packed ? launch_hist_ft<true>(ft, a, grid, cluster, smem, s)
+                  : launch_hist_ft<false>(ft, a, grid, cluster, smem, s);
 }
 
 cudaError_t launch_split(const SplitLaunch& a, cudaStream_t s) {
@@ -719,24 +799,32 @@ cudaError_t launch_pack4(const uint8_t* d_bins, uint64_t n_pad, uint32_t nf, uin
   return cudaGetLastError();
 }
 
-cudaError_t launch_grad(const float* pred, const float* y, float* g, float* h, uint16_t* node,
-                        uint64_t n, int logistic, uint64_t stride, uint64_t phase,
+cudaError_t launch_grad(const float* pred, const float* y, float* g, float* h, uint64_t n,
+                        uint64_t n_pad, int logistic, uint64_t stride, uint64_t phase,
                         uint64_t row_offset, int compute_max, uint32_t* maxbits,
                         cudaStream_t s, int* nl) {
-  const uint64_t n_pad = (n + 63) / 64 * 64;
-  k_grad<<<grid_for(n_pad, 256), 256, 0, s>>>(pred, y, g, h, node, n, n_pad, logistic, stride,
-                                               phase, row_offset, compute_max, maxbits);
+  k_grad<<<grid_for(n_pad, 256), 256, 0, s>>>(pred, y, g, h, n, n_pad, logistic, stride, phase,
+                                               row_offset, compute_max, maxbits);
+  if (nl) (*nl)++;
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quant(const float* g, const float* h, const uint32_t* maxbits, uint64_t n_pad,
+                         int32_t* qg, int32_t* qh, uint16_t* node, int16_t* slot,
+                         long long* hb0, uint64_t hb0_words, cudaStream_t s, int* nl) {
+  k_quant<<<grid_for(n_pad, 256), 256, 0, s>>>(g, h, maxbits, n_pad, qg, qh, node, slot, hb0,
+                                               hb0_words);
   if (nl) (*nl)++;
   return cudaGetLastError();
 }
 
 cudaError_t launch_apply(const uint8_t* bins, uint64_t ld, int packed, uint16_t* node,
-                         const uint32_t* split_ft, uint64_t n_pad, int final_level,
-                         const float* leafval, uint32_t leaf_base, float* pred, cudaStream_t s,
-                         int* nl) {
+                         int16_t* slot, const uint32_t* split_ft, uint64_t n_pad,
+                         int next_odd_only, int final_level, const float* leafval,
+                         uint32_t leaf_base, float* pred, cudaStream_t s, int* nl) {
   const uint64_t n4 = n_pad / 4;
-  k_apply<<<grid_for(n4, 256), 256, 0, s>>>(bins, ld, packed, node, split_ft, n4, final_level,
-                                             leafval, leaf_base, pred);
+  k_apply<<<grid_for(n4, 256), 256, 0, s>>>(bins, ld, packed, node, slot, split_ft, n4,
+                                             next_odd_only, final_level, leafval, leaf_base, pred);
   if (nl) (*nl)++;
   return cudaGetLastError();
 }
