@@ -22,6 +22,33 @@ struct rw_ctx {
   uint64_t launches = 0;  // kernels launched on this context (all time)
 };
 
+// Bins in HBM are stored column-major in tiles of kBinTile rows: tile t holds rows
+// [t*kBinTile, +kBinTile) and, inside it, feature f's bins form one row of `rs` bytes
+// (kBinTile u8, or kBinTile/2 bytes of 4-bit pairs, plus 16 bytes of padding). A feature
+// slice of a tile is therefore one contiguous block (one TMA bulk copy), and the padding
+// (an odd number of 16-byte units) keeps 16-byte shared-memory reads of consecutive
+// features on distinct banks.
+constexpr uint32_t kBinTile = 512;
+
+struct BinLayout {
+  uint32_t nf = 0;
+  uint32_t rs = 0;          // bytes per feature row within a tile
+  uint64_t tile_bytes = 0;  // nf * rs
+  int packed = 0;
+  __host__ __device__ uint64_t offset(uint32_t f, uint64_t r) const {
+    const uint64_t in = r % kBinTile;
+    return (r / kBinTile) * tile_bytes + (uint64_t)f * rs + (packed ? in / 2 : in);
+  }
+  static BinLayout make(uint32_t nf, int packed) {
+    BinLayout L;
+    L.nf = nf;
+    L.packed = packed;
+    L.rs = (packed ? kBinTile / 2 : kBinTile) + 16;
+    L.tile_bytes = (uint64_t)nf * L.rs;
+    return L;
+  }
+};
+
 struct rw_dataset {
   rw_ctx* ctx = nullptr;
   uint64_t n = 0;         // local rows
@@ -30,9 +57,9 @@ struct rw_dataset {
   uint64_t row_offset = 0;
   uint32_t nf = 0, n_bins = 0;
   int packed = 0;
-  uint64_t ld = 0;        // bytes per feature column of d_bins (n_pad, or n_pad/2 packed)
-  uint8_t* d_bins = nullptr;    // [nf][ld] column-major (u8 or 4-bit packed)
-  uint8_t* d_bins_u8 = nullptr; // unpacked copy kept only when packed (for rw_dataset_bins)
+  BinLayout lay;                // layout of d_bins
+  uint8_t* d_bins = nullptr;    // row-tiled column-major (u8 or 4-bit packed), see BinLayout
+  uint8_t* d_bins_u8 = nullptr; // u8 copy (row-tiled) kept only when packed
   float* d_y = nullptr;         // [n_pad]
   float* d_cuts = nullptr;      // [nf][n_bins-1]
   std::vector<float> cuts;
@@ -55,8 +82,7 @@ struct rw_dmodel {
 
 struct HistLaunch {
   const uint8_t* bins;
-  uint64_t ld;
-  int packed;
+  BinLayout lay;
   const int16_t* slot;   // per row: histogram group this level builds into, or -1
   const int32_t* qg;     // per row: fixed-point g (rw_quantize)
   const int32_t* qh;     // per row: fixed-point h
@@ -64,6 +90,7 @@ struct HistLaunch {
   uint32_t nf, nb;
   uint32_t groups;       // histogram groups written (out has `groups` slots)
   long long* out;        // int64 [groups][nf][nb][2], zeroed by the caller
+  int* err;              // set to a nonzero code if a bounded wait gave up
 };
 cudaError_t launch_hist(const HistLaunch& a, cudaStream_t s, int* n_launch);
 
@@ -99,12 +126,13 @@ cudaError_t launch_split(const SplitLaunch& a, cudaStream_t s);
 
 // Rows are padded to a multiple of kRowAlign so every histogram CTA's row range is a
 // whole number of steps for every lane.
-constexpr uint64_t kRowAlign = 2048;
+constexpr uint64_t kRowAlign = 4096;
 
 cudaError_t launch_bin(const float* x_rowmajor, uint64_t n, uint32_t nf, const float* d_cuts,
-                       uint32_t n_bins, uint8_t* d_bins, uint64_t ld, cudaStream_t s, int* nl);
-cudaError_t launch_pack4(const uint8_t* d_bins, uint64_t n_pad, uint32_t nf, uint8_t* d_packed,
-                         cudaStream_t s, int* nl);
+                       uint32_t n_bins, uint8_t* d_bins, const BinLayout& lay, cudaStream_t s,
+                       int* nl);
+cudaError_t launch_pack4(const uint8_t* d_bins, const BinLayout& lay_u8, uint64_t n_pad,
+                         uint8_t* d_packed, const BinLayout& lay_p, cudaStream_t s, int* nl);
 cudaError_t launch_grad(const float* pred, const float* y, float* g, float* h, uint64_t n,
                         uint64_t n_pad, int logistic, uint64_t stride, uint64_t phase,
                         uint64_t row_offset, int compute_max, uint32_t* maxbits,
@@ -116,7 +144,7 @@ cudaError_t launch_quant(const float* g, const float* h, const uint32_t* maxbits
                          long long* hb0, uint64_t hb0_words, cudaStream_t s, int* nl);
 // leaf = 2*leaf + (bin > t) keeping the excluded flag; writes the next level's build
 // slot (next_odd_only: odd children keyed by parent), or at the final level updates pred.
-cudaError_t launch_apply(const uint8_t* bins, uint64_t ld, int packed, uint16_t* node,
+cudaError_t launch_apply(const uint8_t* bins, const BinLayout& lay, uint16_t* node,
                          int16_t* slot, const uint32_t* split_ft, uint64_t n_pad,
                          int next_odd_only, int final_level, const float* leafval,
                          uint32_t leaf_base, float* pred, cudaStream_t s, int* nl);

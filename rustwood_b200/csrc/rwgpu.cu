@@ -6,6 +6,8 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <cstring>
+
 #include <algorithm>
 #include <chrono>
 #include <cmath>
@@ -293,12 +295,14 @@ static int dataset_build(rw_ctx* ctx, const float* d_x, const float* y, bool y_o
   ds->packed = (pack4 && n_bins <= 16) ? 1 : 0;
   ds->cuts.assign(cuts, cuts + (size_t)nf * (n_bins - 1));
   cudaStream_t s = ctx->stream;
+  const BinLayout lay_u8 = BinLayout::make(nf, 0);
+  const size_t u8_bytes = (size_t)(ds->n_pad / kBinTile) * lay_u8.tile_bytes;
   DBuf<uint8_t> bins;
   DBuf<float> dy, dc;
-  cudaError_t e = bins.alloc((size_t)nf * ds->n_pad);
+  cudaError_t e = bins.alloc(u8_bytes);
   if (e == cudaSuccess) e = dy.alloc(ds->n_pad);
   if (e == cudaSuccess) e = dc.alloc(ds->cuts.size());
-  if (e == cudaSuccess) e = cudaMemsetAsync(bins.p, 0, (size_t)nf * ds->n_pad, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(bins.p, 0, u8_bytes, s);
   if (e == cudaSuccess) e = cudaMemsetAsync(dy.p, 0, ds->n_pad * sizeof(float), s);
   if (e == cudaSuccess)
     e = cudaMemcpyAsync(dc.p, ds->cuts.data(), ds->cuts.size() * sizeof(float),
@@ -306,19 +310,22 @@ static int dataset_build(rw_ctx* ctx, const float* d_x, const float* y, bool y_o
   if (e == cudaSuccess)
     e = cudaMemcpyAsync(dy.p, y, n * sizeof(float),
                         y_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s);
-  if (e == cudaSuccess) e = launch_bin(d_x, n, nf, dc.p, n_bins, bins.p, ds->n_pad, s, &nl);
+  if (e == cudaSuccess) e = launch_bin(d_x, n, nf, dc.p, n_bins, bins.p, lay_u8, s, &nl);
   if (e == cudaSuccess && ds->packed) {
+    const BinLayout lay_p = BinLayout::make(nf, 1);
+    const size_t p_bytes = (size_t)(ds->n_pad / kBinTile) * lay_p.tile_bytes;
     DBuf<uint8_t> packed;
-    e = packed.alloc((size_t)nf * ds->n_pad / 2);
-    if (e == cudaSuccess) e = launch_pack4(bins.p, ds->n_pad, nf, packed.p, s, &nl);
+    e = packed.alloc(p_bytes);
+    if (e == cudaSuccess) e = cudaMemsetAsync(packed.p, 0, p_bytes, s);
+    if (e == cudaSuccess) e = launch_pack4(bins.p, lay_u8, ds->n_pad, packed.p, lay_p, s, &nl);
     if (e == cudaSuccess) {
       ds->d_bins_u8 = bins.release();
       ds->d_bins = packed.release();
-      ds->ld = ds->n_pad / 2;
+      ds->lay = lay_p;
     }
   } else if (e == cudaSuccess) {
     ds->d_bins = bins.release();
-    ds->ld = ds->n_pad;
+    ds->lay = lay_u8;
   }
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
   ctx->launches += nl;
@@ -390,10 +397,18 @@ extern "C" int rw_dataset_bins(const rw_dataset* ds, uint8_t* out) {
   if (!ds || !out) return fail(nullptr, RW_ERR_ARG, "NULL argument");
   rw_ctx* ctx = ds->ctx;
   RW_CU(ctx, cudaSetDevice(ctx->device));
+  // Device bins are row-tiled (BinLayout); the host copy is feature-major [nf][n].
   const uint8_t* src = ds->packed ? ds->d_bins_u8 : ds->d_bins;
-  RW_CU(ctx, cudaMemcpy2DAsync(out, ds->n, src, ds->n_pad, ds->n, ds->nf, cudaMemcpyDeviceToHost,
-                               ctx->stream));
+  const BinLayout lay = BinLayout::make(ds->nf, 0);
+  std::vector<uint8_t> tiled((size_t)(ds->n_pad / kBinTile) * lay.tile_bytes);
+  RW_CU(ctx, cudaMemcpyAsync(tiled.data(), src, tiled.size(), cudaMemcpyDeviceToHost,
+                             ctx->stream));
   RW_CU(ctx, cudaStreamSynchronize(ctx->stream));
+  for (uint32_t f = 0; f < ds->nf; f++)
+    for (uint64_t r0 = 0; r0 < ds->n; r0 += kBinTile) {
+      const uint64_t len = std::min<uint64_t>(kBinTile, ds->n - r0);
+      std::memcpy(out + (size_t)f * ds->n + r0, tiled.data() + lay.offset(f, r0), len);
+    }
   return RW_OK;
 }
 
@@ -464,6 +479,9 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
   RW_CU(ctx, best_bin.get(ds, "best_bin", nf));
   RW_CU(ctx, counter.get(ds, "counter", 1));
   RW_CU(ctx, split_ft.get(ds, "split_ft", 2));
+  WsBuf<int> kerr;
+  RW_CU(ctx, kerr.get(ds, "kernel_err", 1));
+  RW_CU(ctx, cudaMemsetAsync(kerr.p, 0, sizeof(int), s));
   RW_CU(ctx, cudaMemsetAsync(g.p, 0, n_pad * 4, s));
   RW_CU(ctx, cudaMemsetAsync(h.p, 0, n_pad * 4, s));
   RW_CU(ctx, cudaMemsetAsync(node.p, 0, n_pad * 2, s));
@@ -555,8 +573,7 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
           d + 1 < D ? (subtract ? (1u << d) : (1u << (d + 1))) : 0u;
       HistLaunch hl;
       hl.bins = ds->d_bins;
-      hl.ld = ds->ld;
-      hl.packed = ds->packed;
+      hl.lay = ds->lay;
       hl.slot = slot.p;
       hl.qg = qg.p;
       hl.qh = qh.p;
@@ -565,6 +582,7 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
       hl.nb = nb;
       hl.groups = groups;
       hl.out = hb;
+      hl.err = kerr.p;
       RW_CU(ctx, launch_hist(hl, s, &nl));
       hist_launches++;
       alg_bytes += (double)n * nf * bin_bytes + 12.0 * (double)n + 8.0 * nf * nb * groups;
@@ -607,7 +625,7 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
       RW_CU(ctx, launch_split(sl, s));
       nl++;
       pt.mark(RW_CAT_SPLIT);
-      RW_CU(ctx, launch_apply(ds->d_bins, ds->ld, ds->packed, node.p, slot.p, split_ft.p, n_pad,
+      RW_CU(ctx, launch_apply(ds->d_bins, ds->lay, node.p, slot.p, split_ft.p, n_pad,
                               subtract ? 1 : 0, d == D - 1, d_leafval.p, t * NL, pred.p, s, &nl));
       pt.mark(d == D - 1 ? RW_CAT_UPDATE_PRED : RW_CAT_APPLY);
     }
@@ -616,6 +634,10 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
   rc = wait_stream(ctx);
   if (rc) return rc;
   ctx->launches += nl;
+  int kerr_h = 0;
+  RW_CU(ctx, cudaMemcpy(&kerr_h, kerr.p, sizeof(int), cudaMemcpyDeviceToHost));
+  if (kerr_h)
+    return fail(ctx, RW_ERR_TIMEOUT, "a histogram pipeline wait gave up (bounded wait expired)");
 
   if (T > 0) {
     RW_CU(ctx, cudaMemcpy(feat, d_feat.p, (size_t)T * D * 4, cudaMemcpyDeviceToHost));
@@ -899,6 +921,9 @@ extern "C" int rw_debug_level_hist(rw_dataset* ds, const int32_t* node, const fl
     if (node[i] < 0) continue;
     if (node[i] > 0x7fff) return fail(ctx, RW_ERR_ARG, "node index above 32767");
     const int32_t a = rw_quantize(g[i], sg), b = rw_quantize(h[i], sh);
+    // the histogram kernel's exact 32-bit partial sums rely on |q| <= 2^RW_QBITS
+    if (std::abs(a) > (1 << RW_QBITS) || std::abs(b) > (1 << RW_QBITS))
+      return fail(ctx, RW_ERR_ARG, "e_g/e_h put |q| above 2^RW_QBITS");
     if ((a | b) == 0) continue;
     qgv[i] = a;
     qhv[i] = b;
@@ -919,8 +944,7 @@ extern "C" int rw_debug_level_hist(rw_dataset* ds, const int32_t* node, const fl
   RW_CU(ctx, cudaMemset(dout.p, 0, words * 8));
   HistLaunch hl;
   hl.bins = ds->d_bins;
-  hl.ld = ds->ld;
-  hl.packed = ds->packed;
+  hl.lay = ds->lay;
   hl.slot = dn.p;
   hl.qg = dg.p;
   hl.qh = dh.p;
@@ -929,11 +953,18 @@ extern "C" int rw_debug_level_hist(rw_dataset* ds, const int32_t* node, const fl
   hl.nb = ds->n_bins;
   hl.groups = groups;
   hl.out = dout.p;
+  DBuf<int> derr;
+  RW_CU(ctx, derr.alloc(1));
+  RW_CU(ctx, cudaMemset(derr.p, 0, sizeof(int)));
+  hl.err = derr.p;
   int nl = 0;
   RW_CU(ctx, launch_hist(hl, ctx->stream, &nl));
   RW_CU(ctx, cudaStreamSynchronize(ctx->stream));
   ctx->launches += nl;
   RW_CU(ctx, cudaMemcpy(out, dout.p, words * 8, cudaMemcpyDeviceToHost));
+  int herr = 0;
+  RW_CU(ctx, cudaMemcpy(&herr, derr.p, sizeof(int), cudaMemcpyDeviceToHost));
+  if (herr) return fail(ctx, RW_ERR_TIMEOUT, "a histogram pipeline wait gave up");
   return RW_OK;
 }
 

@@ -23,6 +23,10 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "rw_expf.h"
 #include "rw_internal.cuh"
 
@@ -31,16 +35,69 @@
 namespace {
 
 constexpr int kHistThreads = 512;
-constexpr uint32_t kBias = 0x80000000u;
-constexpr int kHistSmemBudget = 112 * 1024;  // two CTAs per SM
-constexpr int kTargetCtas = 2 * 148;
+// Rows one histogram CTA may accumulate into its 32-bit shared cells: every |q| is at
+// most 2^RW_QBITS, so a cell's partial sum stays within 2^(30) in magnitude and the
+// 32-bit word holds it exactly (no carries, no returned values needed).
+constexpr uint32_t kMaxRowsPerCta = 1u << (30 - RW_QBITS);
+static_assert(kMaxRowsPerCta >= 512, "quantisation too fine for one bin tile per CTA");
 constexpr int kMaxCluster = 8;
+constexpr int kStages = 2;
+constexpr int kSmemPerSm = 227 * 1024;  // usable shared memory per SM (one or two CTAs)
 
 namespace cg = cooperative_groups;
 
+// ---- TMA bulk copies and mbarriers (PTX) -------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(
+                   smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// 1D bulk copy global -> this CTA's shared memory, completing on `bar` (no multicast).
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// Waits for the mbarrier phase with a ~1 s clock limit; false when the limit passed.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity))
+    if (clock64() - t0 > 2000000000LL) return false;
+  return true;
+}
+
 struct HistArgs {
   const uint8_t* bins;
-  uint64_t ld;
+  BinLayout lay;
   const int16_t* slot;
   const int32_t* qg;
   const int32_t* qh;
@@ -48,151 +105,197 @@ struct HistArgs {
   uint32_t nf, nb;
   uint32_t gchunk;  // groups per CTA (blockIdx.z selects the chunk)
   long long* out;
-  uint64_t rows_per_cta;
+  int* err;
+  uint64_t rows_per_cta;  // multiple of kBinTile
+  uint32_t stage_bytes;   // bytes per stage
+  uint32_t hist_bytes;    // bytes of the shared histogram (stages follow it)
 };
 
-// Adds ±2^32 to the global cell when the 32-bit shared accumulator wrapped in the add
-// of q that returned `old` (the shared word holds the cell's low 32 bits + 2^31).
-__device__ __forceinline__ void carry_out(uint32_t old, int32_t q, long long* gcell) {
-  const uint32_t nw = old + (uint32_t)q;
-  const int delta = (nw < old ? 1 : 0) - (q < 0 ? 1 : 0);
-  if (delta != 0)
-    atomicAdd(reinterpret_cast<unsigned long long*>(gcell),
-              (unsigned long long)((long long)delta * 4294967296LL));
-}
-
-// A wrap is only possible when the returned low word is within 2^26 (>= |q|) of the
-// 32-bit boundary, i.e. old + 2^26 (mod 2^32) < 2^27.
-__device__ __forceinline__ bool near_edge(uint32_t og, uint32_t oh) {
-  return min(og + (1u << 26), oh + (1u << 26)) < (1u << 27);
-}
-
-// One CTA: feature tile [blockIdx.y*FT, +FT) x group chunk x row range, in a cluster of
-// CTAs along the row ranges. Lane (k, j) handles feature j of the tile for row slot k;
-// each thread covers 4 consecutive rows per step (one u32 of u8 bins, or one u16 of
-// 4-bit bins). Shared cells are laid out [group][bin][FT]: the FT lanes of one row hit
-// FT distinct banks. After the rows, the cluster's CTAs sum their shared histograms
-// through distributed shared memory, each CTA flushing a slice to the global int64
-// histogram, so a cell costs one global atomic per cluster rather than per CTA.
-template <int FT, bool PACKED>
-__global__ void __launch_bounds__(kHistThreads, 2) k_hist(HistArgs a) {
-  extern __shared__ uint32_t smem[];
+// One CTA: a tile of FT*FPL consecutive features x group chunk x row range (at most
+// kMaxRowsPerCta rows), in a cluster of CTAs along the row ranges. The row range streams
+// through shared memory one bin tile (kBinTile rows) at a time: thread 0 issues TMA bulk
+// copies -- the CTA's feature slice of the tile is one contiguous block in the row-tiled
+// bin layout, plus the tile's slot/q arrays -- into a double-buffered stage, completing on
+// an mbarrier, while the CTA accumulates the previous tile. Lane (k, j) handles features
+// j + p*FT (p < FPL) of the tile for row slot k, U consecutive rows at a time. Shared
+// words are laid out [group][bin][g|h][FT*FPL]: for each p the FT lanes of one row hit FT
+// distinct banks, and a cell's h word is a fixed offset from its g word. Cells are plain
+// 32-bit integers updated by reductions whose results are not read back: the row bound
+// keeps every partial sum exact. With FT = 32 every lane of a warp works on the same row,
+// so rows that are not built are skipped warp-uniformly. After the rows, the cluster's
+// CTAs sum their shared histograms through distributed shared memory, each CTA adding a
+// slice to the global int64 histogram.
+template <int FT, int FPL, bool PACKED>
+__global__ void __launch_bounds__(kHistThreads, 1) k_hist(HistArgs a) {
+  constexpr uint32_t FTT = FT * FPL;  // features per CTA
+  constexpr uint32_t T = kBinTile;
+  constexpr int RW = 32 / FT;
+  // rows per lane step: 16 (one 16-byte load of u8 bins) when a tile round of
+  // 16 warps x RW slots x 16 rows fits the tile, else 4
+  constexpr uint32_t U = (16u * (kHistThreads / 32) * RW <= T) ? 16u : 4u;
+  extern __shared__ __align__(128) unsigned char hsm[];
+  uint32_t* smem = reinterpret_cast<uint32_t*>(hsm);
   const uint32_t G = a.gchunk, nb = a.nb;
-  const uint32_t cells = G * nb * FT;
-  uint32_t* lo_g = smem;
-  uint32_t* lo_h = smem + cells;
-  for (uint32_t i = threadIdx.x; i < 2 * cells; i += kHistThreads) smem[i] = kBias;
+  const uint32_t words = 2 * G * nb * FTT;
+  unsigned char* stage0 = hsm + a.hist_bytes;
+  __shared__ __align__(8) uint64_t bar[kStages];
+  __shared__ int abort_flag;
+  for (uint32_t i = threadIdx.x; i < words; i += kHistThreads) smem[i] = 0u;
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < kStages; st++) mbar_init(&bar[st], 1);
+    mbar_init_fence();
+    abort_flag = 0;
+  }
   __syncthreads();
 
-  constexpr int RW = 32 / FT;
-  constexpr int kStep = (kHistThreads / 32) * RW * 4;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int j = lane % FT, k = lane / FT;
-  const uint32_t f0 = blockIdx.y * FT;
-  const uint32_t f = f0 + j;
-  const bool fvalid = f < a.nf;
+  const uint32_t f0 = blockIdx.y * FTT;
   const int g0 = (int)(blockIdx.z * a.gchunk);
-  const uint8_t* col = a.bins + (size_t)(fvalid ? f : 0) * a.ld;
-  long long* outf = a.out + (size_t)(fvalid ? f : 0) * nb * 2;
+  const uint32_t rs = a.lay.rs;
   const size_t gstride = (size_t)a.nf * nb * 2;
+  const uint32_t nvalid = a.nf - f0 < FTT ? a.nf - f0 : FTT;
+  bool fval[FPL];
+#pragma unroll
+  for (int p = 0; p < FPL; p++) fval[p] = (uint32_t)(p * FT + j) < nvalid;
 
   const uint64_t r_begin = (uint64_t)blockIdx.x * a.rows_per_cta;
   uint64_t r_end = r_begin + a.rows_per_cta;
   if (r_end > a.n_pad) r_end = a.n_pad;
+  const uint32_t ntiles = r_end > r_begin ? (uint32_t)((r_end - r_begin) / T) : 0u;
 
-  for (uint64_t rb = r_begin + (uint64_t)(warp * RW + k) * 4; rb < r_end; rb += kStep) {
-    const uint2 sl2 = *reinterpret_cast<const uint2*>(a.slot + rb);
-    const int4 qg4 = *reinterpret_cast<const int4*>(a.qg + rb);
-    const int4 qh4 = *reinterpret_cast<const int4*>(a.qh + rb);
-    uint32_t b4;
-    if (PACKED) {
-      const uint32_t p = *reinterpret_cast<const uint16_t*>(col + (rb >> 1));
-      b4 = (p & 0xfu) | ((p & 0xf0u) << 4) | ((p & 0xf00u) << 8) | ((p & 0xf000u) << 12);
-    } else {
-      b4 = *reinterpret_cast<const uint32_t*>(col + rb);
+  auto stage_ptr = [&](int st) { return stage0 + (size_t)st * a.stage_bytes; };
+  auto issue = [&](uint32_t t, int st) {  // thread 0
+    unsigned char* sp = stage_ptr(st);
+    const uint64_t r0 = r_begin + (uint64_t)t * T;
+    const uint32_t bbytes = nvalid * rs;
+    mbar_expect_tx(&bar[st], bbytes + 10u * T);
+    bulk_g2s(sp, a.bins + (r0 / T) * a.lay.tile_bytes + (uint64_t)f0 * rs, bbytes, &bar[st]);
+    unsigned char* rowp = sp + (size_t)FTT * rs;
+    bulk_g2s(rowp, a.slot + r0, 2u * T, &bar[st]);
+    bulk_g2s(rowp + 2u * T, a.qg + r0, 4u * T, &bar[st]);
+    bulk_g2s(rowp + 6u * T, a.qh + r0, 4u * T, &bar[st]);
+  };
+
+  if (threadIdx.x == 0 && ntiles > 0) issue(0, 0);
+  for (uint32_t t = 0; t < ntiles; t++) {
+    const int st = t & 1;
+    if (threadIdx.x == 0 && t + 1 < ntiles && !abort_flag) {
+      fence_proxy_async_smem();  // the stage's last readers finished before the barrier below
+      issue(t + 1, st ^ 1);
     }
-    const int sl[4] = {(int)(int16_t)(sl2.x & 0xffffu), (int)(int16_t)(sl2.x >> 16),
-                       (int)(int16_t)(sl2.y & 0xffffu), (int)(int16_t)(sl2.y >> 16)};
-    const int32_t qg[4] = {qg4.x, qg4.y, qg4.z, qg4.w};
-    const int32_t qh[4] = {qh4.x, qh4.y, qh4.z, qh4.w};
-    uint32_t og[4], oh[4], cell[4];
-    bool act[4];
+    // After a wait gave up, no further copies are issued and no further waits are made.
+    if (!abort_flag && !mbar_wait_bounded(&bar[st], (t >> 1) & 1u)) abort_flag = 1;
+    const unsigned char* sp = stage_ptr(st);
+    const int16_t* s_slot = reinterpret_cast<const int16_t*>(sp + (size_t)FTT * rs);
+    const int32_t* s_qg = reinterpret_cast<const int32_t*>(sp + (size_t)FTT * rs + 2u * T);
+    const int32_t* s_qh = reinterpret_cast<const int32_t*>(sp + (size_t)FTT * rs + 6u * T);
+    if (!abort_flag) {
+      for (uint32_t rg = warp * RW + k; rg < T / U; rg += (kHistThreads / 32) * RW) {
+        const uint32_t r = rg * U;
+        uint32_t bw[FPL][U / 4];
 #pragma unroll
-    for (int s = 0; s < 4; s++) {
-      const uint32_t grp = (uint32_t)(sl[s] - g0);
-      act[s] = fvalid && grp < G;
-      cell[s] = (grp * nb + ((b4 >> (8 * s)) & 0xffu)) * FT + j;
-      if (act[s]) {
-        og[s] = atomicAdd(&lo_g[cell[s]], (uint32_t)qg[s]);
-        oh[s] = atomicAdd(&lo_h[cell[s]], (uint32_t)qh[s]);
+        for (int p = 0; p < FPL; p++) {
+          const unsigned char* sb = sp + (size_t)(p * FT + j) * rs;
+          if (U == 16) {
+            if (PACKED) {
+              const uint2 pk = *reinterpret_cast<const uint2*>(sb + r / 2);
+              const uint32_t pw[2] = {pk.x, pk.y};
+#pragma unroll
+              for (int h2 = 0; h2 < 2; h2++)
+#pragma unroll
+                for (int q2 = 0; q2 < 2; q2++) {
+                  const uint32_t v = pw[h2] >> (16 * q2);
+                  bw[p][(2 * h2 + q2) % (U / 4)] = (v & 0xfu) | ((v & 0xf0u) << 4) |
+                                                   ((v & 0xf00u) << 8) | ((v & 0xf000u) << 12);
+                }
+            } else {
+              const uint4 pk = *reinterpret_cast<const uint4*>(sb + r);
+              const uint32_t pw[4] = {pk.x, pk.y, pk.z, pk.w};
+#pragma unroll
+              for (int q = 0; q < (int)(U / 4); q++) bw[p][q] = pw[q];
+            }
+          } else {
+            if (PACKED) {
+              const uint32_t v = *reinterpret_cast<const uint16_t*>(sb + r / 2);
+              bw[p][0] = (v & 0xfu) | ((v & 0xf0u) << 4) | ((v & 0xf00u) << 8) |
+                         ((v & 0xf000u) << 12);
+            } else {
+              bw[p][0] = *reinterpret_cast<const uint32_t*>(sb + r);
+            }
+          }
+        }
+#pragma unroll
+        for (int q4 = 0; q4 < (int)(U / 4); q4++) {
+          const uint2 sl2 = *reinterpret_cast<const uint2*>(s_slot + r + 4 * q4);
+          const int4 qg4 = *reinterpret_cast<const int4*>(s_qg + r + 4 * q4);
+          const int4 qh4 = *reinterpret_cast<const int4*>(s_qh + r + 4 * q4);
+          const int sl[4] = {(int)(int16_t)(sl2.x & 0xffffu), (int)(int16_t)(sl2.x >> 16),
+                             (int)(int16_t)(sl2.y & 0xffffu), (int)(int16_t)(sl2.y >> 16)};
+          const uint32_t qgr[4] = {(uint32_t)qg4.x, (uint32_t)qg4.y, (uint32_t)qg4.z,
+                                   (uint32_t)qg4.w};
+          const uint32_t qhr[4] = {(uint32_t)qh4.x, (uint32_t)qh4.y, (uint32_t)qh4.z,
+                                   (uint32_t)qh4.w};
+#pragma unroll
+          for (int s = 0; s < 4; s++) {
+            const uint32_t grp = (uint32_t)(sl[s] - g0);
+            if (FT == 32 && grp >= G) continue;  // warp-uniform: every lane works on this row
+            const uint32_t lb = grp * nb * (2 * FTT) + (uint32_t)j;
+#pragma unroll
+            for (int p = 0; p < FPL; p++) {
+              if (fval[p] && (FT == 32 || grp < G)) {
+                const uint32_t bin = __byte_perm(bw[p][q4], 0u, 0x4440u + (uint32_t)s);
+                const uint32_t w = lb + bin * (2 * FTT) + (uint32_t)(p * FT);
+                atomicAdd(&smem[w], qgr[s]);
+                atomicAdd(&smem[w + FTT], qhr[s]);
+              }
+            }
+          }
+        }
       }
     }
-#pragma unroll
-    for (int s = 0; s < 4; s++) {
-      if (act[s] && near_edge(og[s], oh[s])) {
-        const uint32_t bin = (b4 >> (8 * s)) & 0xffu;
-        long long* gc = outf + (size_t)sl[s] * gstride + (size_t)bin * 2;
-        carry_out(og[s], qg[s], gc);
-        carry_out(oh[s], qh[s], gc + 1);
-      }
-    }
+    __syncthreads();  // every reader of stage `st` is done before it is refilled
   }
+  if (abort_flag && threadIdx.x == 0) atomicExch(a.err, 1);
 
   cg::cluster_group cluster = cg::this_cluster();
   cluster.sync();
   const uint32_t cn = cluster.num_blocks(), cr = cluster.block_rank();
-  const uint32_t words = 2 * cells;
   const uint32_t per = (words + cn - 1) / cn;
   const uint32_t w_begin = cr * per, w_end = min(words, w_begin + per);
   for (uint32_t w = w_begin + threadIdx.x; w < w_end; w += kHistThreads) {
     long long v = 0;
     for (uint32_t r = 0; r < cn; r++) {
       const uint32_t* remote = cluster.map_shared_rank(smem, (int)r);
-      v += (long long)remote[w] - (long long)kBias;
+      v += (long long)(int32_t)remote[w];
     }
     if (v == 0) continue;
-    const uint32_t c = w < cells ? w : w - cells;
-    const uint32_t jj = c % FT, rest = c / FT, bin = rest % nb, grp = rest / nb;
-    const uint32_t ff = f0 + jj;
+    const uint32_t blk = w / (2 * FTT), within = w % (2 * FTT);
+    const uint32_t is_h = within >= FTT ? 1u : 0u, fo = within - is_h * FTT;
+    const uint32_t bin = blk % nb, grp = blk / nb;
+    const uint32_t ff = f0 + fo;
     if (ff >= a.nf) continue;
-    long long* gc = a.out + (size_t)(g0 + grp) * gstride + ((size_t)ff * nb + bin) * 2 +
-                    (w < cells ? 0 : 1);
+    long long* gc = a.out + (size_t)(g0 + grp) * gstride + ((size_t)ff * nb + bin) * 2 + is_h;
     atomicAdd(reinterpret_cast<unsigned long long*>(gc), (unsigned long long)v);
   }
   cluster.sync();  // keep this CTA's shared memory alive until every reader is done
 }
 
-template <int FT, bool PACKED>
-cudaError_t launch_hist_t(const HistArgs& args, dim3 grid, int cluster, size_t smem,
-                          cudaStream_t s) {
-  cudaError_t e = cudaFuncSetAttribute(k_hist<FT, PACKED>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(kHistThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = cluster;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k_hist<FT, PACKED>, args);
+template <int FT, int FPL, bool PACKED>
+const void* hist_fn() {
+  return reinterpret_cast<const void*>(&k_hist<FT, FPL, PACKED>);
 }
 
 template <bool PACKED>
-cudaError_t launch_hist_ft(int ft, const HistArgs& args, dim3 grid, int cluster, size_t smem,
-                           cudaStream_t s) {
+const void* pick_hist(int ft, int fpl) {
+  if (fpl == 2) return hist_fn<32, 2, PACKED>();
   switch (ft) {
-    case 32: return launch_hist_t<32, PACKED>(args, grid, cluster, smem, s);
-    case 16: return launch_hist_t<16, PACKED>(args, grid, cluster, smem, s);
-    case 8: return launch_hist_t<8, PACKED>(args, grid, cluster, smem, s);
-    case 4: return launch_hist_t<4, PACKED>(args, grid, cluster, smem, s);
-    case 2: return launch_hist_t<2, PACKED>(args, grid, cluster, smem, s);
-    default: return launch_hist_t<1, PACKED>(args, grid, cluster, smem, s);
+    case 32: return hist_fn<32, 1, PACKED>();
+    case 16: return hist_fn<16, 1, PACKED>();
+    case 8: return hist_fn<8, 1, PACKED>();
+    case 4: return hist_fn<4, 1, PACKED>();
+    case 2: return hist_fn<2, 1, PACKED>();
+    default: return hist_fn<1, 1, PACKED>();
   }
 }
 
@@ -445,7 +548,7 @@ __global__ void __launch_bounds__(kSplitThreads) k_split(SplitLaunch a) {
 
 __global__ void k_bin(const float* __restrict__ x, uint64_t n, uint32_t nf,
                       const float* __restrict__ cuts, uint32_t nb1, uint8_t* __restrict__ bins,
-                      uint64_t ld, uint32_t f0, uint32_t fcount) {
+                      BinLayout lay, uint32_t f0, uint32_t fcount) {
   extern __shared__ float s_cuts[];
   for (uint32_t i = threadIdx.x; i < fcount * nb1; i += blockDim.x)
     s_cuts[i] = cuts[(size_t)f0 * nb1 + i];
@@ -461,20 +564,22 @@ __global__ void k_bin(const float* __restrict__ x, uint64_t n, uint32_t nf,
       if (c[mid] < v) lo = mid + 1;
       else hi = mid;
     }
-    bins[(size_t)(f0 + fl) * ld + r] = (uint8_t)lo;
+    bins[lay.offset(f0 + fl, r)] = (uint8_t)lo;
   }
 }
 
-__global__ void k_pack4(const uint8_t* __restrict__ bins, uint64_t n_pad, uint32_t nf,
-                        uint8_t* __restrict__ packed) {
-  const uint64_t half = n_pad / 2;
-  const uint64_t total = half * nf;
-  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+// 4-bit packing (src/gpu_kernels.rs:628-643): byte = bin(2k) | bin(2k+1) << 4 within each
+// feature row of each tile.
+__global__ void k_pack4(const uint8_t* __restrict__ bins, BinLayout lu, uint64_t n_pad,
+                        uint8_t* __restrict__ packed, BinLayout lp) {
+  const uint64_t pairs = n_pad / 2 * lu.nf;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < pairs;
        i += (uint64_t)gridDim.x * blockDim.x) {
-    const uint64_t f = i / half, k = i % half;
-    const uint8_t lo = bins[f * n_pad + 2 * k] & 0x0f;
-    const uint8_t hi = bins[f * n_pad + 2 * k + 1] & 0x0f;
-    packed[i] = (uint8_t)(lo | (hi << 4));
+    const uint32_t f = (uint32_t)(i % lu.nf);
+    const uint64_t r = (i / lu.nf) * 2;
+    const uint8_t lo = bins[lu.offset(f, r)] & 0x0f;
+    const uint8_t hi = bins[lu.offset(f, r + 1)] & 0x0f;
+    packed[lp.offset(f, r)] = (uint8_t)(lo | (hi << 4));
   }
 }
 
@@ -571,22 +676,21 @@ __global__ void k_quant(const float* __restrict__ g, const float* __restrict__ h
 // excluded flag; then either the next level's build slot (odd children keyed by the
 // parent when subtracting, else the node itself; -1 when excluded or not built), or, at
 // the last level, pred += leafval[leaf] (src/cpu.rs:319-320).
-__global__ void k_apply(const uint8_t* __restrict__ bins, uint64_t ld, int packed,
+__global__ void k_apply(const uint8_t* __restrict__ bins, BinLayout lay,
                         uint16_t* __restrict__ node, int16_t* __restrict__ slot,
                         const uint32_t* __restrict__ split_ft, uint64_t n4, int next_odd_only,
                         int final_level, const float* __restrict__ leafval, uint32_t leaf_base,
                         float* __restrict__ pred) {
   const uint32_t f = split_ft[0], t = split_ft[1];
-  const uint8_t* col = bins + (size_t)f * ld;
   for (uint64_t q = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; q < n4;
        q += (uint64_t)gridDim.x * blockDim.x) {
     const uint64_t r = q * 4;
     uint32_t b4;
-    if (packed) {
-      const uint32_t p = *reinterpret_cast<const uint16_t*>(col + (r >> 1));
+    if (lay.packed) {
+      const uint32_t p = *reinterpret_cast<const uint16_t*>(bins + lay.offset(f, r));
       b4 = (p & 0xfu) | ((p & 0xf0u) << 4) | ((p & 0xf00u) << 8) | ((p & 0xf000u) << 12);
     } else {
-      b4 = *reinterpret_cast<const uint32_t*>(col + r);
+      b4 = *reinterpret_cast<const uint32_t*>(bins + lay.offset(f, r));
     }
     uint2 nd2 = *reinterpret_cast<const uint2*>(node + r);
     uint32_t nds[4] = {nd2.x & 0xffffu, nd2.x >> 16, nd2.y & 0xffffu, nd2.y >> 16};
@@ -722,49 +826,187 @@ int grid_for(uint64_t work, int threads) {
 
 // ---------------------------------------------------------------------------------
 
+int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 1)
+      n = 148;
+  }
+  return n;
+}
+
+// Shared-memory plan of one histogram CTA: the histogram (8 bytes per cell, FT*FPL
+// features) plus dummy cells, plus two stages of (FT*FPL bins rows + 10 bytes of row
+// state) x tile rows. Prefers two features per lane at FT = 32 (per-row work shared by
+// both features), then one feature per lane with FT halving, then group chunks.
+struct HistPlan {
+  int ft, fpl;
+  uint32_t gchunk, tile, stride, stage_bytes, hist_bytes;
+  size_t smem;
+};
+
+HistPlan plan_hist(uint32_t nb, uint32_t groups, uint32_t nf, bool packed) {
+  const uint64_t budget = kSmemPerSm - 2048;
+  struct Cand {
+    int ft, fpl;
+  };
+  const Cand cands[] = {{32, 2}, {32, 1}, {16, 1}, {8, 1}, {4, 1}, {2, 1}, {1, 1}};
+  const uint32_t rs = (packed ? kBinTile / 2 : kBinTile) + 16;
+  for (uint32_t gchunk = groups; gchunk >= 1; gchunk = gchunk > 1 ? (gchunk + 1) / 2 : 0) {
+    for (const Cand& c : cands) {
+      if (c.fpl == 2 && nf <= 32) continue;
+      if (c.fpl == 1 && c.ft > 1 && (uint32_t)c.ft / 2 >= nf) continue;  // no idle tile lanes
+      const uint32_t ftt = (uint32_t)(c.ft * c.fpl);
+      const uint32_t stage = ftt * rs + 10u * kBinTile;
+      const uint64_t hist = 8ull * gchunk * nb * ftt;
+      if (hist + kStages * (uint64_t)stage <= budget) {
+        HistPlan p{};
+        p.ft = c.ft;
+        p.fpl = c.fpl;
+        p.gchunk = gchunk;
+        p.tile = kBinTile;
+        p.stride = rs;
+        p.stage_bytes = (stage + 127) / 128 * 128;
+        p.hist_bytes = (uint32_t)((hist + 127) / 128 * 128);
+        p.smem = p.hist_bytes + kStages * (size_t)p.stage_bytes;
+        return p;
+      }
+    }
+    if (gchunk == 1) break;
+  }
+  HistPlan none{};
+  return none;
+}
+
+// Occupancy of one histogram kernel configuration, queried once per (kernel, smem):
+// co-resident clusters for cluster sizes kMaxCluster, /2, ..., 1 (size 1 = CTAs).
+struct HistOcc {
+  int max_clusters[4];
+};
+
+// The kernel's dynamic shared memory limit only ever grows, so a launch that needs less
+// than an earlier one of the same kernel (another level, bin count or dataset) still fits.
+const HistOcc* hist_occupancy(const void* kfn, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::pair<std::pair<int, const void*>, size_t>, HistOcc> cache;
+  static std::map<std::pair<int, const void*>, size_t> smem_limit;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto kd = std::make_pair(dev, kfn);
+  size_t& lim = smem_limit[kd];
+  if (smem > lim) {
+    if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+      return nullptr;
+    lim = smem;
+  }
+  auto key = std::make_pair(kd, smem);
+  auto it = cache.find(key);
+  if (it != cache.end()) return &it->second;
+  HistOcc o{};
+  int per_sm = 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, kHistThreads, smem) !=
+          cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  for (int ci = 0, cl = kMaxCluster; cl >= 1; cl >>= 1, ci++) {
+    if (cl == 1) {
+      o.max_clusters[ci] = sm_count() * per_sm;
+      continue;
+    }
+    cudaLaunchConfig_t q = {};
+    q.gridDim = dim3(cl, 1, 1);
+    q.blockDim = dim3(kHistThreads);
+    q.dynamicSmemBytes = smem;
+    cudaLaunchAttribute qa[1];
+    qa[0].id = cudaLaunchAttributeClusterDimension;
+    qa[0].val.clusterDim.x = cl;
+    qa[0].val.clusterDim.y = 1;
+    qa[0].val.clusterDim.z = 1;
+    q.attrs = qa;
+    q.numAttrs = 1;
+    int maxc = 0;
+    if (cudaOccupancyMaxActiveClusters(&maxc, kfn, &q) != cudaSuccess) maxc = 0;
+    o.max_clusters[ci] = maxc;
+  }
+  return &(cache[key] = o);
+}
+
 cudaError_t launch_hist(const HistLaunch& L, cudaStream_t s, int* n_launch) {
-  // Feature-tile width FT and group chunk: the CTA's cells 8*G*nb*FT bytes must fit.
-  const uint64_t per_ft_group = 8ull * L.nb;
-  int ft = 32;
-  while (ft > 1 && per_ft_group * L.groups * (uint64_t)ft > (uint64_t)kHistSmemBudget) ft >>= 1;
-  uint32_t gchunk = L.groups;
-  while (gchunk > 1 && per_ft_group * gchunk * (uint64_t)ft > (uint64_t)kHistSmemBudget)
-    gchunk = (gchunk + 1) / 2;
-  while ((uint32_t)ft > 1 && (uint32_t)ft / 2 >= L.nf) ft >>= 1;  // no idle tile lanes
-  const uint32_t ftiles = (L.nf + ft - 1) / ft;
-  const uint32_t gz = (L.groups + gchunk - 1) / gchunk;
-  // Row chunks: whole multiples of kRowAlign rows, about two CTAs per SM in total,
-  // grouped into clusters of up to kMaxCluster CTAs along the row chunks.
-  const uint64_t units = L.n_pad / kRowAlign;
-  uint64_t rchunks = (units + 3) / 4;  // >= 8192 rows per CTA
-  uint64_t max_r = (uint64_t)kTargetCtas / ((uint64_t)ftiles * gz);
-  if (max_r < 1) max_r = 1;
-  if (rchunks > max_r) rchunks = max_r;
-  if (rchunks > units) rchunks = units;
-  if (rchunks < 1) rchunks = 1;
-  const uint64_t rows = (units + rchunks - 1) / rchunks * kRowAlign;
-  rchunks = (L.n_pad + rows - 1) / rows;
+  const HistPlan P = plan_hist(L.nb, L.groups, L.nf, L.lay.packed != 0);
+  if (P.smem == 0) return cudaErrorInvalidConfiguration;
+  const uint32_t ftt = (uint32_t)(P.ft * P.fpl);
+  const uint32_t ftiles = (L.nf + ftt - 1) / ftt;
+  const uint32_t gz = (L.groups + P.gchunk - 1) / P.gchunk;
+  const void* kfn =
+      L.lay.packed ? pick_hist<true>(P.ft, P.fpl) : pick_hist<false>(P.ft, P.fpl);
+  const HistOcc* occ = hist_occupancy(kfn, P.smem);
+  if (!occ) return cudaErrorInvalidConfiguration;
+  const uint64_t units = L.n_pad / P.tile;  // n_pad is a multiple of the tile
+  const uint64_t tiles_of = (uint64_t)ftiles * gz;
+  // One wave: pick the cluster size whose co-resident clusters (clusters must fit inside
+  // a GPC, so not every SM can host one) hold the most CTAs, then size the row chunks
+  // so that every (feature tile, group chunk) gets the same whole number of clusters.
+  uint64_t best_ctas = 0, rchunks = 1;
   int cluster = 1;
-  while (cluster * 2 <= kMaxCluster && (uint64_t)cluster * 2 <= rchunks) cluster *= 2;
-  rchunks = (rchunks + cluster - 1) / cluster * cluster;
+  for (int ci = 0, cl = kMaxCluster; cl >= 1; cl >>= 1, ci++) {
+    const int maxc = occ->max_clusters[ci];
+    if (maxc < 1) continue;
+    uint64_t per_tile = (uint64_t)maxc / tiles_of;  // clusters per (feature tile, group)
+    if (per_tile < 1) per_tile = 1;
+    uint64_t rc = per_tile * (uint64_t)cl;
+    if (rc > units) rc = units / cl * cl;
+    if (rc < (uint64_t)cl) continue;
+    const uint64_t ctas = rc * tiles_of;
+    if (ctas > best_ctas + best_ctas / 16) {  // larger clusters unless they cost >6% of CTAs
+      best_ctas = ctas;
+      rchunks = rc;
+      cluster = cl;
+    }
+  }
+  // No CTA accumulates more than kMaxRowsPerCta rows (larger inputs take more waves).
+  constexpr uint64_t kMaxTiles = kMaxRowsPerCta / kBinTile;
+  if ((units + rchunks - 1) / rchunks > kMaxTiles) {
+    rchunks = (units + kMaxTiles - 1) / kMaxTiles;
+    rchunks = (rchunks + cluster - 1) / cluster * cluster;
+  }
+  const uint64_t tiles_per = (units + rchunks - 1) / rchunks;
+  const uint64_t rows = tiles_per * P.tile;
 
   HistArgs a;
   a.bins = L.bins;
-  a.ld = L.ld;
+  a.lay = L.lay;
   a.slot = L.slot;
   a.qg = L.qg;
   a.qh = L.qh;
   a.n_pad = L.n_pad;
   a.nf = L.nf;
   a.nb = L.nb;
-  a.gchunk = gchunk;
+  a.gchunk = P.gchunk;
   a.out = L.out;
+  a.err = L.err;
   a.rows_per_cta = rows;
-  const size_t smem = 8ull * gchunk * L.nb * (uint64_t)ft;
+  a.stage_bytes = P.stage_bytes;
+  a.hist_bytes = P.hist_bytes;
   dim3 grid((unsigned)rchunks, ftiles, gz);
   if (n_launch) (*n_launch)++;
-  return L.packed ? launch_hist_ft<true>(ft, a, grid, cluster, smem, s)
-                  : launch_hist_ft<false>(ft, a, grid, cluster, smem, s);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kHistThreads);
+  cfg.dynamicSmemBytes = P.smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void* args[] = {&a};
+  return cudaLaunchKernelExC(&cfg, kfn, args);
 }
 
 cudaError_t launch_split(const SplitLaunch& a, cudaStream_t s) {
@@ -777,14 +1019,15 @@ cudaError_t launch_split(const SplitLaunch& a, cudaStream_t s) {
 }
 
 cudaError_t launch_bin(const float* x, uint64_t n, uint32_t nf, const float* d_cuts,
-                       uint32_t n_bins, uint8_t* d_bins, uint64_t ld, cudaStream_t s, int* nl) {
+                       uint32_t n_bins, uint8_t* d_bins, const BinLayout& lay, cudaStream_t s,
+                       int* nl) {
   const uint32_t nb1 = n_bins - 1;
   const uint32_t per = (48 * 1024) / (4 * (nb1 ? nb1 : 1));
   const uint32_t ftile = per < 1 ? 1 : (per > nf ? nf : per);
   for (uint32_t f0 = 0; f0 < nf; f0 += ftile) {
     const uint32_t fc = nf - f0 < ftile ? nf - f0 : ftile;
     const unsigned blocks = (unsigned)((n + 255) / 256);
-    k_bin<<<blocks, 256, (size_t)fc * nb1 * 4, s>>>(x, n, nf, d_cuts, nb1, d_bins, ld, f0, fc);
+    k_bin<<<blocks, 256, (size_t)fc * nb1 * 4, s>>>(x, n, nf, d_cuts, nb1, d_bins, lay, f0, fc);
     if (nl) (*nl)++;
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
@@ -792,9 +1035,10 @@ cudaError_t launch_bin(const float* x, uint64_t n, uint32_t nf, const float* d_c
   return cudaSuccess;
 }
 
-cudaError_t launch_pack4(const uint8_t* d_bins, uint64_t n_pad, uint32_t nf, uint8_t* d_packed,
-                         cudaStream_t s, int* nl) {
-  k_pack4<<<grid_for(n_pad / 2 * nf, 256), 256, 0, s>>>(d_bins, n_pad, nf, d_packed);
+cudaError_t launch_pack4(const uint8_t* d_bins, const BinLayout& lay_u8, uint64_t n_pad,
+                         uint8_t* d_packed, const BinLayout& lay_p, cudaStream_t s, int* nl) {
+  k_pack4<<<grid_for(n_pad / 2 * lay_u8.nf, 256), 256, 0, s>>>(d_bins, lay_u8, n_pad, d_packed,
+                                                               lay_p);
   if (nl) (*nl)++;
   return cudaGetLastError();
 }
@@ -818,13 +1062,13 @@ cudaError_t launch_quant(const float* g, const float* h, const uint32_t* maxbits
   return cudaGetLastError();
 }
 
-cudaError_t launch_apply(const uint8_t* bins, uint64_t ld, int packed, uint16_t* node,
+cudaError_t launch_apply(const uint8_t* bins, const BinLayout& lay, uint16_t* node,
                          int16_t* slot, const uint32_t* split_ft, uint64_t n_pad,
                          int next_odd_only, int final_level, const float* leafval,
                          uint32_t leaf_base, float* pred, cudaStream_t s, int* nl) {
   const uint64_t n4 = n_pad / 4;
-  k_apply<<<grid_for(n4, 256), 256, 0, s>>>(bins, ld, packed, node, slot, split_ft, n4,
-                                             next_odd_only, final_level, leafval, leaf_base, pred);
+  k_apply<<<grid_for(n4, 256), 256, 0, s>>>(bins, lay, node, slot, split_ft, n4, next_odd_only,
+                                             final_level, leafval, leaf_base, pred);
   if (nl) (*nl)++;
   return cudaGetLastError();
 }

@@ -21,6 +21,7 @@ _libm.expf.argtypes = [ctypes.c_float]
 _libm.expf.restype = ctypes.c_float
 
 F32 = np.float32
+QBITS = 17  # RW_QBITS in rustwood_b200/csrc/rw_expf.h
 
 
 def f32(v) -> np.float32:
@@ -66,7 +67,7 @@ def qscale_exp(m: np.float32) -> int:
     if bits & 0x7FFFFFFF == 0:
         return 0
     biased = (bits >> 23) & 0xFF
-    e = 26 - ((1 if biased == 0 else biased) - 126)
+    e = QBITS - ((1 if biased == 0 else biased) - 126)
     return max(-126, min(100, e))
 
 

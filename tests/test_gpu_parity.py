@@ -101,7 +101,9 @@ def test_level_hist_matches_oracle(ctx, nf, nb, groups, odd, packed):
     node[rng.random(n) < 0.1] = -1
     g = rng.normal(0, 1, n).astype(np.float32)
     h = rng.uniform(1e-6, 0.25, n).astype(np.float32)
-    e_g, e_h = 24, 28
+    # scales as the trainer picks them (|q| <= 2^RW_QBITS, RW_QBITS = 17)
+    e_g = 17 - int(np.frexp(np.abs(g).max())[1])
+    e_h = 17 - int(np.frexp(h.max())[1])
     got = np.zeros((groups, nf, nb, 2), np.int64)
     ctx.check(N.lib.rw_debug_level_hist(ds.h, N.ptr(node), N.ptr(g), N.ptr(h), e_g, e_h, groups,
                                         odd, N.ptr(got)))
