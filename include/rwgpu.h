@@ -115,6 +115,8 @@ int rw_ctx_create(const int* gpu_ids, int n_gpus, rw_ctx** out);
  * rw_nccl_unique_id and broadcast out of band. With world == 1, id may be NULL. */
 int rw_ctx_create_rank(int gpu_id, int rank, int world, const void* nccl_id, rw_ctx** out);
 int rw_nccl_unique_id(void* out128);
+/* Destroys the context; its datasets and uploaded models must be destroyed first (they
+ * live in the context's memory pool). */
 void rw_ctx_destroy(rw_ctx* ctx);
 const char* rw_last_error(const rw_ctx* ctx);
 /* The context's CUDA stream (a cudaStream_t), for callers that order their own work

@@ -16,38 +16,23 @@ struct rw_ctx {
   int rank = 0;
   int world = 1;
   cudaStream_t stream = nullptr;
+  // Stream-ordered pool for datasets and working buffers; it keeps freed memory, so
+  // repeated fits (rw_fit, a serving loop) allocate without device synchronisation.
+  cudaMemPool_t pool = nullptr;
   ncclComm_t comm = nullptr;
   int64_t timeout_ms = 60000;
   std::string last_error;
   uint64_t launches = 0;  // kernels launched on this context (all time)
 };
 
-// Bins in HBM are stored column-major in tiles of kBinTile rows: tile t holds rows
-// [t*kBinTile, +kBinTile) and, inside it, feature f's bins form one row of `rs` bytes
-// (kBinTile u8, or kBinTile/2 bytes of 4-bit pairs, plus 16 bytes of padding). A feature
-// slice of a tile is therefore one contiguous block (one TMA bulk copy), and the padding
-// (an odd number of 16-byte units) keeps 16-byte shared-memory reads of consecutive
-// features on distinct banks.
-constexpr uint32_t kBinTile = 512;
-
-struct BinLayout {
-  uint32_t nf = 0;
-  uint32_t rs = 0;          // bytes per feature row within a tile
-  uint64_t tile_bytes = 0;  // nf * rs
-  int packed = 0;
-  __host__ __device__ uint64_t offset(uint32_t f, uint64_t r) const {
-    const uint64_t in = r % kBinTile;
-    return (r / kBinTile) * tile_bytes + (uint64_t)f * rs + (packed ? in / 2 : in);
-  }
-  static BinLayout make(uint32_t nf, int packed) {
-    BinLayout L;
-    L.nf = nf;
-    L.packed = packed;
-    L.rs = (packed ? kBinTile / 2 : kBinTile) + 16;
-    L.tile_bytes = (uint64_t)nf * L.rs;
-    return L;
-  }
-};
+// Bins are stored twice in HBM:
+//   colbins  feature-major u8 [nf][n_pad]: the split feature's column read by the leaf-index
+//            update, and the host-visible copy;
+//   rowbins  tile-major [ftiles][n_pad][tile bytes]: features in tiles of kHistFeat, each
+//            row's tile t is one contiguous run of kHistFeat bytes (u8) or kHistFeat/2 bytes
+//            (4-bit pairs, the even feature in the low nibble), so the histogram build
+//            gathers a row's tile in one access and streams a tile's rows sequentially.
+constexpr uint32_t kHistFeat = 64;
 
 struct rw_dataset {
   rw_ctx* ctx = nullptr;
@@ -57,11 +42,11 @@ struct rw_dataset {
   uint64_t row_offset = 0;
   uint32_t nf = 0, n_bins = 0;
   int packed = 0;
-  BinLayout lay;                // layout of d_bins
-  uint8_t* d_bins = nullptr;    // row-tiled column-major (u8 or 4-bit packed), see BinLayout
-  uint8_t* d_bins_u8 = nullptr; // u8 copy (row-tiled) kept only when packed
-  float* d_y = nullptr;         // [n_pad]
-  float* d_cuts = nullptr;      // [nf][n_bins-1]
+  uint32_t ftiles = 0;           // ceil(nf / kHistFeat)
+  uint8_t* d_colbins = nullptr;  // u8 [nf][n_pad]
+  uint8_t* d_rowbins = nullptr;  // [ftiles][n_pad][tile bytes], u8 or 4-bit pairs
+  float* d_y = nullptr;          // [n_pad]
+  float* d_cuts = nullptr;       // [nf][n_bins-1]
   std::vector<float> cuts;
   // Working buffers of the boosting loop, kept across fits (named, grown on demand).
   std::map<std::string, std::pair<void*, size_t>> ws;
@@ -80,19 +65,41 @@ struct rw_dmodel {
 
 // ---- kernel launchers (train_kernels.cu) ------------------------------------------
 
+// One level's histogram build. The rows to accumulate form a list grouped by histogram
+// group: group k's rows are rows[seg[k] .. seg[k+1]). Without a list, every row in
+// [0, n_ident) belongs to group 0.
 struct HistLaunch {
-  const uint8_t* bins;
-  BinLayout lay;
-  const int16_t* slot;   // per row: histogram group this level builds into, or -1
-  const int32_t* qg;     // per row: fixed-point g (rw_quantize)
-  const int32_t* qh;     // per row: fixed-point h
-  uint64_t n_pad;        // multiple of kRowAlign
+  const uint8_t* rowbins;
+  uint64_t n_pad;         // rows per tile in rowbins
+  int packed;
+  const int2* q;          // per row: (fixed-point g, fixed-point h), rw_quantize
+  const uint32_t* rows;   // row list, or nullptr for the identity list
+  const uint32_t* seg;    // [groups + 1] list offsets (nullptr with the identity list)
+  uint32_t n_ident;       // identity list length, a multiple of 128 (rows past n have q = 0)
+  uint32_t groups;        // histogram groups written (out has `groups` slots)
   uint32_t nf, nb;
-  uint32_t groups;       // histogram groups written (out has `groups` slots)
-  long long* out;        // int64 [groups][nf][nb][2], zeroed by the caller
-  int* err;              // set to a nonzero code if a bounded wait gave up
+  long long* out;         // int64 [groups][nf][nb][2], zeroed by the caller
+  int* err;               // nullable: set to 1 if a bounded wait on a bulk copy gave up
 };
 cudaError_t launch_hist(const HistLaunch& a, cudaStream_t s, int* n_launch);
+
+// Per-level row lists: after a level's leaf-index update, the rows of the children that
+// the next level builds, grouped by histogram group.
+struct RowLists {
+  uint32_t* cnt;        // [2^D] rows per child node (non-excluded), counted by k_apply
+  uint32_t* cursor;     // [2^D] per-group scatter cursors
+  uint32_t* seg;        // [2^D + 1] list offsets per group
+  uint8_t* built_odd;   // [2^(D-1)] per node pair: 1 if the odd child's histogram is built
+  uint32_t* rows;       // [n_pad] the list
+};
+
+// A feature's best split at one level: gain (-inf when no bin is feasible), threshold
+// bin and its cut value.
+struct SplitRec {
+  double gain;
+  uint32_t bin;
+  float thr;
+};
 
 struct SplitLaunch {
   const long long* hb;  // built histogram
@@ -101,53 +108,76 @@ struct SplitLaunch {
   long long* hb_next;   // built-histogram buffer of the next level, zeroed here (nullable)
   uint64_t hb_next_words;
   uint32_t n_nodes, nf, nb;
-  int mode;             // 0: hb holds every node; 1: hb holds odd nodes keyed by parent
+  int mode;             // 0: hb holds every node; 1: hb holds one child per pair, keyed by parent
+  const uint8_t* built_odd;  // mode 1: per pair, 1 if the odd child was built (else the even)
+  uint32_t* zero_u32;   // nullable: zero_words u32 zeroed here (next level's list counters)
+  uint32_t zero_words;
   const uint32_t* maxbits;
   double lambda, min_child, lr;
   const int32_t* monotone;  // device [nf] or null
+  long long* mono;      // with monotone: [nf][nb-1][4] exact left/right sums, zero on entry
+  double* term;         // [nf][n_nodes][nb-1] per-node gain terms
+  long long* prefix;    // last level: [nf][n_nodes][nb][2] exact per-node bin prefixes (g, h)
   float colsample;
   uint32_t tree_seed;
-  double* best_gain;
-  uint32_t* best_bin;
-  uint32_t* counter;
   const float* cuts;
-  uint32_t* feat;
-  float* thr;
-  uint16_t* thr_bin;
-  uint32_t* split_ft;
-  float* fi_gain;
-  float* fi_count;
-  uint32_t slot;
+  SplitRec* rec;        // [nf] out
   int last_level;
-  float* leafval;
-  uint32_t leaf_base;
+  float* leafc;         // last level: [nf][2 * n_nodes] leaf values per candidate feature
 };
-cudaError_t launch_split(const SplitLaunch& a, cudaStream_t s);
+cudaError_t launch_split(const SplitLaunch& a, cudaStream_t s, int* nl);
 
-// Rows are padded to a multiple of kRowAlign so every histogram CTA's row range is a
-// whole number of steps for every lane.
+// Rows are padded to a multiple of kRowAlign (whole 4-row steps for every kernel).
 constexpr uint64_t kRowAlign = 4096;
 
+// Bins both layouts (colbins u8; rowbins u8, packed to 4-bit pairs by launch_pack4).
 cudaError_t launch_bin(const float* x_rowmajor, uint64_t n, uint32_t nf, const float* d_cuts,
-                       uint32_t n_bins, uint8_t* d_bins, const BinLayout& lay, cudaStream_t s,
-                       int* nl);
-cudaError_t launch_pack4(const uint8_t* d_bins, const BinLayout& lay_u8, uint64_t n_pad,
-                         uint8_t* d_packed, const BinLayout& lay_p, cudaStream_t s, int* nl);
+                       uint32_t n_bins, uint64_t n_pad, uint8_t* d_colbins, uint8_t* d_rowbins,
+                       cudaStream_t s, int* nl);
+// rowbins u8 -> 4-bit pairs (separate buffers).
+cudaError_t launch_pack4(const uint8_t* d_u8, uint64_t n_pad, uint32_t nf, uint8_t* d_packed,
+                         cudaStream_t s, int* nl);
 cudaError_t launch_grad(const float* pred, const float* y, float* g, float* h, uint64_t n,
                         uint64_t n_pad, int logistic, uint64_t stride, uint64_t phase,
                         uint64_t row_offset, int compute_max, uint32_t* maxbits,
                         cudaStream_t s, int* nl);
-// Per round: fixed-point q, the excluded flag (bit 15 of node) and level-0 slots; also
-// zeroes the level-0 built histogram (hb0_words int64).
+// Per round: fixed-point q = (qg, qh), the excluded flag (bit 15 of node) and node reset;
+// also zeroes the level-0 built histogram (hb0_words int64).
 cudaError_t launch_quant(const float* g, const float* h, const uint32_t* maxbits, uint64_t n_pad,
-                         int32_t* qg, int32_t* qh, uint16_t* node, int16_t* slot,
-                         long long* hb0, uint64_t hb0_words, cudaStream_t s, int* nl);
-// leaf = 2*leaf + (bin > t) keeping the excluded flag; writes the next level's build
-// slot (next_odd_only: odd children keyed by parent), or at the final level updates pred.
-cudaError_t launch_apply(const uint8_t* bins, const BinLayout& lay, uint16_t* node,
-                         int16_t* slot, const uint32_t* split_ft, uint64_t n_pad,
-                         int next_odd_only, int final_level, const float* leafval,
-                         uint32_t leaf_base, float* pred, cudaStream_t s, int* nl);
+                         int2* q, uint16_t* node, long long* hb0, uint64_t hb0_words,
+                         cudaStream_t s, int* nl);
+// The level's split (argmax over the per-feature records) and model slot, then
+// leaf = 2*leaf + (bin > t) keeping the excluded flag; counts the rows of every child
+// (cnt, non-final levels), or at the final level writes the leaf values and updates pred.
+struct ApplyLaunch {
+  const uint8_t* colbins;
+  uint64_t n_pad;
+  uint16_t* node;
+  const SplitRec* rec;
+  uint32_t nf;
+  uint32_t n_children;
+  uint32_t* cnt;
+  int final_level;
+  const float* leafc;  // final level: [nf][n_leaves]
+  uint32_t n_leaves;
+  float* pred;
+  uint32_t* feat;
+  float* thr;
+  uint16_t* thr_bin;
+  float* fi_gain;
+  float* fi_count;
+  uint32_t slot;
+  float* leafval;
+  uint32_t leaf_base;
+  uint32_t* split_out;  // nullable: (feature, bin) of the chosen split
+};
+cudaError_t launch_apply(const ApplyLaunch& a, cudaStream_t s, int* nl);
+// The next level's row list from the child counts: with subtraction, per pair the child
+// with fewer rows is built (the odd one on ties, or always when force_odd), grouped by
+// pair; without, every child is its own group.
+cudaError_t launch_rowlist(const uint16_t* node, uint64_t n_pad, uint32_t n_children,
+                           int subtract, int force_odd, const RowLists& rl, cudaStream_t s,
+                           int* nl);
 cudaError_t launch_fill_f32(float* p, float v, uint64_t n, cudaStream_t s, int* nl);
 
 // GOSS: exact k-th largest |g| by radix selection (4 passes of 8-bit digits).

@@ -47,20 +47,37 @@ int cuda_fail(rw_ctx* ctx, cudaError_t e, const char* what) {
       return fail((ctx), RW_ERR_NCCL, std::string(#expr) + ": " + ncclGetErrorString(_r)); \
   } while (0)
 
-// Device allocation owned by a scope.
+// Stream-ordered allocation from the context's pool (ordered on the context stream).
+cudaError_t pool_alloc(rw_ctx* ctx, void** p, size_t bytes) {
+  return cudaMallocFromPoolAsync(p, std::max<size_t>(bytes, 1), ctx->pool, ctx->stream);
+}
+void pool_free(rw_ctx* ctx, void* p) {
+  if (p) cudaFreeAsync(p, ctx->stream);
+}
+
+// Device allocation owned by a scope: from the context's pool (alloc(ctx, n), freed in
+// stream order) or plain cudaMalloc (alloc(n)).
 template <typename T>
 struct DBuf {
   T* p = nullptr;
   size_t n = 0;
+  rw_ctx* pool_ctx = nullptr;
   DBuf() = default;
   DBuf(const DBuf&) = delete;
   DBuf& operator=(const DBuf&) = delete;
   ~DBuf() {
-    if (p) cudaFree(p);
+    if (!p) return;
+    if (pool_ctx) pool_free(pool_ctx, p);
+    else cudaFree(p);
   }
   cudaError_t alloc(size_t count) {
     n = count;
     return cudaMalloc(reinterpret_cast<void**>(&p), std::max<size_t>(count, 1) * sizeof(T));
+  }
+  cudaError_t alloc(rw_ctx* ctx, size_t count) {
+    n = count;
+    pool_ctx = ctx;
+    return pool_alloc(ctx, reinterpret_cast<void**>(&p), count * sizeof(T));
   }
   T* release() {
     T* q = p;
@@ -83,11 +100,11 @@ struct WsBuf {
       return cudaSuccess;
     }
     if (it != ds->ws.end()) {
-      cudaFree(it->second.first);
+      pool_free(ds->ctx, it->second.first);
       ds->ws.erase(it);
     }
     void* q = nullptr;
-    cudaError_t e = cudaMalloc(&q, bytes);
+    cudaError_t e = pool_alloc(ds->ctx, &q, bytes);
     if (e != cudaSuccess) return e;
     ds->ws[name] = {q, bytes};
     p = static_cast<T*>(q);
@@ -212,8 +229,20 @@ extern "C" int rw_ctx_create_rank(int gpu_id, int rank, int world, const void* n
   ctx->world = world;
   e = cudaSetDevice(gpu_id);
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) {
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = gpu_id;
+    e = cudaMemPoolCreate(&ctx->pool, &props);
+    uint64_t keep = UINT64_MAX;
+    if (e == cudaSuccess)
+      e = cudaMemPoolSetAttribute(ctx->pool, cudaMemPoolAttrReleaseThreshold, &keep);
+  }
   if (e != cudaSuccess) {
     int rc = cuda_fail(nullptr, e, "context setup");
+    if (ctx->stream) cudaStreamDestroy(ctx->stream);
+    if (ctx->pool) cudaMemPoolDestroy(ctx->pool);
     delete ctx;
     return rc;
   }
@@ -246,6 +275,7 @@ extern "C" int rw_ctx_create_rank(int gpu_id, int rank, int world, const void* n
     if (r != ncclSuccess) {
       if (ctx->comm) ncclCommAbort(ctx->comm);
       cudaStreamDestroy(ctx->stream);
+      cudaMemPoolDestroy(ctx->pool);
       delete ctx;
       return fail(nullptr, RW_ERR_NCCL,
                   std::string("NCCL communicator init failed: ") + ncclGetErrorString(r));
@@ -261,6 +291,7 @@ extern "C" void rw_ctx_destroy(rw_ctx* ctx) {
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   if (ctx->comm) ncclCommDestroy(ctx->comm);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
+  if (ctx->pool) cudaMemPoolDestroy(ctx->pool);
   delete ctx;
 }
 
@@ -293,16 +324,18 @@ static int dataset_build(rw_ctx* ctx, const float* d_x, const float* y, bool y_o
   ds->nf = nf;
   ds->n_bins = n_bins;
   ds->packed = (pack4 && n_bins <= 16) ? 1 : 0;
+  ds->ftiles = (nf + kHistFeat - 1) / kHistFeat;
+  const uint32_t rb_u8 = ds->ftiles * kHistFeat;  // u8 row-bin bytes per row (all tiles)
   ds->cuts.assign(cuts, cuts + (size_t)nf * (n_bins - 1));
   cudaStream_t s = ctx->stream;
-  const BinLayout lay_u8 = BinLayout::make(nf, 0);
-  const size_t u8_bytes = (size_t)(ds->n_pad / kBinTile) * lay_u8.tile_bytes;
-  DBuf<uint8_t> bins;
+  const size_t col_bytes = (size_t)nf * ds->n_pad, row_u8_bytes = (size_t)rb_u8 * ds->n_pad;
+  DBuf<uint8_t> colb, rowb;
   DBuf<float> dy, dc;
-  cudaError_t e = bins.alloc(u8_bytes);
-  if (e == cudaSuccess) e = dy.alloc(ds->n_pad);
-  if (e == cudaSuccess) e = dc.alloc(ds->cuts.size());
-  if (e == cudaSuccess) e = cudaMemsetAsync(bins.p, 0, u8_bytes, s);
+  cudaError_t e = colb.alloc(ctx, col_bytes);
+  if (e == cudaSuccess) e = rowb.alloc(ctx, row_u8_bytes);
+  if (e == cudaSuccess) e = dy.alloc(ctx, ds->n_pad);
+  if (e == cudaSuccess) e = dc.alloc(ctx, ds->cuts.size());
+  if (e == cudaSuccess) e = cudaMemsetAsync(colb.p, 0, col_bytes, s);
   if (e == cudaSuccess) e = cudaMemsetAsync(dy.p, 0, ds->n_pad * sizeof(float), s);
   if (e == cudaSuccess)
     e = cudaMemcpyAsync(dc.p, ds->cuts.data(), ds->cuts.size() * sizeof(float),
@@ -310,29 +343,24 @@ static int dataset_build(rw_ctx* ctx, const float* d_x, const float* y, bool y_o
   if (e == cudaSuccess)
     e = cudaMemcpyAsync(dy.p, y, n * sizeof(float),
                         y_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s);
-  if (e == cudaSuccess) e = launch_bin(d_x, n, nf, dc.p, n_bins, bins.p, lay_u8, s, &nl);
+  if (e == cudaSuccess)
+    e = launch_bin(d_x, n, nf, dc.p, n_bins, ds->n_pad, colb.p, rowb.p, s, &nl);
   if (e == cudaSuccess && ds->packed) {
-    const BinLayout lay_p = BinLayout::make(nf, 1);
-    const size_t p_bytes = (size_t)(ds->n_pad / kBinTile) * lay_p.tile_bytes;
     DBuf<uint8_t> packed;
-    e = packed.alloc(p_bytes);
-    if (e == cudaSuccess) e = cudaMemsetAsync(packed.p, 0, p_bytes, s);
-    if (e == cudaSuccess) e = launch_pack4(bins.p, lay_u8, ds->n_pad, packed.p, lay_p, s, &nl);
-    if (e == cudaSuccess) {
-      ds->d_bins_u8 = bins.release();
-      ds->d_bins = packed.release();
-      ds->lay = lay_p;
-    }
+    e = packed.alloc(ctx, (size_t)(rb_u8 / 2) * ds->n_pad);
+    if (e == cudaSuccess) e = launch_pack4(rowb.p, ds->n_pad, nf, packed.p, s, &nl);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);  // before the u8 rows are freed
+    if (e == cudaSuccess) ds->d_rowbins = packed.release();
   } else if (e == cudaSuccess) {
-    ds->d_bins = bins.release();
-    ds->lay = lay_u8;
+    ds->d_rowbins = rowb.release();
   }
+  if (e == cudaSuccess) ds->d_colbins = colb.release();
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
   ctx->launches += nl;
   if (e != cudaSuccess) {
     int rc = cuda_fail(ctx, e, "dataset upload/binning");
-    if (ds->d_bins) cudaFree(ds->d_bins);
-    if (ds->d_bins_u8) cudaFree(ds->d_bins_u8);
+    pool_free(ctx, ds->d_colbins);
+    pool_free(ctx, ds->d_rowbins);
     delete ds;
     return rc;
   }
@@ -363,7 +391,7 @@ extern "C" int rw_dataset_create(rw_ctx* ctx, const float* x, const float* y, ui
   *out = nullptr;
   RW_CU(ctx, cudaSetDevice(ctx->device));
   DBuf<float> dx;
-  RW_CU(ctx, dx.alloc((size_t)n * nf));
+  RW_CU(ctx, dx.alloc(ctx, (size_t)n * nf));
   RW_CU(ctx, cudaMemcpyAsync(dx.p, x, (size_t)n * nf * sizeof(float), cudaMemcpyHostToDevice,
                              ctx->stream));
   return dataset_build(ctx, dx.p, y, false, n, nf, cuts, n_bins, pack4, n_global, row_offset,
@@ -385,11 +413,12 @@ extern "C" int rw_dataset_create_device(rw_ctx* ctx, const float* d_x, const flo
 extern "C" void rw_dataset_destroy(rw_dataset* ds) {
   if (!ds) return;
   cudaSetDevice(ds->ctx->device);
-  cudaFree(ds->d_bins);
-  if (ds->d_bins_u8) cudaFree(ds->d_bins_u8);
-  cudaFree(ds->d_y);
-  cudaFree(ds->d_cuts);
-  for (auto& kv : ds->ws) cudaFree(kv.second.first);
+  rw_ctx* ctx = ds->ctx;
+  pool_free(ctx, ds->d_colbins);
+  pool_free(ctx, ds->d_rowbins);
+  pool_free(ctx, ds->d_y);
+  pool_free(ctx, ds->d_cuts);
+  for (auto& kv : ds->ws) pool_free(ctx, kv.second.first);
   delete ds;
 }
 
@@ -397,18 +426,9 @@ extern "C" int rw_dataset_bins(const rw_dataset* ds, uint8_t* out) {
   if (!ds || !out) return fail(nullptr, RW_ERR_ARG, "NULL argument");
   rw_ctx* ctx = ds->ctx;
   RW_CU(ctx, cudaSetDevice(ctx->device));
-  // Device bins are row-tiled (BinLayout); the host copy is feature-major [nf][n].
-  const uint8_t* src = ds->packed ? ds->d_bins_u8 : ds->d_bins;
-  const BinLayout lay = BinLayout::make(ds->nf, 0);
-  std::vector<uint8_t> tiled((size_t)(ds->n_pad / kBinTile) * lay.tile_bytes);
-  RW_CU(ctx, cudaMemcpyAsync(tiled.data(), src, tiled.size(), cudaMemcpyDeviceToHost,
-                             ctx->stream));
+  RW_CU(ctx, cudaMemcpy2DAsync(out, ds->n, ds->d_colbins, ds->n_pad, ds->n, ds->nf,
+                               cudaMemcpyDeviceToHost, ctx->stream));
   RW_CU(ctx, cudaStreamSynchronize(ctx->stream));
-  for (uint32_t f = 0; f < ds->nf; f++)
-    for (uint64_t r0 = 0; r0 < ds->n; r0 += kBinTile) {
-      const uint64_t len = std::min<uint64_t>(kBinTile, ds->n - r0);
-      std::memcpy(out + (size_t)f * ds->n + r0, tiled.data() + lay.offset(f, r0), len);
-    }
   return RW_OK;
 }
 
@@ -441,7 +461,8 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
     stride = sd >= 1.8446744073709552e19 ? UINT64_MAX : (uint64_t)sd;
   }
 
-  const uint64_t cell = (uint64_t)nf * nb * 2;  // int64 words per histogram node
+  // int64 words per histogram node: [tile][bin][g|h][kHistFeat columns]
+  const uint64_t cell = (uint64_t)ds->ftiles * nb * 2 * kHistFeat;
   const uint64_t hb_groups = subtract ? std::max<uint64_t>(1, D >= 2 ? (1ull << (D - 2)) : 1)
                                       : (1ull << (D - 1));
   const uint64_t hf_nodes = 1ull << (D - 1);
@@ -449,11 +470,15 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
   // Working buffers live in the dataset's cache: repeated fits allocate nothing.
   WsBuf<float> pred, g, h, d_leafval, d_thr, d_fi_gain, d_fi_count;
   WsBuf<uint16_t> node, d_thr_bin;
-  WsBuf<int16_t> slot;
-  WsBuf<int32_t> qg, qh;
+  WsBuf<int2> q;
+  WsBuf<uint32_t> rl_rows, rl_counters, rl_seg;
+  WsBuf<uint8_t> rl_odd;
   WsBuf<long long> hb0, hb1, hf0, hf1;
-  WsBuf<uint32_t> d_feat, maxbits, best_bin, counter, split_ft;
-  WsBuf<double> best_gain;
+  WsBuf<uint32_t> d_feat, maxbits;
+  WsBuf<SplitRec> rec;
+  WsBuf<float> leafc;
+  WsBuf<double> term;
+  WsBuf<long long> mono_sums;
   WsBuf<int32_t> d_mono;
   WsBuf<unsigned long long> goss_counts;
   WsBuf<uint32_t> goss_sel;
@@ -461,9 +486,11 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
   RW_CU(ctx, g.get(ds, "g", n_pad));
   RW_CU(ctx, h.get(ds, "h", n_pad));
   RW_CU(ctx, node.get(ds, "node", n_pad));
-  RW_CU(ctx, slot.get(ds, "slot", n_pad));
-  RW_CU(ctx, qg.get(ds, "qg", n_pad));
-  RW_CU(ctx, qh.get(ds, "qh", n_pad));
+  RW_CU(ctx, q.get(ds, "q", n_pad));
+  RW_CU(ctx, rl_rows.get(ds, "rl_rows", n_pad));
+  RW_CU(ctx, rl_counters.get(ds, "rl_counters", 2 * (size_t)NL));  // [cnt: NL][cursor: NL]
+  RW_CU(ctx, rl_seg.get(ds, "rl_seg", (size_t)NL + 1));
+  RW_CU(ctx, rl_odd.get(ds, "rl_odd", (size_t)NL / 2));
   RW_CU(ctx, hb0.get(ds, "hb0", hb_groups * cell));
   RW_CU(ctx, hb1.get(ds, "hb1", hb_groups * cell));
   RW_CU(ctx, hf0.get(ds, "hf0", hf_nodes * cell));
@@ -475,21 +502,20 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
   RW_CU(ctx, d_fi_gain.get(ds, "fi_gain", nf));
   RW_CU(ctx, d_fi_count.get(ds, "fi_count", nf));
   RW_CU(ctx, maxbits.get(ds, "maxbits", (size_t)std::max<uint32_t>(T, 1) * 2));
-  RW_CU(ctx, best_gain.get(ds, "best_gain", nf));
-  RW_CU(ctx, best_bin.get(ds, "best_bin", nf));
-  RW_CU(ctx, counter.get(ds, "counter", 1));
-  RW_CU(ctx, split_ft.get(ds, "split_ft", 2));
   WsBuf<int> kerr;
   RW_CU(ctx, kerr.get(ds, "kernel_err", 1));
   RW_CU(ctx, cudaMemsetAsync(kerr.p, 0, sizeof(int), s));
+  RW_CU(ctx, rec.get(ds, "split_rec", nf));
+  RW_CU(ctx, leafc.get(ds, "leaf_cand", (size_t)nf * NL));
+  RW_CU(ctx, term.get(ds, "gain_terms", (size_t)nf * (NL / 2) * (nb - 1)));
+  WsBuf<long long> prefix;
+  RW_CU(ctx, prefix.get(ds, "leaf_prefix", (size_t)nf * (NL / 2) * nb * 2));
   RW_CU(ctx, cudaMemsetAsync(g.p, 0, n_pad * 4, s));
   RW_CU(ctx, cudaMemsetAsync(h.p, 0, n_pad * 4, s));
   RW_CU(ctx, cudaMemsetAsync(node.p, 0, n_pad * 2, s));
-  RW_CU(ctx, cudaMemsetAsync(slot.p, 0xff, n_pad * 2, s));
   RW_CU(ctx, cudaMemsetAsync(d_fi_gain.p, 0, nf * 4, s));
   RW_CU(ctx, cudaMemsetAsync(d_fi_count.p, 0, nf * 4, s));
   RW_CU(ctx, cudaMemsetAsync(maxbits.p, 0, maxbits.n * 4, s));
-  RW_CU(ctx, cudaMemsetAsync(counter.p, 0, 4, s));
   RW_CU(ctx, cudaMemsetAsync(d_leafval.p, 0, std::max<size_t>(d_leafval.n, 1) * 4, s));
   bool any_mono = false;
   std::vector<int32_t> mono(nf, 0);
@@ -500,6 +526,8 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
   if (any_mono) {
     RW_CU(ctx, d_mono.get(ds, "mono", nf));
     RW_CU(ctx, cudaMemcpyAsync(d_mono.p, mono.data(), nf * 4, cudaMemcpyHostToDevice, s));
+    RW_CU(ctx, mono_sums.get(ds, "mono_sums", (size_t)nf * (nb - 1) * 4));
+    RW_CU(ctx, cudaMemsetAsync(mono_sums.p, 0, mono_sums.n * sizeof(long long), s));
   }
   GossState gst{nullptr, nullptr};
   if (goss) {
@@ -559,7 +587,7 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
                              &nl));
     }
     if (ctx->comm) RW_NC(ctx, ncclAllReduce(mb, mb, 2, ncclUint32, ncclMax, ctx->comm, s));
-    RW_CU(ctx, launch_quant(g.p, h.p, mb, n_pad, qg.p, qh.p, node.p, slot.p, hb0.p, cell, s, &nl));
+    RW_CU(ctx, launch_quant(g.p, h.p, mb, n_pad, q.p, node.p, hb0.p, cell, s, &nl));
     pt.mark(RW_CAT_GRADIENTS);
 
     const uint32_t tree_seed = t * 2654435761u + 0x455A4B41u;  // src/booster.rs:351
@@ -572,17 +600,18 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
       const uint32_t groups_next =
           d + 1 < D ? (subtract ? (1u << d) : (1u << (d + 1))) : 0u;
       HistLaunch hl;
-      hl.bins = ds->d_bins;
-      hl.lay = ds->lay;
-      hl.slot = slot.p;
-      hl.qg = qg.p;
-      hl.qh = qh.p;
+      hl.rowbins = ds->d_rowbins;
       hl.n_pad = n_pad;
+      hl.packed = ds->packed;
+      hl.q = q.p;
+      hl.rows = d == 0 ? nullptr : rl_rows.p;  // level 0: every row
+      hl.seg = d == 0 ? nullptr : rl_seg.p;
+      hl.n_ident = (uint32_t)round_up(n, 128);  // rows past n carry q = 0
+      hl.err = kerr.p;
+      hl.groups = groups;
       hl.nf = nf;
       hl.nb = nb;
-      hl.groups = groups;
       hl.out = hb;
-      hl.err = kerr.p;
       RW_CU(ctx, launch_hist(hl, s, &nl));
       hist_launches++;
       alg_bytes += (double)n * nf * bin_bytes + 12.0 * (double)n + 8.0 * nf * nb * groups;
@@ -601,32 +630,54 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
       sl.nf = nf;
       sl.nb = nb;
       sl.mode = mode;
+      sl.built_odd = mode == 1 ? rl_odd.p : nullptr;
+      sl.zero_u32 = d + 1 < D ? rl_counters.p : nullptr;
+      sl.zero_words = 2 * NL;
       sl.maxbits = mb;
       sl.lambda = (double)p->lambda;
       sl.min_child = (double)p->min_child_h;
       sl.lr = (double)p->learning_rate;
       sl.monotone = any_mono ? d_mono.p : nullptr;
+      sl.mono = any_mono ? mono_sums.p : nullptr;
+      sl.term = term.p;
+      sl.prefix = prefix.p;
       sl.colsample = p->colsample;
       sl.tree_seed = tree_seed;
-      sl.best_gain = best_gain.p;
-      sl.best_bin = best_bin.p;
-      sl.counter = counter.p;
       sl.cuts = ds->d_cuts;
-      sl.feat = d_feat.p;
-      sl.thr = d_thr.p;
-      sl.thr_bin = d_thr_bin.p;
-      sl.split_ft = split_ft.p;
-      sl.fi_gain = d_fi_gain.p;
-      sl.fi_count = d_fi_count.p;
-      sl.slot = t * D + d;
+      sl.rec = rec.p;
       sl.last_level = d == D - 1;
-      sl.leafval = d_leafval.p;
-      sl.leaf_base = t * NL;
-      RW_CU(ctx, launch_split(sl, s));
-      nl++;
+      sl.leafc = leafc.p;
+      RW_CU(ctx, launch_split(sl, s, &nl));
       pt.mark(RW_CAT_SPLIT);
-      RW_CU(ctx, launch_apply(ds->d_bins, ds->lay, node.p, slot.p, split_ft.p, n_pad,
-                              subtract ? 1 : 0, d == D - 1, d_leafval.p, t * NL, pred.p, s, &nl));
+      const uint32_t n_children = 2u << d;
+      ApplyLaunch al;
+      al.colbins = ds->d_colbins;
+      al.n_pad = n_pad;
+      al.node = node.p;
+      al.rec = rec.p;
+      al.nf = nf;
+      al.n_children = n_children;
+      al.cnt = rl_counters.p;
+      al.final_level = d == D - 1;
+      al.leafc = leafc.p;
+      al.n_leaves = NL;
+      al.pred = pred.p;
+      al.feat = d_feat.p;
+      al.thr = d_thr.p;
+      al.thr_bin = d_thr_bin.p;
+      al.fi_gain = d_fi_gain.p;
+      al.fi_count = d_fi_count.p;
+      al.slot = t * D + d;
+      al.leafval = d_leafval.p;
+      al.leaf_base = t * NL;
+      al.split_out = nullptr;
+      RW_CU(ctx, launch_apply(al, s, &nl));
+      if (d + 1 < D) {
+        // with several ranks every rank must build the same child of each pair
+        RowLists rl{rl_counters.p, rl_counters.p + NL, rl_seg.p, rl_odd.p, rl_rows.p};
+        RW_CU(ctx, launch_rowlist(node.p, n_pad, n_children, subtract ? 1 : 0,
+                                  ctx->world > 1 ? 1 : 0, rl, s, &nl));
+      }
       pt.mark(d == D - 1 ? RW_CAT_UPDATE_PRED : RW_CAT_APPLY);
     }
   }
@@ -634,10 +685,6 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
   rc = wait_stream(ctx);
   if (rc) return rc;
   ctx->launches += nl;
-  int kerr_h = 0;
-  RW_CU(ctx, cudaMemcpy(&kerr_h, kerr.p, sizeof(int), cudaMemcpyDeviceToHost));
-  if (kerr_h)
-    return fail(ctx, RW_ERR_TIMEOUT, "a histogram pipeline wait gave up (bounded wait expired)");
 
   if (T > 0) {
     RW_CU(ctx, cudaMemcpy(feat, d_feat.p, (size_t)T * D * 4, cudaMemcpyDeviceToHost));
@@ -645,6 +692,13 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
     if (thr_bin)
       RW_CU(ctx, cudaMemcpy(thr_bin, d_thr_bin.p, (size_t)T * D * 2, cudaMemcpyDeviceToHost));
     RW_CU(ctx, cudaMemcpy(leafval, d_leafval.p, (size_t)T * NL * 4, cudaMemcpyDeviceToHost));
+  }
+  int kerr_h = 0;
+  RW_CU(ctx, cudaMemcpy(&kerr_h, kerr.p, sizeof(int), cudaMemcpyDeviceToHost));
+  if (kerr_h) {
+    cudaEventDestroy(ev0);
+    cudaEventDestroy(ev1);
+    return fail(ctx, RW_ERR_TIMEOUT, "a histogram bulk-copy wait gave up (bounded wait expired)");
   }
   RW_CU(ctx, cudaMemcpy(fi_gain, d_fi_gain.p, nf * 4, cudaMemcpyDeviceToHost));
   RW_CU(ctx, cudaMemcpy(fi_count, d_fi_count.p, nf * 4, cudaMemcpyDeviceToHost));
@@ -914,8 +968,10 @@ extern "C" int rw_debug_level_hist(rw_dataset* ds, const int32_t* node, const fl
   rw_ctx* ctx = ds->ctx;
   RW_CU(ctx, cudaSetDevice(ctx->device));
   const uint64_t n = ds->n, n_pad = ds->n_pad;
-  std::vector<int16_t> sl(n_pad, -1);
-  std::vector<int32_t> qgv(n_pad, 0), qhv(n_pad, 0);
+  // The level's row list, grouped by histogram group (counting sort), and q per row.
+  std::vector<int2> qv(n_pad, make_int2(0, 0));
+  std::vector<int32_t> grp(n, -1);
+  std::vector<uint32_t> seg(groups + 1, 0);
   const float sg = rw_pow2f(e_g), sh = rw_pow2f(e_h);
   for (uint64_t i = 0; i < n; i++) {
     if (node[i] < 0) continue;
@@ -925,46 +981,63 @@ extern "C" int rw_debug_level_hist(rw_dataset* ds, const int32_t* node, const fl
     if (std::abs(a) > (1 << RW_QBITS) || std::abs(b) > (1 << RW_QBITS))
       return fail(ctx, RW_ERR_ARG, "e_g/e_h put |q| above 2^RW_QBITS");
     if ((a | b) == 0) continue;
-    qgv[i] = a;
-    qhv[i] = b;
-    if (odd_only) sl[i] = (node[i] & 1) ? (int16_t)(node[i] >> 1) : (int16_t)-1;
-    else sl[i] = (int16_t)node[i];
+    qv[i] = make_int2(a, b);
+    const int32_t gi = odd_only ? ((node[i] & 1) ? (node[i] >> 1) : -1) : node[i];
+    if (gi < 0) continue;
+    if ((uint32_t)gi >= groups) return fail(ctx, RW_ERR_ARG, "node beyond the groups");
+    grp[i] = gi;
+    seg[gi + 1]++;
   }
-  const size_t words = (size_t)groups * ds->nf * ds->n_bins * 2;
-  DBuf<int16_t> dn;
-  DBuf<int32_t> dg, dh;
+  for (uint32_t k = 0; k < groups; k++) seg[k + 1] += seg[k];
+  std::vector<uint32_t> rows(std::max<uint32_t>(seg[groups], 1));
+  {
+    std::vector<uint32_t> cur(seg.begin(), seg.end() - 1);
+    for (uint64_t i = 0; i < n; i++)
+      if (grp[i] >= 0) rows[cur[grp[i]]++] = (uint32_t)i;
+  }
+  // device cells: [group][tile][bin][g|h][kHistFeat columns]; out: [group][nf][nb][2]
+  const size_t words = (size_t)groups * ds->ftiles * ds->n_bins * 2 * kHistFeat;
+  DBuf<int2> dq;
+  DBuf<uint32_t> drows, dseg;
   DBuf<long long> dout;
-  RW_CU(ctx, dn.alloc(n_pad));
-  RW_CU(ctx, dg.alloc(n_pad));
-  RW_CU(ctx, dh.alloc(n_pad));
+  RW_CU(ctx, dq.alloc(n_pad));
+  RW_CU(ctx, drows.alloc(rows.size()));
+  RW_CU(ctx, dseg.alloc(seg.size()));
   RW_CU(ctx, dout.alloc(words));
-  RW_CU(ctx, cudaMemcpy(dn.p, sl.data(), n_pad * 2, cudaMemcpyHostToDevice));
-  RW_CU(ctx, cudaMemcpy(dg.p, qgv.data(), n_pad * 4, cudaMemcpyHostToDevice));
-  RW_CU(ctx, cudaMemcpy(dh.p, qhv.data(), n_pad * 4, cudaMemcpyHostToDevice));
+  RW_CU(ctx, cudaMemcpy(dq.p, qv.data(), n_pad * sizeof(int2), cudaMemcpyHostToDevice));
+  RW_CU(ctx, cudaMemcpy(drows.p, rows.data(), rows.size() * 4, cudaMemcpyHostToDevice));
+  RW_CU(ctx, cudaMemcpy(dseg.p, seg.data(), seg.size() * 4, cudaMemcpyHostToDevice));
   RW_CU(ctx, cudaMemset(dout.p, 0, words * 8));
   HistLaunch hl;
-  hl.bins = ds->d_bins;
-  hl.lay = ds->lay;
-  hl.slot = dn.p;
-  hl.qg = dg.p;
-  hl.qh = dh.p;
-  hl.n_pad = n_pad;
+  hl.rowbins = ds->d_rowbins;
+  hl.n_pad = ds->n_pad;
+  hl.packed = ds->packed;
+  hl.err = nullptr;
+  hl.q = dq.p;
+  hl.rows = drows.p;
+  hl.seg = dseg.p;
+  hl.n_ident = 0;
+  hl.groups = groups;
   hl.nf = ds->nf;
   hl.nb = ds->n_bins;
-  hl.groups = groups;
   hl.out = dout.p;
-  DBuf<int> derr;
-  RW_CU(ctx, derr.alloc(1));
-  RW_CU(ctx, cudaMemset(derr.p, 0, sizeof(int)));
-  hl.err = derr.p;
   int nl = 0;
   RW_CU(ctx, launch_hist(hl, ctx->stream, &nl));
   RW_CU(ctx, cudaStreamSynchronize(ctx->stream));
   ctx->launches += nl;
-  RW_CU(ctx, cudaMemcpy(out, dout.p, words * 8, cudaMemcpyDeviceToHost));
-  int herr = 0;
-  RW_CU(ctx, cudaMemcpy(&herr, derr.p, sizeof(int), cudaMemcpyDeviceToHost));
-  if (herr) return fail(ctx, RW_ERR_TIMEOUT, "a histogram pipeline wait gave up");
+  std::vector<int64_t> cells(words);
+  RW_CU(ctx, cudaMemcpy(cells.data(), dout.p, words * 8, cudaMemcpyDeviceToHost));
+  const uint32_t nf = ds->nf, nb = ds->n_bins;
+  for (uint32_t gi = 0; gi < groups; gi++)
+    for (uint32_t f = 0; f < nf; f++) {
+      const uint32_t t = f / kHistFeat, j = f % kHistFeat, col = (j >> 1) + 32u * (j & 1u);
+      for (uint32_t b = 0; b < nb; b++) {
+        const size_t k = (((size_t)gi * ds->ftiles + t) * nb + b) * 2 * kHistFeat + col;
+        int64_t* o = out + (((size_t)gi * nf + f) * nb + b) * 2;
+        o[0] = cells[k];
+        o[1] = cells[k + kHistFeat];
+      }
+    }
   return RW_OK;
 }
 

@@ -3,23 +3,25 @@
 // Per boosting round (src/booster.rs:349-501 is the reference's sequence):
 //   k_grad / GOSS           gradients, row sampling, per-round max |g| and max h
 //   [ncclAllReduce max]     multi-GPU: global maxima (the fixed-point scales)
-//   k_quant                 per-row fixed-point q(g), q(h), excluded flag, level-0 slots
+//   k_quant                 per-row fixed-point q = (q(g), q(h)), excluded flag, node reset
 //   per level d:
-//     k_hist                exact fixed-point histogram of the built nodes
+//     k_hist                exact fixed-point histogram of the built nodes, over the
+//                           level's row list (all rows at level 0)
 //     [ncclAllReduce]       multi-GPU: sum of the built histograms (int64, exact)
 //     k_split               derive sibling nodes, f64 gain scan, argmax, model write,
 //                           leaf values at the last level (no separate leaf pass)
-//     k_apply               leaf = 2*leaf + (bin > t) and the next level's build slot;
+//     k_apply               leaf = 2*leaf + (bin > t) and per-child row counts;
 //                           at the last level pred += leafval[leaf]
+//     k_rowlist             the next level's row list: per node pair the child with
+//                           fewer rows, grouped by pair (the sibling is parent - built)
 //
 // Exactness: histogram cells are int64 sums of per-row fixed-point values
-// q = round(x * 2^e) (rw_expf.h). Shared memory holds the low 32 bits of each cell as
-// an int32 atomic accumulator biased by 2^31; the rare carries out of the low word are
-// added to the global int64 cell as +-2^32, and the low words are flushed at the end.
-// The result equals the int64 sum of q over the contributing rows regardless of
-// scheduling, so histograms, splits and leaf values are bit-identical run to run and
-// at every GPU count.
-#include <cooperative_groups.h>
+// q = round(x * 2^e) with |q| <= 2^RW_QBITS (rw_expf.h). A histogram CTA accumulates at
+// most kMaxRowsPerCta rows into 32-bit shared cells before adding them to the global
+// int64 cells, so every partial sum is exact. The result equals the int64 sum of q over
+// the contributing rows whatever the scheduling, the row order of the lists or which
+// child of a pair is built, so histograms, splits and leaf values are bit-identical run
+// to run and at every GPU count.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -34,20 +36,21 @@
 
 namespace {
 
-constexpr int kHistThreads = 512;
-// Rows one histogram CTA may accumulate into its 32-bit shared cells: every |q| is at
-// most 2^RW_QBITS, so a cell's partial sum stays within 2^(30) in magnitude and the
-// 32-bit word holds it exactly (no carries, no returned values needed).
+constexpr int kHistThreads = 1024;
+// Rows one histogram CTA accumulates into its 32-bit shared cells before adding them to
+// the global int64 cells: every |q| is at most 2^RW_QBITS, so a cell's partial sum
+// stays within 2^30 in magnitude and the 32-bit word holds it exactly.
 constexpr uint32_t kMaxRowsPerCta = 1u << (30 - RW_QBITS);
-static_assert(kMaxRowsPerCta >= 512, "quantisation too fine for one bin tile per CTA");
-constexpr int kMaxCluster = 8;
-constexpr int kStages = 2;
-constexpr int kSmemPerSm = 227 * 1024;  // usable shared memory per SM (one or two CTAs)
-
-namespace cg = cooperative_groups;
+static_assert(kMaxRowsPerCta >= 1024, "quantisation too fine for the histogram row bound");
+// Row gathers in flight per warp step (32 warps per CTA keep 256 rows in flight per SM).
+constexpr int kHistU = 8;
+// The all-rows level streams its rows through shared memory in stages of kStreamRows
+// (one TMA bulk copy of the stage's bin rows and one of its q values), kStreamStages deep.
+constexpr uint32_t kStreamRows = 128;
+constexpr int kStreamStages = 4;
+static_assert(kStreamRows == (kHistThreads / 32) * 4, "one 4-row step per warp per stage");
 
 // ---- TMA bulk copies and mbarriers (PTX) -------------------------------------------
-
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
 }
@@ -95,230 +98,192 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   return true;
 }
 
-struct HistArgs {
-  const uint8_t* bins;
-  BinLayout lay;
-  const int16_t* slot;
-  const int32_t* qg;
-  const int32_t* qh;
-  uint64_t n_pad;
-  uint32_t nf, nb;
-  uint32_t gchunk;  // groups per CTA (blockIdx.z selects the chunk)
-  long long* out;
-  int* err;
-  uint64_t rows_per_cta;  // multiple of kBinTile
-  uint32_t stage_bytes;   // bytes per stage
-  uint32_t hist_bytes;    // bytes of the shared histogram (stages follow it)
-};
+// Adds one row's tile to the shared cells: lane j owns columns j (feature 2j) and 32+j
+// (feature 2j+1); `bb` holds the two bins (u8 pair or one byte of 4-bit pairs). A lane
+// whose feature is past nf adds into the dummy bin row `nb` (never flushed), which keeps
+// the warp free of divergent branches.
+template <bool PACKED>
+__device__ __forceinline__ void hist_add_row(uint32_t* hs, uint32_t bb, int2 qq, uint32_t lane,
+                                             bool v0, bool v1, uint32_t nb) {
+  uint32_t b0 = PACKED ? (bb & 0xfu) : (bb & 0xffu);
+  uint32_t b1 = PACKED ? ((bb >> 4) & 0xfu) : (bb >> 8);
+  b0 = v0 ? b0 : nb;
+  b1 = v1 ? b1 : nb;
+  const uint32_t c0 = b0 * (2 * kHistFeat) + lane, c1 = b1 * (2 * kHistFeat) + 32 + lane;
+  atomicAdd(&hs[c0], (uint32_t)qq.x);
+  atomicAdd(&hs[c0 + kHistFeat], (uint32_t)qq.y);
+  atomicAdd(&hs[c1], (uint32_t)qq.x);
+  atomicAdd(&hs[c1 + kHistFeat], (uint32_t)qq.y);
+}
 
-// One CTA: a tile of FT*FPL consecutive features x group chunk x row range (at most
-// kMaxRowsPerCta rows), in a cluster of CTAs along the row ranges. The row range streams
-// through shared memory one bin tile (kBinTile rows) at a time: thread 0 issues TMA bulk
-// copies -- the CTA's feature slice of the tile is one contiguous block in the row-tiled
-// bin layout, plus the tile's slot/q arrays -- into a double-buffered stage, completing on
-// an mbarrier, while the CTA accumulates the previous tile. Lane (k, j) handles features
-// j + p*FT (p < FPL) of the tile for row slot k, U consecutive rows at a time. Shared
-// words are laid out [group][bin][g|h][FT*FPL]: for each p the FT lanes of one row hit FT
-// distinct banks, and a cell's h word is a fixed offset from its g word. Cells are plain
-// 32-bit integers updated by reductions whose results are not read back: the row bound
-// keeps every partial sum exact. With FT = 32 every lane of a warp works on the same row,
-// so rows that are not built are skipped warp-uniformly. After the rows, the cluster's
-// CTAs sum their shared histograms through distributed shared memory, each CTA adding a
-// slice to the global int64 histogram.
-template <int FT, int FPL, bool PACKED>
-__global__ void __launch_bounds__(kHistThreads, 1) k_hist(HistArgs a) {
-  constexpr uint32_t FTT = FT * FPL;  // features per CTA
-  constexpr uint32_t T = kBinTile;
-  constexpr int RW = 32 / FT;
-  // rows per lane step: 16 (one 16-byte load of u8 bins) when a tile round of
-  // 16 warps x RW slots x 16 rows fits the tile, else 4
-  constexpr uint32_t U = (16u * (kHistThreads / 32) * RW <= T) ? 16u : 4u;
-  extern __shared__ __align__(128) unsigned char hsm[];
-  uint32_t* smem = reinterpret_cast<uint32_t*>(hsm);
-  const uint32_t G = a.gchunk, nb = a.nb;
-  const uint32_t words = 2 * G * nb * FTT;
-  unsigned char* stage0 = hsm + a.hist_bytes;
-  __shared__ __align__(8) uint64_t bar[kStages];
-  __shared__ int abort_flag;
-  for (uint32_t i = threadIdx.x; i < words; i += kHistThreads) smem[i] = 0u;
-  if (threadIdx.x == 0) {
-    for (int st = 0; st < kStages; st++) mbar_init(&bar[st], 1);
-    mbar_init_fence();
-    abort_flag = 0;
-  }
-  __syncthreads();
-
+// Histogram of one level over a row list (or all rows), exact in fixed point.
+//
+// Row bins are tile-major: tile t's row r is the kHistFeat-byte (u8) or kHistFeat/2-byte
+// (4-bit) run at rowbins + (t * n_pad + r) * tile_bytes. The work space is (feature tile
+// t, list index i), tile-major; CTA b takes the contiguous slice [b*per, (b+1)*per) and
+// walks it in parts that stay inside one (tile, group) and hold at most kMaxRowsPerCta
+// rows. Per part the CTA accumulates into shared 32-bit cells laid out
+// [bin][g|h][64 columns]: lane j of a warp handles the tile's features 2j and 2j+1
+// (columns j and 32+j, so the warp's 32 lanes update 32 distinct banks). With a row list
+// the warps gather their rows' runs and q values directly; over all rows (the identity
+// list) the part is one contiguous range, streamed through shared memory by TMA bulk
+// copies in stages, so HBM sees long sequential reads. The cells are updated by
+// reductions whose results are not read back. At the end of a part its nonzero cells
+// are added to the global int64 histogram, which has the same cell layout per (group,
+// tile) -- [group][tile][bin][g|h][64 columns], column j holding feature 2j and column
+// 32+j feature 2j+1 -- and cleared.
+template <bool PACKED>
+__global__ void __launch_bounds__(kHistThreads) k_hist(HistLaunch a, uint32_t ftiles) {
+  extern __shared__ __align__(16) uint32_t hs[];
+  __shared__ __align__(8) uint64_t bar[kStreamStages];
+  __shared__ int s_abort;
+  constexpr uint32_t TB = PACKED ? kHistFeat / 2 : kHistFeat;  // tile bytes per row
+  const uint32_t nb = a.nb, words = nb * 2 * kHistFeat;
+  const uint32_t L = a.seg ? __ldg(a.seg + a.groups) : a.n_ident;
+  const uint64_t total = (uint64_t)L * ftiles;
+  // identity slices are whole stages (n_ident is a multiple of kStreamRows)
+  uint64_t per = (total + gridDim.x - 1) / gridDim.x;
+  if (!a.rows) per = (per + kStreamRows - 1) / kStreamRows * kStreamRows;
+  uint64_t w = (uint64_t)blockIdx.x * per;
+  const uint64_t w_end = min(total, w + per);
+  if (w >= w_end) return;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int j = lane % FT, k = lane / FT;
-  const uint32_t f0 = blockIdx.y * FTT;
-  const int g0 = (int)(blockIdx.z * a.gchunk);
-  const uint32_t rs = a.lay.rs;
-  const size_t gstride = (size_t)a.nf * nb * 2;
-  const uint32_t nvalid = a.nf - f0 < FTT ? a.nf - f0 : FTT;
-  bool fval[FPL];
-#pragma unroll
-  for (int p = 0; p < FPL; p++) fval[p] = (uint32_t)(p * FT + j) < nvalid;
-
-  const uint64_t r_begin = (uint64_t)blockIdx.x * a.rows_per_cta;
-  uint64_t r_end = r_begin + a.rows_per_cta;
-  if (r_end > a.n_pad) r_end = a.n_pad;
-  const uint32_t ntiles = r_end > r_begin ? (uint32_t)((r_end - r_begin) / T) : 0u;
-
-  auto stage_ptr = [&](int st) { return stage0 + (size_t)st * a.stage_bytes; };
-  auto issue = [&](uint32_t t, int st) {  // thread 0
-    unsigned char* sp = stage_ptr(st);
-    const uint64_t r0 = r_begin + (uint64_t)t * T;
-    const uint32_t bbytes = nvalid * rs;
-    mbar_expect_tx(&bar[st], bbytes + 10u * T);
-    bulk_g2s(sp, a.bins + (r0 / T) * a.lay.tile_bytes + (uint64_t)f0 * rs, bbytes, &bar[st]);
-    unsigned char* rowp = sp + (size_t)FTT * rs;
-    bulk_g2s(rowp, a.slot + r0, 2u * T, &bar[st]);
-    bulk_g2s(rowp + 2u * T, a.qg + r0, 4u * T, &bar[st]);
-    bulk_g2s(rowp + 6u * T, a.qh + r0, 4u * T, &bar[st]);
-  };
-
-  if (threadIdx.x == 0 && ntiles > 0) issue(0, 0);
-  for (uint32_t t = 0; t < ntiles; t++) {
-    const int st = t & 1;
-    if (threadIdx.x == 0 && t + 1 < ntiles && !abort_flag) {
-      fence_proxy_async_smem();  // the stage's last readers finished before the barrier below
-      issue(t + 1, st ^ 1);
+  unsigned char* stage0 = reinterpret_cast<unsigned char*>(hs + words + 2 * kHistFeat);
+  constexpr uint32_t kStageBytes = kStreamRows * (TB + 8);
+  for (uint32_t c = threadIdx.x; c < words; c += kHistThreads) hs[c] = 0u;
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    if (!a.rows) {
+      for (int st = 0; st < kStreamStages; st++) mbar_init(&bar[st], 1);
+      mbar_init_fence();
     }
-    // After a wait gave up, no further copies are issued and no further waits are made.
-    if (!abort_flag && !mbar_wait_bounded(&bar[st], (t >> 1) & 1u)) abort_flag = 1;
-    const unsigned char* sp = stage_ptr(st);
-    const int16_t* s_slot = reinterpret_cast<const int16_t*>(sp + (size_t)FTT * rs);
-    const int32_t* s_qg = reinterpret_cast<const int32_t*>(sp + (size_t)FTT * rs + 2u * T);
-    const int32_t* s_qh = reinterpret_cast<const int32_t*>(sp + (size_t)FTT * rs + 6u * T);
-    if (!abort_flag) {
-      for (uint32_t rg = warp * RW + k; rg < T / U; rg += (kHistThreads / 32) * RW) {
-        const uint32_t r = rg * U;
-        uint32_t bw[FPL][U / 4];
+  }
+  uint32_t phase_base = 0;  // stages consumed so far (mbarrier phase bookkeeping)
+  while (w < w_end) {
+    const uint32_t t = (uint32_t)(w / L);
+    const uint32_t i0 = (uint32_t)(w % L);
+    // the group holding list index i0: the last k with seg[k] <= i0
+    uint32_t grp = 0, g_end = L;
+    if (a.seg) {
+      uint32_t lo = 0, hi = a.groups;
+      while (hi - lo > 1) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (__ldg(a.seg + mid) <= i0) lo = mid;
+        else hi = mid;
+      }
+      grp = lo;
+      g_end = __ldg(a.seg + lo + 1);
+    }
+    uint64_t i1 = min((uint64_t)g_end, (uint64_t)i0 + kMaxRowsPerCta);
+    i1 = min(i1, (uint64_t)i0 + (w_end - w));
+    const uint32_t fbase = t * kHistFeat;
+    const bool v0 = fbase + 2 * lane < a.nf, v1 = fbase + 2 * lane + 1 < a.nf;
+    const unsigned char* tile = a.rowbins + (size_t)t * a.n_pad * TB;
+    __syncthreads();  // cleared cells (and barrier init) are visible
+    if (!a.rows) {
+      // ---- streamed: rows i0 .. i1 in stages of kStreamRows ----
+      const uint32_t nst = (uint32_t)((i1 - i0) / kStreamRows);
+      auto issue = [&](uint32_t k) {
+        const int st = (int)((phase_base + k) % kStreamStages);
+        unsigned char* sp = stage0 + (size_t)st * kStageBytes;
+        const uint64_t r0 = i0 + (uint64_t)k * kStreamRows;
+        mbar_expect_tx(&bar[st], kStageBytes);
+        bulk_g2s(sp, tile + r0 * TB, kStreamRows * TB, &bar[st]);
+        bulk_g2s(sp + kStreamRows * TB, a.q + r0, kStreamRows * 8, &bar[st]);
+      };
+      if (threadIdx.x == 0) {
+        fence_proxy_async_smem();
+        for (uint32_t k = 0; k < nst && k < (uint32_t)kStreamStages; k++) issue(k);
+      }
+      uint32_t consumed = 0;
+      for (uint32_t k = 0; k < nst; k++) {
+        const uint32_t gk = phase_base + k;
+        const int st = (int)(gk % kStreamStages);
+        if (!s_abort && !mbar_wait_bounded(&bar[st], (gk / kStreamStages) & 1u)) s_abort = 1;
+        if (!s_abort) {
+          const unsigned char* sp = stage0 + (size_t)st * kStageBytes;
+          const int2* sq = reinterpret_cast<const int2*>(sp + kStreamRows * TB);
 #pragma unroll
-        for (int p = 0; p < FPL; p++) {
-          const unsigned char* sb = sp + (size_t)(p * FT + j) * rs;
-          if (U == 16) {
-            if (PACKED) {
-              const uint2 pk = *reinterpret_cast<const uint2*>(sb + r / 2);
-              const uint32_t pw[2] = {pk.x, pk.y};
-#pragma unroll
-              for (int h2 = 0; h2 < 2; h2++)
-#pragma unroll
-                for (int q2 = 0; q2 < 2; q2++) {
-                  const uint32_t v = pw[h2] >> (16 * q2);
-                  bw[p][(2 * h2 + q2) % (U / 4)] = (v & 0xfu) | ((v & 0xf0u) << 4) |
-                                                   ((v & 0xf00u) << 8) | ((v & 0xf000u) << 12);
-                }
-            } else {
-              const uint4 pk = *reinterpret_cast<const uint4*>(sb + r);
-              const uint32_t pw[4] = {pk.x, pk.y, pk.z, pk.w};
-#pragma unroll
-              for (int q = 0; q < (int)(U / 4); q++) bw[p][q] = pw[q];
-            }
-          } else {
-            if (PACKED) {
-              const uint32_t v = *reinterpret_cast<const uint16_t*>(sb + r / 2);
-              bw[p][0] = (v & 0xfu) | ((v & 0xf0u) << 4) | ((v & 0xf00u) << 8) |
-                         ((v & 0xf000u) << 12);
-            } else {
-              bw[p][0] = *reinterpret_cast<const uint32_t*>(sb + r);
-            }
+          for (int u = 0; u < 4; u++) {
+            const uint32_t r = warp * 4 + u;
+            const uint32_t bb = PACKED ? (uint32_t)sp[r * TB + lane]
+                                       : (uint32_t)*reinterpret_cast<const uint16_t*>(sp + r * TB + 2 * lane);
+            hist_add_row<PACKED>(hs, bb, sq[r], lane, v0, v1, nb);
           }
         }
-#pragma unroll
-        for (int q4 = 0; q4 < (int)(U / 4); q4++) {
-          const uint2 sl2 = *reinterpret_cast<const uint2*>(s_slot + r + 4 * q4);
-          const int4 qg4 = *reinterpret_cast<const int4*>(s_qg + r + 4 * q4);
-          const int4 qh4 = *reinterpret_cast<const int4*>(s_qh + r + 4 * q4);
-          const int sl[4] = {(int)(int16_t)(sl2.x & 0xffffu), (int)(int16_t)(sl2.x >> 16),
-                             (int)(int16_t)(sl2.y & 0xffffu), (int)(int16_t)(sl2.y >> 16)};
-          const uint32_t qgr[4] = {(uint32_t)qg4.x, (uint32_t)qg4.y, (uint32_t)qg4.z,
-                                   (uint32_t)qg4.w};
-          const uint32_t qhr[4] = {(uint32_t)qh4.x, (uint32_t)qh4.y, (uint32_t)qh4.z,
-                                   (uint32_t)qh4.w};
-#pragma unroll
-          for (int s = 0; s < 4; s++) {
-            const uint32_t grp = (uint32_t)(sl[s] - g0);
-            if (FT == 32 && grp >= G) continue;  // warp-uniform: every lane works on this row
-            const uint32_t lb = grp * nb * (2 * FTT) + (uint32_t)j;
-#pragma unroll
-            for (int p = 0; p < FPL; p++) {
-              if (fval[p] && (FT == 32 || grp < G)) {
-                const uint32_t bin = __byte_perm(bw[p][q4], 0u, 0x4440u + (uint32_t)s);
-                const uint32_t w = lb + bin * (2 * FTT) + (uint32_t)(p * FT);
-                atomicAdd(&smem[w], qgr[s]);
-                atomicAdd(&smem[w + FTT], qhr[s]);
-              }
-            }
-          }
+        __syncthreads();  // every reader of stage st is done
+        if (s_abort) break;
+        consumed = k + 1;
+        if (threadIdx.x == 0 && k + kStreamStages < nst) {
+          fence_proxy_async_smem();
+          issue(k + kStreamStages);
         }
       }
+      if (s_abort) {
+        // a wait gave up: let the copies already issued land (bounded) before leaving
+        const uint32_t issued = min(nst, consumed + (uint32_t)kStreamStages);
+        if (threadIdx.x == 0)
+          for (uint32_t k = consumed; k < issued; k++) {
+            const uint32_t gk = phase_base + k;
+            mbar_wait_bounded(&bar[gk % kStreamStages], (gk / kStreamStages) & 1u);
+          }
+        __syncthreads();
+        break;
+      }
+      phase_base += nst;
+    } else {
+      // ---- gathered: the list's rows ----
+      const uint32_t boff = PACKED ? lane : 2 * lane;
+      for (uint32_t b = i0 + warp * kHistU; b < (uint32_t)i1; b += (kHistThreads / 32) * kHistU) {
+        // past the part's end a step reads row 0 and adds q = 0 (no divergent branches)
+        uint32_t rid[kHistU], bb[kHistU];
+        int2 qq[kHistU];
+#pragma unroll
+        for (int u = 0; u < kHistU; u++) {
+          const uint32_t ii = b + u;
+          rid[u] = ii < (uint32_t)i1 ? __ldg(a.rows + ii) : 0u;
+        }
+#pragma unroll
+        for (int u = 0; u < kHistU; u++) {
+          const unsigned char* rp = tile + (size_t)rid[u] * TB + boff;
+          bb[u] = PACKED ? (uint32_t)__ldg(rp) : (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(rp));
+          qq[u] = __ldg(a.q + rid[u]);
+          if (b + u >= (uint32_t)i1) qq[u] = make_int2(0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < kHistU; u++) hist_add_row<PACKED>(hs, bb[u], qq[u], lane, v0, v1, nb);
+      }
     }
-    __syncthreads();  // every reader of stage `st` is done before it is refilled
-  }
-  if (abort_flag && threadIdx.x == 0) atomicExch(a.err, 1);
-
-  cg::cluster_group cluster = cg::this_cluster();
-  cluster.sync();
-  const uint32_t cn = cluster.num_blocks(), cr = cluster.block_rank();
-  const uint32_t per = (words + cn - 1) / cn;
-  const uint32_t w_begin = cr * per, w_end = min(words, w_begin + per);
-  for (uint32_t w = w_begin + threadIdx.x; w < w_end; w += kHistThreads) {
-    long long v = 0;
-    for (uint32_t r = 0; r < cn; r++) {
-      const uint32_t* remote = cluster.map_shared_rank(smem, (int)r);
-      v += (long long)(int32_t)remote[w];
+    __syncthreads();
+    // the global cells of (grp, t) use the shared layout, so consecutive threads add
+    // into consecutive int64 words
+    unsigned long long* gout =
+        reinterpret_cast<unsigned long long*>(a.out + ((size_t)grp * ftiles + t) * words);
+    for (uint32_t c = threadIdx.x; c < words; c += kHistThreads) {
+      const uint32_t v = hs[c];
+      if (v == 0u) continue;
+      hs[c] = 0u;
+      atomicAdd(gout + c, (unsigned long long)(long long)(int32_t)v);
     }
-    if (v == 0) continue;
-    const uint32_t blk = w / (2 * FTT), within = w % (2 * FTT);
-    const uint32_t is_h = within >= FTT ? 1u : 0u, fo = within - is_h * FTT;
-    const uint32_t bin = blk % nb, grp = blk / nb;
-    const uint32_t ff = f0 + fo;
-    if (ff >= a.nf) continue;
-    long long* gc = a.out + (size_t)(g0 + grp) * gstride + ((size_t)ff * nb + bin) * 2 + is_h;
-    atomicAdd(reinterpret_cast<unsigned long long*>(gc), (unsigned long long)v);
+    w += i1 - i0;
   }
-  cluster.sync();  // keep this CTA's shared memory alive until every reader is done
-}
-
-template <int FT, int FPL, bool PACKED>
-const void* hist_fn() {
-  return reinterpret_cast<const void*>(&k_hist<FT, FPL, PACKED>);
-}
-
-template <bool PACKED>
-const void* pick_hist(int ft, int fpl) {
-  if (fpl == 2) return hist_fn<32, 2, PACKED>();
-  switch (ft) {
-    case 32: return hist_fn<32, 1, PACKED>();
-    case 16: return hist_fn<16, 1, PACKED>();
-    case 8: return hist_fn<8, 1, PACKED>();
-    case 4: return hist_fn<4, 1, PACKED>();
-    case 2: return hist_fn<2, 1, PACKED>();
-    default: return hist_fn<1, 1, PACKED>();
-  }
+  if (s_abort && threadIdx.x == 0 && a.err) atomicExch(a.err, 1);
 }
 
 // --------------------------------------------------------------------------------
-// Split scan: one CTA per feature; its 32 warps take 32 nodes at a time (one node per
-// warp), lanes take 8 consecutive bins. Per-node gain terms go to shared memory and
-// each bin's thread adds them in node order, as src/cpu.rs:242-259 does.
+// Split scan (src/cpu.rs:235-276), in two kernels:
+//   k_gain  one CTA per (node, feature), one thread per bin: the node's histogram
+//           (the sibling derived as parent - built child), its exact int64 prefix over
+//           bins, and the per-node gain term of every threshold in f64 exactly as
+//           src/cpu.rs:242-259 writes it;
+//   k_best  one CTA per feature, one thread per threshold: the terms summed in node
+//           order (the order src/cpu.rs adds them), the candidate masks, the feature's
+//           best threshold (ties to the lowest bin) and, at the last level, the leaf
+//           values that threshold would give.
+// The cross-feature argmax is taken by the leaf-index update (k_apply).
 
-constexpr int kSplitThreads = 1024;
-constexpr int kSplitWarps = kSplitThreads / 32;
-
-struct SplitSmem {
-  double term[kSplitWarps][256];
-  long long mono[4][256];  // exact left/right (g, h) totals over nodes (monotone only)
-  double red_g[kSplitWarps];
-  uint32_t red_i[kSplitWarps];
-  int last;
-  uint32_t s_f, s_b;
-};
-
-__device__ __forceinline__ long long shfl_up_ll(long long v, int d) {
-  return __shfl_up_sync(0xffffffffu, v, d);
-}
+constexpr int kGainThreads = 256;  // >= n_bins
+constexpr int kBestThreads = 256;
 
 __device__ __forceinline__ uint32_t hash01_bits(uint32_t id, uint32_t seed) {
   // src/gpu_kernels.rs hash01 (salted integer hash of (id, seed)).
@@ -337,8 +302,8 @@ __device__ __forceinline__ void argmax_merge(double& g, uint32_t& i, double g2, 
   }
 }
 
-// Block-wide argmax; the result is valid in thread 0.
-__device__ void block_argmax(double& g, uint32_t& i, SplitSmem& sm) {
+// Block-wide argmax over kBestThreads threads; the result is valid in thread 0.
+__device__ void block_argmax256(double& g, uint32_t& i, double* red_g, uint32_t* red_i) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) {
@@ -347,239 +312,283 @@ __device__ void block_argmax(double& g, uint32_t& i, SplitSmem& sm) {
     if (lane + off < 32) argmax_merge(g, i, g2, i2);
   }
   if (lane == 0) {
-    sm.red_g[warp] = g;
-    sm.red_i[warp] = i;
+    red_g[warp] = g;
+    red_i[warp] = i;
   }
   __syncthreads();
-  if (warp == 0) {
-    g = lane < kSplitWarps ? sm.red_g[lane] : -RW_INF;
-    i = lane < kSplitWarps ? sm.red_i[lane] : 0xffffffffu;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const double g2 = __shfl_down_sync(0xffffffffu, g, off);
-      const uint32_t i2 = __shfl_down_sync(0xffffffffu, i, off);
-      if (lane + off < 32) argmax_merge(g, i, g2, i2);
-    }
-  }
-  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int w = 1; w < kBestThreads / 32; w++) argmax_merge(g, i, red_g[w], red_i[w]);
 }
 
-__global__ void __launch_bounds__(kSplitThreads) k_split(SplitLaunch a) {
-  extern __shared__ __align__(16) unsigned char split_raw[];
-  SplitSmem& sm = *reinterpret_cast<SplitSmem*>(split_raw);
-  const uint32_t f = blockIdx.x;
-  const uint32_t nf = a.nf, nb = a.nb, nsplit = nb - 1;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const double inv_g = 1.0 / (double)rw_pow2f(rw_qscale_exp(a.maxbits[0]));
-  const double inv_h = 1.0 / (double)rw_pow2f(rw_qscale_exp(a.maxbits[1]));
-  const double lambda = a.lambda, mc = a.min_child;
-  const int mono = a.monotone ? a.monotone[f] : 0;
+__device__ __forceinline__ double q_inv_scale(uint32_t maxbits) {
+  return 1.0 / (double)rw_pow2f(rw_qscale_exp(maxbits));
+}
 
-  // The next level's built-histogram buffer is zeroed here (this CTA's slice).
+// One CTA per (node, tile, group of 4 columns); thread b owns bin b of the 4 features in
+// those columns. A 32-byte sector of the layout holds exactly 4 columns, so every load
+// and store is a whole-sector vector access.
+constexpr uint32_t kGainCols = 4;
+
+__global__ void __launch_bounds__(kGainThreads) k_gain(SplitLaunch a) {
+  __shared__ long long wsum[kGainThreads / 32][2 * kGainCols];
+  __shared__ long long tot[2 * kGainCols];
+  const uint32_t nd = blockIdx.x;
+  const uint32_t t = blockIdx.y / (kHistFeat / kGainCols);
+  const uint32_t c0 = (blockIdx.y % (kHistFeat / kGainCols)) * kGainCols;
+  const uint32_t nf = a.nf, nb = a.nb, nsplit = nb - 1, b = threadIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t ftiles = (nf + kHistFeat - 1) / kHistFeat;
+  uint32_t fq[kGainCols];
+  bool any = false;
+#pragma unroll
+  for (int i = 0; i < (int)kGainCols; i++) {
+    const uint32_t c = c0 + i;  // column -> feature: j -> 2j, 32 + j -> 2j + 1
+    fq[i] = t * kHistFeat + 2 * (c % 32) + c / 32;
+    any |= fq[i] < nf;
+  }
+  if (!any) return;  // uniform per CTA
+  long long x[2 * kGainCols];  // g of the 4 columns, then h
+#pragma unroll
+  for (int i = 0; i < 2 * (int)kGainCols; i++) x[i] = 0;
+  if (b < nb) {
+    const size_t cell = ((size_t)t * nb + b) * (2 * kHistFeat) + c0;  // within a node
+    const size_t node_words = (size_t)ftiles * nb * 2 * kHistFeat;
+    // 4 consecutive int64 columns (one 32-byte sector) for g and for h
+    auto load4 = [](const long long* src, long long* dst) {
+      const longlong2 u = __ldcg(reinterpret_cast<const longlong2*>(src));
+      const longlong2 v = __ldcg(reinterpret_cast<const longlong2*>(src + 2));
+      dst[0] = u.x;
+      dst[1] = u.y;
+      dst[2] = v.x;
+      dst[3] = v.y;
+    };
+    const size_t k = (a.mode == 0 ? nd : (nd >> 1)) * node_words + cell;
+    load4(a.hb + k, x);
+    load4(a.hb + k + kHistFeat, x + kGainCols);
+    // mode 1: the pair's built child is in hb (keyed by the parent); its sibling is
+    // parent - built
+    if (a.mode == 1 &&
+        (a.built_odd ? a.built_odd[nd >> 1] != 0 : true) != ((nd & 1u) != 0)) {
+      long long pp[2 * kGainCols];
+      load4(a.hp + k, pp);
+      load4(a.hp + k + kHistFeat, pp + kGainCols);
+#pragma unroll
+      for (int i = 0; i < 2 * (int)kGainCols; i++) x[i] = pp[i] - x[i];
+    }
+    long long* o = a.hf + nd * node_words + cell;
+    reinterpret_cast<longlong2*>(o)[0] = make_longlong2(x[0], x[1]);
+    reinterpret_cast<longlong2*>(o)[1] = make_longlong2(x[2], x[3]);
+    reinterpret_cast<longlong2*>(o + kHistFeat)[0] = make_longlong2(x[4], x[5]);
+    reinterpret_cast<longlong2*>(o + kHistFeat)[1] = make_longlong2(x[6], x[7]);
+  }
+  // inclusive prefixes over bins (exact int64), 8 at once
+  long long p[2 * kGainCols];
+#pragma unroll
+  for (int i = 0; i < 2 * (int)kGainCols; i++) p[i] = x[i];
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+#pragma unroll
+    for (int i = 0; i < 2 * (int)kGainCols; i++) {
+      const long long v = __shfl_up_sync(0xffffffffu, p[i], d);
+      if (lane >= d) p[i] += v;
+    }
+  }
+  if (lane == 31)
+#pragma unroll
+    for (int i = 0; i < 2 * (int)kGainCols; i++) wsum[warp][i] = p[i];
+  __syncthreads();
+  if (threadIdx.x < 2 * kGainCols) {
+    long long c = 0;
+    for (int w = 0; w < kGainThreads / 32; w++) {
+      const long long v = wsum[w][threadIdx.x];
+      wsum[w][threadIdx.x] = c;
+      c += v;
+    }
+    tot[threadIdx.x] = c;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 2 * (int)kGainCols; i++) p[i] += wsum[warp][i];
+  if (a.last_level && b < nb) {
+    // prefixes for the leaf values of whichever threshold k_best picks
+#pragma unroll
+    for (int i = 0; i < (int)kGainCols; i++)
+      if (fq[i] < nf)
+        reinterpret_cast<longlong2*>(a.prefix)[((size_t)fq[i] * a.n_nodes + nd) * nb + b] =
+            make_longlong2(p[i], p[kGainCols + i]);
+  }
+  if (b >= nsplit) return;
+  const double inv_g = q_inv_scale(a.maxbits[0]), inv_h = q_inv_scale(a.maxbits[1]);
+  const double lambda = a.lambda, mc = a.min_child;
+#pragma unroll
+  for (int i = 0; i < (int)kGainCols; i++) {
+    const uint32_t f = fq[i];
+    if (f >= nf) continue;
+    const long long pgi = p[i], phi = p[kGainCols + i];
+    const long long tg = tot[i], th = tot[kGainCols + i];
+    const double gt = (double)tg * inv_g, ht = (double)th * inv_h;
+    const double parent = gt * gt / (ht + lambda);
+    const double gl = (double)pgi * inv_g, hl = (double)phi * inv_h;
+    const double gr = gt - gl, hr = ht - hl;
+    const double valid = (double)((hl >= mc) & (hr >= mc));
+    a.term[((size_t)f * a.n_nodes + nd) * nsplit + b] =
+        valid * (gl * gl / (hl + lambda) + gr * gr / (hr + lambda) - parent);
+    if (a.mono && a.monotone[f] != 0) {
+      // exact left/right (g, h) totals over all nodes for the monotone rule
+      unsigned long long* m =
+          reinterpret_cast<unsigned long long*>(a.mono + ((size_t)f * nsplit + b) * 4);
+      atomicAdd(m + 0, (unsigned long long)pgi);
+      atomicAdd(m + 1, (unsigned long long)phi);
+      atomicAdd(m + 2, (unsigned long long)(tg - pgi));
+      atomicAdd(m + 3, (unsigned long long)(th - phi));
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kBestThreads) k_best(SplitLaunch a) {
+  __shared__ double red_g[kBestThreads / 32];
+  __shared__ uint32_t red_i[kBestThreads / 32];
+  __shared__ uint32_t s_b;
+  const uint32_t f = blockIdx.x;
+  const uint32_t nf = a.nf, nb = a.nb, nsplit = nb - 1, b = threadIdx.x;
+  // zero the next level's built-histogram buffer (this CTA's slice) and list counters
   if (a.hb_next) {
     const uint64_t per = (a.hb_next_words + nf - 1) / nf;
     const uint64_t w0 = (uint64_t)f * per;
     const uint64_t w1 = w0 + per < a.hb_next_words ? w0 + per : a.hb_next_words;
-    for (uint64_t w = w0 + threadIdx.x; w < w1; w += kSplitThreads) a.hb_next[w] = 0;
+    for (uint64_t w = w0 + threadIdx.x; w < w1; w += kBestThreads) a.hb_next[w] = 0;
   }
-  if (mono)
-    for (int i = threadIdx.x; i < 4 * 256; i += kSplitThreads) (&sm.mono[0][0])[i] = 0;
-
-  double gain = 0.0;
-  const uint32_t b_self = threadIdx.x;
-
-  for (uint32_t c = 0; c < a.n_nodes; c += kSplitWarps) {
-    const uint32_t nd = c + warp;
-    if (nd < a.n_nodes) {
-      long long vg[8], vh[8];
-#pragma unroll
-      for (int i = 0; i < 8; i++) {
-        const uint32_t b = lane * 8 + i;
-        long long xg = 0, xh = 0;
-        if (b < nb) {
-          if (a.mode == 0) {
-            const long long* p = a.hb + (((size_t)nd * nf + f) * nb + b) * 2;
-            xg = p[0];
-            xh = p[1];
-          } else {
-            const long long* po = a.hb + (((size_t)(nd >> 1) * nf + f) * nb + b) * 2;
-            if (nd & 1u) {
-              xg = po[0];
-              xh = po[1];
-            } else {
-              const long long* pp = a.hp + (((size_t)(nd >> 1) * nf + f) * nb + b) * 2;
-              xg = pp[0] - po[0];
-              xh = pp[1] - po[1];
-            }
-          }
-          long long* q = a.hf + (((size_t)nd * nf + f) * nb + b) * 2;
-          q[0] = xg;
-          q[1] = xh;
-        }
-        vg[i] = xg;
-        vh[i] = xh;
-      }
-#pragma unroll
-      for (int i = 1; i < 8; i++) {
-        vg[i] += vg[i - 1];
-        vh[i] += vh[i - 1];
-      }
-      long long sg = vg[7], sh = vh[7];
-#pragma unroll
-      for (int d = 1; d < 32; d <<= 1) {
-        const long long tg = shfl_up_ll(sg, d), th = shfl_up_ll(sh, d);
-        if (lane >= d) {
-          sg += tg;
-          sh += th;
-        }
-      }
-      const long long eg = sg - vg[7], eh = sh - vh[7];
-      const long long totg = __shfl_sync(0xffffffffu, sg, 31);
-      const long long toth = __shfl_sync(0xffffffffu, sh, 31);
-      const double gt = (double)totg * inv_g;
-      const double ht = (double)toth * inv_h;
-      const double parent = gt * gt / (ht + lambda);
-#pragma unroll
-      for (int i = 0; i < 8; i++) {
-        const uint32_t b = lane * 8 + i;
-        if (b < nsplit) {
-          const long long pgi = vg[i] + eg, phi = vh[i] + eh;
-          const double gl = (double)pgi * inv_g;
-          const double hl = (double)phi * inv_h;
-          const double gr = gt - gl, hr = ht - hl;
-          const double valid = (double)((hl >= mc) & (hr >= mc));
-          sm.term[warp][b] = valid * (gl * gl / (hl + lambda) + gr * gr / (hr + lambda) - parent);
-          if (mono) {
-            atomicAdd(reinterpret_cast<unsigned long long*>(&sm.mono[0][b]), (unsigned long long)pgi);
-            atomicAdd(reinterpret_cast<unsigned long long*>(&sm.mono[1][b]), (unsigned long long)phi);
-            atomicAdd(reinterpret_cast<unsigned long long*>(&sm.mono[2][b]),
-                      (unsigned long long)(totg - pgi));
-            atomicAdd(reinterpret_cast<unsigned long long*>(&sm.mono[3][b]),
-                      (unsigned long long)(toth - phi));
-          }
-        }
-      }
-    }
-    __syncthreads();
-    if (b_self < nsplit) {
-      const uint32_t cnt = (a.n_nodes - c) < (uint32_t)kSplitWarps ? (a.n_nodes - c) : kSplitWarps;
-      for (uint32_t w = 0; w < cnt; w++) gain += sm.term[w][b_self];
-    }
-    __syncthreads();
-  }
-
-  // candidate masks (extensions): per-tree column sampling and monotone direction
-  const bool dropped = a.colsample < 1.0f &&
-                       (float)hash01_bits(f, a.tree_seed ^ 0x5bd1e995u) / 16777215.0f >=
-                           a.colsample;
+  if (a.zero_u32 && f == 0)
+    for (uint32_t w = threadIdx.x; w < a.zero_words; w += kBestThreads) a.zero_u32[w] = 0u;
+  const double inv_g = q_inv_scale(a.maxbits[0]), inv_h = q_inv_scale(a.maxbits[1]);
+  const double lambda = a.lambda;
   double key = -RW_INF;
-  if (b_self < nsplit) {
+  if (b < nsplit) {
+    double gain = 0.0;
+    const double* t = a.term + (size_t)f * a.n_nodes * nsplit + b;
+    for (uint32_t nd = 0; nd < a.n_nodes; nd++) gain += __ldcg(t + (size_t)nd * nsplit);
     key = gain;
-    if (dropped) key = -1e30;
-    else if (mono) {
-      const double glt = (double)sm.mono[0][b_self] * inv_g;
-      const double hlt = (double)sm.mono[1][b_self] * inv_h;
-      const double grt = (double)sm.mono[2][b_self] * inv_g;
-      const double hrt = (double)sm.mono[3][b_self] * inv_h;
+    // candidate masks (extensions): per-tree column sampling and monotone direction
+    const int mono = a.mono ? a.monotone[f] : 0;
+    const bool dropped = a.colsample < 1.0f &&
+                         (float)hash01_bits(f, a.tree_seed ^ 0x5bd1e995u) / 16777215.0f >=
+                             a.colsample;
+    if (mono) {
+      long long* m = a.mono + ((size_t)f * nsplit + b) * 4;
+      const double glt = (double)__ldcg(m + 0) * inv_g, hlt = (double)__ldcg(m + 1) * inv_h;
+      const double grt = (double)__ldcg(m + 2) * inv_g, hrt = (double)__ldcg(m + 3) * inv_h;
+      m[0] = m[1] = m[2] = m[3] = 0;  // ready for the next level
       const double wl = -glt / (hlt + lambda);
       const double wr = -grt / (hrt + lambda);
-      if ((mono > 0 && wl > wr) || (mono < 0 && wl < wr)) key = -1e30;
+      if (!dropped && ((mono > 0 && wl > wr) || (mono < 0 && wl < wr))) key = -1e30;
     }
+    if (dropped) key = -1e30;
     if (key != key) key = -RW_INF;  // NaN never wins (cpu.rs: `gv > bg`)
   }
-  uint32_t idx = b_self;
-  block_argmax(key, idx, sm);
+  uint32_t idx = b;
+  block_argmax256(key, idx, red_g, red_i);
   if (threadIdx.x == 0) {
-    a.best_gain[f] = key;
-    a.best_bin[f] = key == -RW_INF ? 0u : idx;
-    __threadfence();
-    const uint32_t ticket = atomicAdd(a.counter, 1u);
-    sm.last = ticket == nf - 1;
+    // ties: the lowest bin; an all-infeasible feature reports bin 0
+    const uint32_t bb = key == -RW_INF ? 0u : idx;
+    s_b = bb;
+    SplitRec r;
+    r.gain = key;
+    r.bin = bb;
+    r.thr = a.cuts[(size_t)f * nsplit + bb];
+    a.rec[f] = r;
   }
+  if (!a.last_level) return;
   __syncthreads();
-  if (!sm.last) return;
-  __threadfence();
-
-  // Last CTA: argmax across features (lowest feature wins ties) and model write.
-  double bk = -RW_INF;
-  uint32_t bf = 0xffffffffu;
-  for (uint32_t ff = threadIdx.x; ff < nf; ff += kSplitThreads)
-    argmax_merge(bk, bf, __ldcg(a.best_gain + ff), ff);
-  block_argmax(bk, bf, sm);
-  if (threadIdx.x == 0) {
-    if (bk == -RW_INF) bf = 0;
-    const uint32_t bb = __ldcg(a.best_bin + bf);
-    sm.s_f = bf;
-    sm.s_b = bb;
-    a.feat[a.slot] = bf;
-    a.thr[a.slot] = a.cuts[(size_t)bf * nsplit + bb];
-    if (a.thr_bin) a.thr_bin[a.slot] = (uint16_t)bb;
-    a.split_ft[0] = bf;
-    a.split_ft[1] = bb;
-    a.fi_gain[bf] += (float)(bk > 0.0 ? bk : 0.0);
-    a.fi_count[bf] += 1.0f;
-    *a.counter = 0u;
-  }
-  __syncthreads();
-  if (a.last_level) {
-    const uint32_t fs = sm.s_f, bs = sm.s_b;
-    for (uint32_t nd = threadIdx.x; nd < a.n_nodes; nd += kSplitThreads) {
-      long long lg = 0, lh = 0, tg = 0, th = 0;
-      const long long* p = a.hf + (((size_t)nd * nf + fs) * nb) * 2;
-      for (uint32_t b = 0; b < nb; b++) {
-        const long long xg = __ldcg(p + 2 * b), xh = __ldcg(p + 2 * b + 1);
-        tg += xg;
-        th += xh;
-        if (b <= bs) {
-          lg += xg;
-          lh += xh;
-        }
-      }
-      const long long rg = tg - lg, rh = th - lh;
-      const double lgd = (double)lg * inv_g, lhd = (double)lh * inv_h;
-      const double rgd = (double)rg * inv_g, rhd = (double)rh * inv_h;
-      a.leafval[a.leaf_base + 2 * nd] = (float)(-a.lr * lgd / (lhd + lambda));
-      a.leafval[a.leaf_base + 2 * nd + 1] = (float)(-a.lr * rgd / (rhd + lambda));
-    }
+  // Last level: the leaf values this feature's best split would give (src/cpu.rs:286-318
+  // from the exact per-node prefix sums k_gain kept), one thread per node; k_apply keeps
+  // the winning feature's.
+  const uint32_t bs = s_b;
+  for (uint32_t nd = threadIdx.x; nd < a.n_nodes; nd += kBestThreads) {
+    const longlong2* pr = reinterpret_cast<const longlong2*>(a.prefix) + ((size_t)f * a.n_nodes + nd) * nb;
+    const longlong2 l = __ldcg(pr + bs), tt = __ldcg(pr + nb - 1);
+    const long long lg = l.x, lh = l.y, tg = tt.x, th = tt.y;
+    const long long rg = tg - lg, rh = th - lh;
+    const double lgd = (double)lg * inv_g, lhd = (double)lh * inv_h;
+    const double rgd = (double)rg * inv_g, rhd = (double)rh * inv_h;
+    float* out = a.leafc + (size_t)f * (2 * a.n_nodes);
+    out[2 * nd] = (float)(-a.lr * lgd / (lhd + lambda));
+    out[2 * nd + 1] = (float)(-a.lr * rgd / (rhd + lambda));
   }
 }
 
 // --------------------------------------------------------------------------------
 
-__global__ void k_bin(const float* __restrict__ x, uint64_t n, uint32_t nf,
-                      const float* __restrict__ cuts, uint32_t nb1, uint8_t* __restrict__ bins,
-                      BinLayout lay, uint32_t f0, uint32_t fcount) {
-  extern __shared__ float s_cuts[];
-  for (uint32_t i = threadIdx.x; i < fcount * nb1; i += blockDim.x)
-    s_cuts[i] = cuts[(size_t)f0 * nb1 + i];
+// Binning (src/gpu_kernels.rs:496-529 == src/cpu.rs:149-155): bin = #{cut < v}, by binary
+// search over the feature's cuts (staged in shared memory); NaN compares false, giving
+// bin 0. One CTA bins 256 rows of one 64-feature tile: it writes colbins directly and
+// the rows' tile of rowbins through a shared [256][64] staging block (16-byte stores).
+constexpr int kBinRows = 256;
+
+__global__ void __launch_bounds__(kBinRows) k_bin(const float* __restrict__ x, uint64_t n,
+                                                  uint32_t nf, const float* __restrict__ cuts,
+                                                  uint32_t nb1, uint64_t n_pad,
+                                                  uint8_t* __restrict__ colbins,
+                                                  uint8_t* __restrict__ rowbins) {
+  extern __shared__ __align__(16) unsigned char bin_smem[];
+  uint8_t* tile = bin_smem;                                        // [kBinRows][kHistFeat]
+  float* s_cuts = reinterpret_cast<float*>(bin_smem + kBinRows * kHistFeat);  // [64][nb1]
+  const uint32_t t = blockIdx.y, f0 = t * kHistFeat;
+  const uint32_t fc = nf - f0 < kHistFeat ? nf - f0 : kHistFeat;
+  for (uint32_t i = threadIdx.x; i < fc * nb1; i += kBinRows) s_cuts[i] = cuts[(size_t)f0 * nb1 + i];
+  for (uint32_t i = threadIdx.x; i < kBinRows * kHistFeat / 16; i += kBinRows)
+    reinterpret_cast<uint4*>(tile)[i] = make_uint4(0u, 0u, 0u, 0u);
   __syncthreads();
-  const uint64_t r = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (r >= n) return;
-  for (uint32_t fl = 0; fl < fcount; fl++) {
-    const float v = __ldg(x + r * nf + f0 + fl);
-    const float* c = s_cuts + (size_t)fl * nb1;
-    uint32_t lo = 0, hi = nb1;
-    while (lo < hi) {
-      const uint32_t mid = (lo + hi) >> 1;
-      if (c[mid] < v) lo = mid + 1;
-      else hi = mid;
+  const uint64_t r0 = (uint64_t)blockIdx.x * kBinRows, r = r0 + threadIdx.x;
+  if (r < n) {
+    for (uint32_t fl = 0; fl < fc; fl++) {
+      const float v = __ldg(x + r * nf + f0 + fl);
+      const float* c = s_cuts + (size_t)fl * nb1;
+      uint32_t lo = 0, hi = nb1;
+      while (lo < hi) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (c[mid] < v) lo = mid + 1;
+        else hi = mid;
+      }
+      colbins[(size_t)(f0 + fl) * n_pad + r] = (uint8_t)lo;
+      tile[threadIdx.x * kHistFeat + fl] = (uint8_t)lo;
     }
-    bins[lay.offset(f0 + fl, r)] = (uint8_t)lo;
+  }
+  __syncthreads();
+  // rows r0 .. r0+255 of tile t (rows past n stay zero; n_pad is a multiple of 256)
+  for (uint32_t i = threadIdx.x; i < kBinRows * kHistFeat / 16; i += kBinRows) {
+    const uint32_t row = i / (kHistFeat / 16), part = i % (kHistFeat / 16);
+    if (r0 + row < n_pad)
+      *reinterpret_cast<uint4*>(rowbins + ((size_t)t * n_pad + r0 + row) * kHistFeat + part * 16) =
+          reinterpret_cast<const uint4*>(tile)[i];
   }
 }
 
-// 4-bit packing (src/gpu_kernels.rs:628-643): byte = bin(2k) | bin(2k+1) << 4 within each
-// feature row of each tile.
-__global__ void k_pack4(const uint8_t* __restrict__ bins, BinLayout lu, uint64_t n_pad,
-                        uint8_t* __restrict__ packed, BinLayout lp) {
-  const uint64_t pairs = n_pad / 2 * lu.nf;
-  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < pairs;
+// 4-bit packing (src/gpu_kernels.rs:628-643 packs pairs the same way): within each row's
+// feature tile, byte k = bin(2k) | bin(2k+1) << 4. One thread per 16 output bytes.
+__global__ void k_pack4(const uint8_t* __restrict__ u8, uint64_t n_pad, uint32_t ftiles,
+                        uint8_t* __restrict__ packed) {
+  const uint64_t items = n_pad * ftiles * 2;  // 2 x 16 output bytes per row tile
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < items;
        i += (uint64_t)gridDim.x * blockDim.x) {
-    const uint32_t f = (uint32_t)(i % lu.nf);
-    const uint64_t r = (i / lu.nf) * 2;
-    const uint8_t lo = bins[lu.offset(f, r)] & 0x0f;
-    const uint8_t hi = bins[lu.offset(f, r + 1)] & 0x0f;
-    packed[lp.offset(f, r)] = (uint8_t)(lo | (hi << 4));
+    const uint64_t r = i / (ftiles * 2);
+    const uint32_t rem = (uint32_t)(i % (ftiles * 2)), t = rem / 2, half = rem % 2;
+    const uint8_t* src = u8 + ((size_t)t * n_pad + r) * kHistFeat + half * 32;
+    const uint4 a = *reinterpret_cast<const uint4*>(src);
+    const uint4 b = *reinterpret_cast<const uint4*>(src + 16);
+    const uint32_t in[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    uint32_t out[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const uint32_t lo = in[2 * k], hi = in[2 * k + 1];
+      // bytes (b0 b1 b2 b3) -> nibble pairs (b0|b1<<4, b2|b3<<4)
+      const uint32_t plo = (lo & 0xfu) | ((lo >> 4) & 0xf0u) | (((lo >> 16) & 0xfu) << 8) |
+                           (((lo >> 24) & 0xfu) << 12);
+      const uint32_t phi = (hi & 0xfu) | ((hi >> 4) & 0xf0u) | (((hi >> 16) & 0xfu) << 8) |
+                           (((hi >> 24) & 0xfu) << 12);
+      out[k] = plo | (phi << 16);
+    }
+    *reinterpret_cast<uint4*>(packed + ((size_t)t * n_pad + r) * (kHistFeat / 2) + half * 16) =
+        make_uint4(out[0], out[1], out[2], out[3]);
   }
 }
 
@@ -648,14 +657,13 @@ __global__ void k_grad(const float* __restrict__ pred, const float* __restrict__
 }
 
 // Per round: q = round(x * 2^e) for g and h (scales from the final maxima), the row's
-// excluded flag (node bit 15; a row whose g and h both quantise to 0 adds nothing to
-// any sum), node reset and the level-0 build slot. Also zeroes the level-0 histogram.
+// excluded flag (node bit 15; a row whose g and h both quantise to 0 adds nothing to any
+// sum) and node reset. Also zeroes the level-0 histogram.
 constexpr uint16_t kExcluded = 0x8000;
 
 __global__ void k_quant(const float* __restrict__ g, const float* __restrict__ h,
                         const uint32_t* __restrict__ maxbits, uint64_t n_pad,
-                        int32_t* __restrict__ qg, int32_t* __restrict__ qh,
-                        uint16_t* __restrict__ node, int16_t* __restrict__ slot,
+                        int2* __restrict__ q, uint16_t* __restrict__ node,
                         long long* __restrict__ hb0, uint64_t hb0_words) {
   const float sg = rw_pow2f(rw_qscale_exp(maxbits[0]));
   const float sh = rw_pow2f(rw_qscale_exp(maxbits[1]));
@@ -664,62 +672,200 @@ __global__ void k_quant(const float* __restrict__ g, const float* __restrict__ h
   for (uint64_t w = tid; w < hb0_words; w += nthr) hb0[w] = 0;
   for (uint64_t i = tid; i < n_pad; i += nthr) {
     const int32_t a = rw_quantize(g[i], sg), b = rw_quantize(h[i], sh);
-    const bool excl = (a | b) == 0;
-    qg[i] = a;
-    qh[i] = b;
-    node[i] = excl ? kExcluded : 0;
-    slot[i] = excl ? -1 : 0;
+    q[i] = make_int2(a, b);
+    node[i] = (a | b) == 0 ? kExcluded : 0;
   }
 }
 
-// leaf = 2*leaf + (bin[f*] > t*) (src/cpu.rs:278-281) for 4 rows per thread, keeping the
-// excluded flag; then either the next level's build slot (odd children keyed by the
-// parent when subtracting, else the node itself; -1 when excluded or not built), or, at
-// the last level, pred += leafval[leaf] (src/cpu.rs:319-320).
-__global__ void k_apply(const uint8_t* __restrict__ bins, BinLayout lay,
-                        uint16_t* __restrict__ node, int16_t* __restrict__ slot,
-                        const uint32_t* __restrict__ split_ft, uint64_t n4, int next_odd_only,
-                        int final_level, const float* __restrict__ leafval, uint32_t leaf_base,
-                        float* __restrict__ pred) {
-  const uint32_t f = split_ft[0], t = split_ft[1];
-  for (uint64_t q = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; q < n4;
-       q += (uint64_t)gridDim.x * blockDim.x) {
-    const uint64_t r = q * 4;
-    uint32_t b4;
-    if (lay.packed) {
-      const uint32_t p = *reinterpret_cast<const uint16_t*>(bins + lay.offset(f, r));
-      b4 = (p & 0xfu) | ((p & 0xf0u) << 4) | ((p & 0xf00u) << 8) | ((p & 0xf000u) << 12);
-    } else {
-      b4 = *reinterpret_cast<const uint32_t*>(bins + lay.offset(f, r));
+// Every CTA first picks the level's split from the per-feature records (highest gain,
+// ties to the lowest feature: src/cpu.rs:271; no feasible split anywhere gives feature
+// 0, bin 0); CTA 0 also writes the model slot and feature importance
+// (src/cpu.rs:272-276) and, at the last level, the tree's leaf values.
+// Then leaf = 2*leaf + (bin[f*] > t*) (src/cpu.rs:278-281) for 4 rows per thread, keeping
+// the excluded flag. Non-final levels count the non-excluded rows of every child (block
+// counts in shared memory, warp-aggregated, then one global add per nonzero child); the
+// final level adds the tree's leaf value to pred (src/cpu.rs:319-320).
+constexpr int kApplyThreads = 256;
+
+__global__ void __launch_bounds__(kApplyThreads) k_apply(ApplyLaunch a) {
+  extern __shared__ uint32_t s_cnt[];
+  __shared__ double red_g[kApplyThreads / 32];
+  __shared__ uint32_t red_i[kApplyThreads / 32];
+  __shared__ uint32_t s_ft[2];
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const bool counting = !a.final_level && a.cnt;
+  if (counting)
+    for (uint32_t c = threadIdx.x; c < a.n_children; c += blockDim.x) s_cnt[c] = 0u;
+  {
+    double bk = -RW_INF;
+    uint32_t bf = 0xffffffffu;
+    for (uint32_t ff = threadIdx.x; ff < a.nf; ff += blockDim.x)
+      argmax_merge(bk, bf, __ldcg(&a.rec[ff].gain), ff);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const double g2 = __shfl_down_sync(0xffffffffu, bk, off);
+      const uint32_t i2 = __shfl_down_sync(0xffffffffu, bf, off);
+      if (lane + off < 32) argmax_merge(bk, bf, g2, i2);
     }
-    uint2 nd2 = *reinterpret_cast<const uint2*>(node + r);
-    uint32_t nds[4] = {nd2.x & 0xffffu, nd2.x >> 16, nd2.y & 0xffffu, nd2.y >> 16};
-    int sl[4];
+    if (lane == 0) {
+      red_g[warp] = bk;
+      red_i[warp] = bf;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      for (int w = 1; w < kApplyThreads / 32; w++) argmax_merge(bk, bf, red_g[w], red_i[w]);
+      if (bk == -RW_INF) bf = 0;
+      const uint32_t bb = __ldcg(&a.rec[bf].bin);
+      s_ft[0] = bf;
+      s_ft[1] = bb;
+      if (blockIdx.x == 0) {
+        a.feat[a.slot] = bf;
+        a.thr[a.slot] = __ldcg(&a.rec[bf].thr);
+        if (a.thr_bin) a.thr_bin[a.slot] = (uint16_t)bb;
+        a.fi_gain[bf] += (float)(bk > 0.0 ? bk : 0.0);
+        a.fi_count[bf] += 1.0f;
+        if (a.split_out) {
+          a.split_out[0] = bf;
+          a.split_out[1] = bb;
+        }
+      }
+    }
+    __syncthreads();
+  }
+  const uint32_t f = s_ft[0], t = s_ft[1];
+  const float* lv = a.final_level ? a.leafc + (size_t)f * a.n_leaves : nullptr;
+  if (a.final_level && blockIdx.x == 0)
+    for (uint32_t l = threadIdx.x; l < a.n_leaves; l += blockDim.x)
+      a.leafval[a.leaf_base + l] = __ldcg(lv + l);
+  const uint8_t* col = a.colbins + (size_t)f * a.n_pad;
+  const uint64_t n4 = a.n_pad / 4;
+  // every lane of a warp runs the same number of iterations (match_any needs them all)
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  const uint64_t warp_first = (uint64_t)blockIdx.x * blockDim.x + warp * 32;
+  for (uint64_t wq = warp_first; wq < n4; wq += stride) {
+    const uint64_t qi = wq + lane;
+    const bool live = qi < n4;
+    uint32_t nds[4] = {kExcluded, kExcluded, kExcluded, kExcluded};
+    if (live) {
+      const uint64_t r = qi * 4;
+      const uint32_t b4 = *reinterpret_cast<const uint32_t*>(col + r);
+      uint2 nd2 = *reinterpret_cast<const uint2*>(a.node + r);
+      nds[0] = nd2.x & 0xffffu;
+      nds[1] = nd2.x >> 16;
+      nds[2] = nd2.y & 0xffffu;
+      nds[3] = nd2.y >> 16;
+#pragma unroll
+      for (int s = 0; s < 4; s++) {
+        const uint32_t ex = nds[s] & kExcluded;
+        nds[s] = ex | ((nds[s] & 0x7fffu) * 2u + (((b4 >> (8 * s)) & 0xffu) > t ? 1u : 0u));
+      }
+      nd2.x = (nds[0] & 0xffffu) | (nds[1] << 16);
+      nd2.y = (nds[2] & 0xffffu) | (nds[3] << 16);
+      *reinterpret_cast<uint2*>(a.node + r) = nd2;
+      if (a.final_level) {
+        float4 p4 = *reinterpret_cast<const float4*>(a.pred + r);
+        p4.x += __ldg(lv + (nds[0] & 0x7fffu));
+        p4.y += __ldg(lv + (nds[1] & 0x7fffu));
+        p4.z += __ldg(lv + (nds[2] & 0x7fffu));
+        p4.w += __ldg(lv + (nds[3] & 0x7fffu));
+        *reinterpret_cast<float4*>(a.pred + r) = p4;
+      }
+    }
+    if (counting) {
+#pragma unroll
+      for (int s = 0; s < 4; s++) {
+        const uint32_t key = (nds[s] & kExcluded) ? 0xffffffffu : nds[s];
+        const uint32_t peers = __match_any_sync(0xffffffffu, key);
+        if (key != 0xffffffffu && lane == (uint32_t)(__ffs(peers) - 1))
+          atomicAdd(&s_cnt[key], (uint32_t)__popc(peers));
+      }
+    }
+  }
+  if (counting) {
+    __syncthreads();
+    for (uint32_t c = threadIdx.x; c < a.n_children; c += blockDim.x)
+      if (s_cnt[c]) atomicAdd(a.cnt + c, s_cnt[c]);
+  }
+}
+
+// The next level's row list (levels 0 .. D-2). Every CTA derives the groups' sizes and
+// list offsets from the child counts (identical in all CTAs); CTA 0 also publishes them
+// with the built-child flags. Then each CTA lists its slice of rows: warp-aggregated
+// shared-memory ranks per group, one global cursor reservation per nonempty group, and a
+// store of the row id at seg[group] + reservation + rank. Row order inside a group
+// depends on scheduling; the histograms it feeds do not.
+constexpr int kListThreads = 512;
+constexpr uint32_t kListRowsPerCta = kListThreads * 4;
+
+__global__ void __launch_bounds__(kListThreads)
+    k_rowlist(const uint16_t* __restrict__ node, uint64_t n_pad, uint32_t n_children,
+              int subtract, int force_odd, RowLists rl) {
+  extern __shared__ uint32_t ls[];
+  const uint32_t groups = subtract ? n_children / 2 : n_children;
+  uint32_t* s_seg = ls;               // [groups + 1]
+  uint32_t* s_cnt = ls + groups + 1;  // [groups]
+  uint32_t* s_base = s_cnt + groups;  // [groups]
+  uint8_t* s_odd = reinterpret_cast<uint8_t*>(s_base + groups);  // [groups]
+  // group sizes -> exclusive offsets (sequential chunks per thread, then a serial pass
+  // over the chunk totals by thread 0; groups <= 2^11)
+  for (uint32_t k = threadIdx.x; k < groups; k += kListThreads) {
+    uint32_t sz;
+    if (subtract) {
+      const uint32_t ce = __ldcg(rl.cnt + 2 * k), co = __ldcg(rl.cnt + 2 * k + 1);
+      const uint8_t odd = (force_odd || co <= ce) ? 1 : 0;
+      s_odd[k] = odd;
+      sz = odd ? co : ce;
+    } else {
+      sz = __ldcg(rl.cnt + k);
+    }
+    s_seg[k + 1] = sz;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    s_seg[0] = 0u;
+    for (uint32_t k = 0; k < groups; k++) s_seg[k + 1] += s_seg[k];
+  }
+  __syncthreads();
+  if (blockIdx.x == 0) {
+    for (uint32_t k = threadIdx.x; k <= groups; k += kListThreads) rl.seg[k] = s_seg[k];
+    if (subtract)
+      for (uint32_t k = threadIdx.x; k < groups; k += kListThreads) rl.built_odd[k] = s_odd[k];
+  }
+  const uint32_t lane = threadIdx.x & 31;
+  for (uint64_t r0 = (uint64_t)blockIdx.x * kListRowsPerCta; r0 < n_pad;
+       r0 += (uint64_t)gridDim.x * kListRowsPerCta) {
+    for (uint32_t k = threadIdx.x; k < groups; k += kListThreads) s_cnt[k] = 0u;
+    __syncthreads();
+    uint32_t key[4], rank[4];
 #pragma unroll
     for (int s = 0; s < 4; s++) {
-      const uint32_t ex = nds[s] & kExcluded;
-      const uint32_t leaf = (nds[s] & 0x7fffu) * 2u + (((b4 >> (8 * s)) & 0xffu) > t ? 1u : 0u);
-      nds[s] = ex | leaf;
-      if (ex) sl[s] = -1;
-      else if (next_odd_only) sl[s] = (leaf & 1u) ? (int)(leaf >> 1) : -1;
-      else sl[s] = (int)leaf;
+      const uint64_t r = r0 + (uint64_t)s * kListThreads + threadIdx.x;
+      key[s] = 0xffffffffu;
+      if (r < n_pad) {
+        const uint32_t nd = node[r];
+        if (!(nd & kExcluded)) {
+          if (!subtract) key[s] = nd;
+          else if ((nd & 1u) == s_odd[nd >> 1]) key[s] = nd >> 1;
+        }
+      }
+      const uint32_t peers = __match_any_sync(0xffffffffu, key[s]);
+      const uint32_t leader = (uint32_t)(__ffs(peers) - 1);
+      uint32_t base = 0u;
+      if (key[s] != 0xffffffffu && lane == leader) base = atomicAdd(&s_cnt[key[s]], (uint32_t)__popc(peers));
+      base = __shfl_sync(0xffffffffu, base, (int)leader);
+      rank[s] = base + (uint32_t)__popc(peers & ((1u << lane) - 1u));
     }
-    nd2.x = (nds[0] & 0xffffu) | (nds[1] << 16);
-    nd2.y = (nds[2] & 0xffffu) | (nds[3] << 16);
-    *reinterpret_cast<uint2*>(node + r) = nd2;
-    if (final_level) {
-      float4 p4 = *reinterpret_cast<const float4*>(pred + r);
-      p4.x += leafval[leaf_base + (nds[0] & 0x7fffu)];
-      p4.y += leafval[leaf_base + (nds[1] & 0x7fffu)];
-      p4.z += leafval[leaf_base + (nds[2] & 0x7fffu)];
-      p4.w += leafval[leaf_base + (nds[3] & 0x7fffu)];
-      *reinterpret_cast<float4*>(pred + r) = p4;
-    } else {
-      uint2 s2;
-      s2.x = ((uint32_t)sl[0] & 0xffffu) | ((uint32_t)sl[1] << 16);
-      s2.y = ((uint32_t)sl[2] & 0xffffu) | ((uint32_t)sl[3] << 16);
-      *reinterpret_cast<uint2*>(slot + r) = s2;
+    __syncthreads();
+    for (uint32_t k = threadIdx.x; k < groups; k += kListThreads)
+      if (s_cnt[k]) s_base[k] = atomicAdd(rl.cursor + k, s_cnt[k]);
+    __syncthreads();
+#pragma unroll
+    for (int s = 0; s < 4; s++) {
+      if (key[s] == 0xffffffffu) continue;
+      const uint64_t at = (uint64_t)s_seg[key[s]] + s_base[key[s]] + rank[s];
+      if (at < n_pad) rl.rows[at] = (uint32_t)(r0 + (uint64_t)s * kListThreads + threadIdx.x);
     }
+    __syncthreads();
   }
 }
 
@@ -837,208 +983,98 @@ int sm_count() {
   return n;
 }
 
-// Shared-memory plan of one histogram CTA: the histogram (8 bytes per cell, FT*FPL
-// features) plus dummy cells, plus two stages of (FT*FPL bins rows + 10 bytes of row
-// state) x tile rows. Prefers two features per lane at FT = 32 (per-row work shared by
-// both features), then one feature per lane with FT halving, then group chunks.
-struct HistPlan {
-  int ft, fpl;
-  uint32_t gchunk, tile, stride, stage_bytes, hist_bytes;
-  size_t smem;
-};
-
-HistPlan plan_hist(uint32_t nb, uint32_t groups, uint32_t nf, bool packed) {
-  const uint64_t budget = kSmemPerSm - 2048;
-  struct Cand {
-    int ft, fpl;
-  };
-  const Cand cands[] = {{32, 2}, {32, 1}, {16, 1}, {8, 1}, {4, 1}, {2, 1}, {1, 1}};
-  const uint32_t rs = (packed ? kBinTile / 2 : kBinTile) + 16;
-  for (uint32_t gchunk = groups; gchunk >= 1; gchunk = gchunk > 1 ? (gchunk + 1) / 2 : 0) {
-    for (const Cand& c : cands) {
-      if (c.fpl == 2 && nf <= 32) continue;
-      if (c.fpl == 1 && c.ft > 1 && (uint32_t)c.ft / 2 >= nf) continue;  // no idle tile lanes
-      const uint32_t ftt = (uint32_t)(c.ft * c.fpl);
-      const uint32_t stage = ftt * rs + 10u * kBinTile;
-      const uint64_t hist = 8ull * gchunk * nb * ftt;
-      if (hist + kStages * (uint64_t)stage <= budget) {
-        HistPlan p{};
-        p.ft = c.ft;
-        p.fpl = c.fpl;
-        p.gchunk = gchunk;
-        p.tile = kBinTile;
-        p.stride = rs;
-        p.stage_bytes = (stage + 127) / 128 * 128;
-        p.hist_bytes = (uint32_t)((hist + 127) / 128 * 128);
-        p.smem = p.hist_bytes + kStages * (size_t)p.stage_bytes;
-        return p;
-      }
-    }
-    if (gchunk == 1) break;
-  }
-  HistPlan none{};
-  return none;
-}
-
-// Occupancy of one histogram kernel configuration, queried once per (kernel, smem):
-// co-resident clusters for cluster sizes kMaxCluster, /2, ..., 1 (size 1 = CTAs).
-struct HistOcc {
-  int max_clusters[4];
-};
-
-// The kernel's dynamic shared memory limit only ever grows, so a launch that needs less
-// than an earlier one of the same kernel (another level, bin count or dataset) still fits.
-const HistOcc* hist_occupancy(const void* kfn, size_t smem) {
+// The dynamic shared-memory limit of a kernel only ever grows (per device), so a launch
+// that needs less than an earlier one of the same kernel still fits. Returns the CTAs
+// per SM for (kernel, block size, shared bytes), cached.
+static int set_smem_and_occupancy(const void* kfn, int threads, size_t smem) {
   static std::mutex mu;
-  static std::map<std::pair<std::pair<int, const void*>, size_t>, HistOcc> cache;
-  static std::map<std::pair<int, const void*>, size_t> smem_limit;
+  static std::map<std::pair<int, const void*>, size_t> limit;
+  static std::map<std::pair<std::pair<int, const void*>, size_t>, int> occ;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
   std::lock_guard<std::mutex> lock(mu);
   const auto kd = std::make_pair(dev, kfn);
-  size_t& lim = smem_limit[kd];
+  size_t& lim = limit[kd];
   if (smem > lim) {
     if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess)
-      return nullptr;
+      return 0;
     lim = smem;
   }
-  auto key = std::make_pair(kd, smem);
-  auto it = cache.find(key);
-  if (it != cache.end()) return &it->second;
-  HistOcc o{};
-  int per_sm = 1;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, kHistThreads, smem) !=
-          cudaSuccess ||
-      per_sm < 1)
-    per_sm = 1;
-  for (int ci = 0, cl = kMaxCluster; cl >= 1; cl >>= 1, ci++) {
-    if (cl == 1) {
-      o.max_clusters[ci] = sm_count() * per_sm;
-      continue;
-    }
-    cudaLaunchConfig_t q = {};
-    q.gridDim = dim3(cl, 1, 1);
-    q.blockDim = dim3(kHistThreads);
-    q.dynamicSmemBytes = smem;
-    cudaLaunchAttribute qa[1];
-    qa[0].id = cudaLaunchAttributeClusterDimension;
-    qa[0].val.clusterDim.x = cl;
-    qa[0].val.clusterDim.y = 1;
-    qa[0].val.clusterDim.z = 1;
-    q.attrs = qa;
-    q.numAttrs = 1;
-    int maxc = 0;
-    if (cudaOccupancyMaxActiveClusters(&maxc, kfn, &q) != cudaSuccess) maxc = 0;
-    o.max_clusters[ci] = maxc;
-  }
-  return &(cache[key] = o);
+  const auto key = std::make_pair(kd, smem);
+  auto it = occ.find(key);
+  if (it != occ.end()) return it->second;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, threads, smem) != cudaSuccess)
+    per_sm = 0;
+  occ[key] = per_sm;
+  return per_sm;
 }
+
+// All training kernels ask for the maximum shared-memory carveout, so consecutive
+// launches of the level loop never change the SM's L1/shared split between them.
+static void prefer_max_smem(const void* kfn) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, bool> done;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return;
+  std::lock_guard<std::mutex> lock(mu);
+  bool& d = done[std::make_pair(dev, kfn)];
+  if (d) return;
+  cudaFuncSetAttribute(kfn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                       cudaSharedmemCarveoutMaxShared);
+  d = true;
+}
+#define RW_PREFER_SMEM(k) prefer_max_smem(reinterpret_cast<const void*>(&k))
 
 cudaError_t launch_hist(const HistLaunch& L, cudaStream_t s, int* n_launch) {
-  const HistPlan P = plan_hist(L.nb, L.groups, L.nf, L.lay.packed != 0);
-  if (P.smem == 0) return cudaErrorInvalidConfiguration;
-  const uint32_t ftt = (uint32_t)(P.ft * P.fpl);
-  const uint32_t ftiles = (L.nf + ftt - 1) / ftt;
-  const uint32_t gz = (L.groups + P.gchunk - 1) / P.gchunk;
-  const void* kfn =
-      L.lay.packed ? pick_hist<true>(P.ft, P.fpl) : pick_hist<false>(P.ft, P.fpl);
-  const HistOcc* occ = hist_occupancy(kfn, P.smem);
-  if (!occ) return cudaErrorInvalidConfiguration;
-  const uint64_t units = L.n_pad / P.tile;  // n_pad is a multiple of the tile
-  const uint64_t tiles_of = (uint64_t)ftiles * gz;
-  // One wave: pick the cluster size whose co-resident clusters (clusters must fit inside
-  // a GPC, so not every SM can host one) hold the most CTAs, then size the row chunks
-  // so that every (feature tile, group chunk) gets the same whole number of clusters.
-  uint64_t best_ctas = 0, rchunks = 1;
-  int cluster = 1;
-  for (int ci = 0, cl = kMaxCluster; cl >= 1; cl >>= 1, ci++) {
-    const int maxc = occ->max_clusters[ci];
-    if (maxc < 1) continue;
-    uint64_t per_tile = (uint64_t)maxc / tiles_of;  // clusters per (feature tile, group)
-    if (per_tile < 1) per_tile = 1;
-    uint64_t rc = per_tile * (uint64_t)cl;
-    if (rc > units) rc = units / cl * cl;
-    if (rc < (uint64_t)cl) continue;
-    const uint64_t ctas = rc * tiles_of;
-    if (ctas > best_ctas + best_ctas / 16) {  // larger clusters unless they cost >6% of CTAs
-      best_ctas = ctas;
-      rchunks = rc;
-      cluster = cl;
-    }
-  }
-  // No CTA accumulates more than kMaxRowsPerCta rows (larger inputs take more waves).
-  constexpr uint64_t kMaxTiles = kMaxRowsPerCta / kBinTile;
-  if ((units + rchunks - 1) / rchunks > kMaxTiles) {
-    rchunks = (units + kMaxTiles - 1) / kMaxTiles;
-    rchunks = (rchunks + cluster - 1) / cluster * cluster;
-  }
-  const uint64_t tiles_per = (units + rchunks - 1) / rchunks;
-  const uint64_t rows = tiles_per * P.tile;
-
-  HistArgs a;
-  a.bins = L.bins;
-  a.lay = L.lay;
-  a.slot = L.slot;
-  a.qg = L.qg;
-  a.qh = L.qh;
-  a.n_pad = L.n_pad;
-  a.nf = L.nf;
-  a.nb = L.nb;
-  a.gchunk = P.gchunk;
-  a.out = L.out;
-  a.err = L.err;
-  a.rows_per_cta = rows;
-  a.stage_bytes = P.stage_bytes;
-  a.hist_bytes = P.hist_bytes;
-  dim3 grid((unsigned)rchunks, ftiles, gz);
+  if (L.nb < 2 || L.nb > 256 || (L.packed && L.nb > 16)) return cudaErrorInvalidValue;
+  const uint32_t ftiles = (L.nf + kHistFeat - 1) / kHistFeat;
+  const uint32_t tb = L.packed ? kHistFeat / 2 : kHistFeat;
+  const size_t smem = (size_t)(L.nb + 1) * 2 * kHistFeat * 4 +  // + the dummy bin row
+                      (L.rows ? 0 : (size_t)kStreamStages * kStreamRows * (tb + 8));
+  if (!L.rows && (L.n_ident % kStreamRows) != 0) return cudaErrorInvalidValue;
+  const void* kfn = L.packed ? reinterpret_cast<const void*>(&k_hist<true>)
+                             : reinterpret_cast<const void*>(&k_hist<false>);
+  const int per_sm = set_smem_and_occupancy(kfn, kHistThreads, smem);
+  if (per_sm < 1) return cudaErrorInvalidConfiguration;
+  const int grid = sm_count() * per_sm;
   if (n_launch) (*n_launch)++;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(kHistThreads);
-  cfg.dynamicSmemBytes = P.smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = cluster;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  void* args[] = {&a};
-  return cudaLaunchKernelExC(&cfg, kfn, args);
+  RW_PREFER_SMEM(k_hist<true>);
+  RW_PREFER_SMEM(k_hist<false>);
+  if (L.packed) k_hist<true><<<grid, kHistThreads, smem, s>>>(L, ftiles);
+  else k_hist<false><<<grid, kHistThreads, smem, s>>>(L, ftiles);
+  return cudaGetLastError();
 }
 
-cudaError_t launch_split(const SplitLaunch& a, cudaStream_t s) {
-  const size_t smem = sizeof(SplitSmem);
-  cudaError_t e = cudaFuncSetAttribute(k_split, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
-  if (e != cudaSuccess) return e;
-  k_split<<<a.nf, kSplitThreads, smem, s>>>(a);
+cudaError_t launch_split(const SplitLaunch& a, cudaStream_t s, int* nl) {
+  if (a.nb > (uint32_t)kGainThreads) return cudaErrorInvalidValue;
+  RW_PREFER_SMEM(k_gain);
+  RW_PREFER_SMEM(k_best);
+  const uint32_t ftiles = (a.nf + kHistFeat - 1) / kHistFeat;
+  k_gain<<<dim3(a.n_nodes, ftiles * (kHistFeat / kGainCols)), kGainThreads, 0, s>>>(a);
+  k_best<<<a.nf, kBestThreads, 0, s>>>(a);
+  if (nl) (*nl) += 2;
   return cudaGetLastError();
 }
 
 cudaError_t launch_bin(const float* x, uint64_t n, uint32_t nf, const float* d_cuts,
-                       uint32_t n_bins, uint8_t* d_bins, const BinLayout& lay, cudaStream_t s,
-                       int* nl) {
-  const uint32_t nb1 = n_bins - 1;
-  const uint32_t per = (48 * 1024) / (4 * (nb1 ? nb1 : 1));
-  const uint32_t ftile = per < 1 ? 1 : (per > nf ? nf : per);
-  for (uint32_t f0 = 0; f0 < nf; f0 += ftile) {
-    const uint32_t fc = nf - f0 < ftile ? nf - f0 : ftile;
-    const unsigned blocks = (unsigned)((n + 255) / 256);
-    k_bin<<<blocks, 256, (size_t)fc * nb1 * 4, s>>>(x, n, nf, d_cuts, nb1, d_bins, lay, f0, fc);
-    if (nl) (*nl)++;
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-  }
-  return cudaSuccess;
+                       uint32_t n_bins, uint64_t n_pad, uint8_t* d_colbins, uint8_t* d_rowbins,
+                       cudaStream_t s, int* nl) {
+  const uint32_t nb1 = n_bins - 1, ftiles = (nf + kHistFeat - 1) / kHistFeat;
+  const size_t smem = (size_t)kBinRows * kHistFeat + (size_t)kHistFeat * nb1 * 4;
+  if (set_smem_and_occupancy(reinterpret_cast<const void*>(&k_bin), kBinRows, smem) < 1)
+    return cudaErrorInvalidConfiguration;
+  dim3 grid((unsigned)(n_pad / kBinRows), ftiles);
+  k_bin<<<grid, kBinRows, smem, s>>>(x, n, nf, d_cuts, nb1, n_pad, d_colbins, d_rowbins);
+  if (nl) (*nl)++;
+  return cudaGetLastError();
 }
 
-cudaError_t launch_pack4(const uint8_t* d_bins, const BinLayout& lay_u8, uint64_t n_pad,
-                         uint8_t* d_packed, const BinLayout& lay_p, cudaStream_t s, int* nl) {
-  k_pack4<<<grid_for(n_pad / 2 * lay_u8.nf, 256), 256, 0, s>>>(d_bins, lay_u8, n_pad, d_packed,
-                                                               lay_p);
+cudaError_t launch_pack4(const uint8_t* d_u8, uint64_t n_pad, uint32_t nf, uint8_t* d_packed,
+                         cudaStream_t s, int* nl) {
+  const uint32_t ftiles = (nf + kHistFeat - 1) / kHistFeat;
+  k_pack4<<<grid_for(n_pad * ftiles * 2, 256), 256, 0, s>>>(d_u8, n_pad, ftiles, d_packed);
   if (nl) (*nl)++;
   return cudaGetLastError();
 }
@@ -1047,6 +1083,7 @@ cudaError_t launch_grad(const float* pred, const float* y, float* g, float* h, u
                         uint64_t n_pad, int logistic, uint64_t stride, uint64_t phase,
                         uint64_t row_offset, int compute_max, uint32_t* maxbits,
                         cudaStream_t s, int* nl) {
+  RW_PREFER_SMEM(k_grad);
   k_grad<<<grid_for(n_pad, 256), 256, 0, s>>>(pred, y, g, h, n, n_pad, logistic, stride, phase,
                                                row_offset, compute_max, maxbits);
   if (nl) (*nl)++;
@@ -1054,21 +1091,35 @@ cudaError_t launch_grad(const float* pred, const float* y, float* g, float* h, u
 }
 
 cudaError_t launch_quant(const float* g, const float* h, const uint32_t* maxbits, uint64_t n_pad,
-                         int32_t* qg, int32_t* qh, uint16_t* node, int16_t* slot,
-                         long long* hb0, uint64_t hb0_words, cudaStream_t s, int* nl) {
-  k_quant<<<grid_for(n_pad, 256), 256, 0, s>>>(g, h, maxbits, n_pad, qg, qh, node, slot, hb0,
-                                               hb0_words);
+                         int2* q, uint16_t* node, long long* hb0, uint64_t hb0_words,
+                         cudaStream_t s, int* nl) {
+  RW_PREFER_SMEM(k_quant);
+  k_quant<<<grid_for(n_pad, 256), 256, 0, s>>>(g, h, maxbits, n_pad, q, node, hb0, hb0_words);
   if (nl) (*nl)++;
   return cudaGetLastError();
 }
 
-cudaError_t launch_apply(const uint8_t* bins, const BinLayout& lay, uint16_t* node,
-                         int16_t* slot, const uint32_t* split_ft, uint64_t n_pad,
-                         int next_odd_only, int final_level, const float* leafval,
-                         uint32_t leaf_base, float* pred, cudaStream_t s, int* nl) {
-  const uint64_t n4 = n_pad / 4;
-  k_apply<<<grid_for(n4, 256), 256, 0, s>>>(bins, lay, node, slot, split_ft, n4, next_odd_only,
-                                             final_level, leafval, leaf_base, pred);
+cudaError_t launch_apply(const ApplyLaunch& a, cudaStream_t s, int* nl) {
+  const uint64_t n4 = a.n_pad / 4;
+  const size_t smem = a.final_level ? 0 : (size_t)a.n_children * 4;
+  RW_PREFER_SMEM(k_apply);
+  k_apply<<<grid_for(n4, kApplyThreads), kApplyThreads, smem, s>>>(a);
+  if (nl) (*nl)++;
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rowlist(const uint16_t* node, uint64_t n_pad, uint32_t n_children,
+                           int subtract, int force_odd, const RowLists& rl, cudaStream_t s,
+                           int* nl) {
+  const uint32_t groups = subtract ? n_children / 2 : n_children;
+  const size_t smem = ((size_t)groups * 3 + 1) * 4 + groups;
+  if (set_smem_and_occupancy(reinterpret_cast<const void*>(&k_rowlist), kListThreads, smem) < 1)
+    return cudaErrorInvalidConfiguration;
+  uint64_t blocks = (n_pad + kListRowsPerCta - 1) / kListRowsPerCta;
+  if (blocks > (uint64_t)sm_count() * 4) blocks = (uint64_t)sm_count() * 4;
+  RW_PREFER_SMEM(k_rowlist);
+  k_rowlist<<<(unsigned)blocks, kListThreads, smem, s>>>(node, n_pad, n_children, subtract,
+                                                        force_odd, rl);
   if (nl) (*nl)++;
   return cudaGetLastError();
 }
@@ -1087,6 +1138,7 @@ cudaError_t launch_goss_init(const GossState& st, uint64_t k, cudaStream_t s, in
 
 cudaError_t launch_goss_digit_hist(const float* g, uint64_t n, const GossState& st, int pass,
                                    cudaStream_t s, int* nl) {
+  RW_PREFER_SMEM(k_goss_digit_hist);
   k_goss_digit_hist<<<grid_for(n, 256), 256, 0, s>>>(g, n, st.counts, st.sel, pass);
   if (nl) (*nl)++;
   return cudaGetLastError();
@@ -1101,6 +1153,7 @@ cudaError_t launch_goss_digit_select(const GossState& st, int pass, cudaStream_t
 cudaError_t launch_goss_apply(float* g, float* h, uint64_t n, uint64_t row_offset,
                               const GossState& st, double keep_prob, float fact, uint64_t seed,
                               uint32_t* maxbits, cudaStream_t s, int* nl) {
+  RW_PREFER_SMEM(k_goss_apply);
   k_goss_apply<<<grid_for(n, 256), 256, 0, s>>>(g, h, n, row_offset, st.sel, keep_prob, fact,
                                                  seed, maxbits);
   if (nl) (*nl)++;
