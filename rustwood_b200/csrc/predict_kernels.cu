@@ -15,6 +15,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
+
 #include "rw_internal.cuh"
 
 namespace {
@@ -74,6 +76,68 @@ __global__ void __launch_bounds__(kPredThreads) k_predict_u8_simd(
     for (int s = 0; s < 4; s++)
       if (r0 + s < n) out[r0 + s] = acc[s];
   }
+}
+
+// Tiled u8 scorer (depth D <= 8 known at compile time): a persistent CTA stages its tree
+// chunk in shared memory once, then walks row blocks of kTileRows rows. Per block the
+// rows' bins are staged feature-major in shared memory as one 32-bit word per (feature,
+// thread) -- the thread's 4 rows -- so every split's bins come from a conflict-free shared
+// load; a byte-SIMD compare gives the 4 rows' bits and one LOP3 places them at bit D-1-d of
+// each row's byte. Trees are scored in order and each row's sum is sequential f32 (the
+// same order as predict_cpu).
+constexpr uint32_t kTileRows = kPredThreads * 4;
+
+template <int D>
+__global__ void __launch_bounds__(kPredThreads) k_predict_u8_tiled(
+    const uint8_t* __restrict__ bins, uint64_t n, uint64_t ld, uint32_t nf, uint32_t t0,
+    uint32_t tc, const uint32_t* __restrict__ split8, const float* __restrict__ leafval,
+    float base, int first_chunk, float* __restrict__ out) {
+  extern __shared__ __align__(16) unsigned char pred_raw[];
+  float* s_leaf = reinterpret_cast<float*>(pred_raw);
+  uint32_t* s_split = reinterpret_cast<uint32_t*>(pred_raw + ((size_t)tc << D) * 4);
+  uint32_t* s_rows = s_split + (size_t)tc * D;  // [nf][kPredThreads]
+  stage_model(t0, tc, D, split8, leafval, s_split, s_leaf);
+  const uint32_t tid = threadIdx.x;
+  const uint64_t nblk = (n + kTileRows - 1) / kTileRows;
+  for (uint64_t blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
+    const uint64_t r0 = blk * kTileRows + (uint64_t)tid * 4;  // this thread's 4 rows
+    __syncthreads();  // the previous block's rows (and the model) are settled
+    for (uint32_t f = 0; f < nf; f++)
+      s_rows[f * kPredThreads + tid] =
+          r0 + 3 < ld ? __ldg(reinterpret_cast<const uint32_t*>(bins + (size_t)f * ld + r0)) : 0u;
+    __syncthreads();
+    float acc[4];
+    if (first_chunk) {
+      acc[0] = acc[1] = acc[2] = acc[3] = base;
+    } else {
+#pragma unroll
+      for (int k = 0; k < 4; k++) acc[k] = r0 + k < n ? out[r0 + k] : 0.0f;
+    }
+    const uint32_t* rows = s_rows + tid;
+    for (uint32_t t = 0; t < tc; t++) {
+      const uint32_t* sp = s_split + t * D;
+      uint32_t leaf4 = 0;
+#pragma unroll
+      for (int d = 0; d < D; d++) {
+        const uint32_t sv = sp[d];
+        const uint32_t m = __vcmpgtu4(rows[(sv >> 8) * kPredThreads], (sv & 0xffu) * 0x01010101u);
+        leaf4 |= m & (0x01010101u << (D - 1 - d));
+      }
+      const float* lv = s_leaf + ((size_t)t << D);
+      acc[0] += lv[leaf4 & 0xffu];
+      acc[1] += lv[(leaf4 >> 8) & 0xffu];
+      acc[2] += lv[(leaf4 >> 16) & 0xffu];
+      acc[3] += lv[leaf4 >> 24];
+    }
+#pragma unroll
+    for (int k = 0; k < 4; k++)
+      if (r0 + k < n) out[r0 + k] = acc[k];
+  }
+}
+
+template <int D>
+const void* tiled_fn() {
+  return reinterpret_cast<const void*>(&k_predict_u8_tiled<D>);
 }
 
 // One row per thread, any depth and any row stride.
@@ -151,11 +215,58 @@ int pred_grid(uint64_t work) {
 
 }  // namespace
 
+// The tiled scorer for depth 1..8 when the rows' bins fit next to a tree chunk.
+static cudaError_t launch_predict_u8_tiled(const uint8_t* bins, uint64_t n, uint64_t ld,
+                                           const rw_dmodel& m, float* out, cudaStream_t s,
+                                           bool* used) {
+  *used = false;
+  const size_t rows_bytes = (size_t)m.nf * kPredThreads * 4;
+  if (m.depth < 1 || m.depth > 8 || rows_bytes > 96 * 1024) return cudaSuccess;
+  const size_t per_tree = ((size_t)4 << m.depth) + 4 * (size_t)m.depth;
+  const size_t budget = 220 * 1024 - rows_bytes;
+  uint32_t tc = (uint32_t)std::min<size_t>(m.n_trees, budget / per_tree);
+  if (tc < 1) return cudaSuccess;
+  const void* fns[9] = {nullptr,          tiled_fn<1>(), tiled_fn<2>(), tiled_fn<3>(), tiled_fn<4>(),
+                        tiled_fn<5>(),    tiled_fn<6>(), tiled_fn<7>(), tiled_fn<8>()};
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const uint64_t nblk = (n + kTileRows - 1) / kTileRows;
+  for (uint32_t t0 = 0; t0 < m.n_trees; t0 += tc) {
+    const uint32_t c = m.n_trees - t0 < tc ? m.n_trees - t0 : tc;
+    const size_t smem = ((size_t)c << m.depth) * 4 + (size_t)c * m.depth * 4 + rows_bytes;
+    cudaError_t e = cudaFuncSetAttribute(fns[m.depth], cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    int per_sm = 1;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fns[m.depth], kPredThreads, smem);
+    const uint64_t grid = std::max<uint64_t>(1, std::min<uint64_t>(nblk, (uint64_t)sms * std::max(per_sm, 1)));
+    int first = t0 == 0;
+    uint64_t nn = n, ll = ld;
+    uint32_t nf = m.nf, tt0 = t0, cc = c;
+    const uint32_t* sp = m.d_split8;
+    const float* lp = m.d_leafval;
+    float b = m.base;
+    const uint8_t* bp = bins;
+    float* op = out;
+    void* args[] = {&bp, &nn, &ll, &nf, &tt0, &cc, &sp, &lp, &b, &first, &op};
+    e = cudaLaunchKernel(fns[m.depth], dim3((unsigned)grid), dim3(kPredThreads), args, smem, s);
+    if (e != cudaSuccess) return e;
+  }
+  *used = true;
+  return cudaSuccess;
+}
+
 cudaError_t launch_predict_u8(const uint8_t* bins, uint64_t n, uint64_t ld, const rw_dmodel& m,
                               float* out, cudaStream_t s) {
   if (n == 0) return cudaSuccess;
   const bool simd = m.depth <= 8 && (ld % 4) == 0 && ld >= ((n + 3) & ~3ull) &&
                     (reinterpret_cast<uintptr_t>(bins) % 4) == 0;
+  if (simd && m.n_trees > 0) {
+    bool used = false;
+    cudaError_t e = launch_predict_u8_tiled(bins, n, ld, m, out, s, &used);
+    if (e != cudaSuccess || used) return e;
+  }
   const uint32_t tc = trees_per_chunk(m.n_trees, m.depth, 4);
   for (uint32_t t0 = 0; t0 < m.n_trees; t0 += tc) {
     const uint32_t c = m.n_trees - t0 < tc ? m.n_trees - t0 : tc;

@@ -698,7 +698,8 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
   if (kerr_h) {
     cudaEventDestroy(ev0);
     cudaEventDestroy(ev1);
-    return fail(ctx, RW_ERR_TIMEOUT, "a histogram bulk-copy wait gave up (bounded wait expired)");
+    return fail(ctx, RW_ERR_TIMEOUT,
+                "a histogram bulk-copy wait gave up (bounded wait expired)");
   }
   RW_CU(ctx, cudaMemcpy(fi_gain, d_fi_gain.p, nf * 4, cudaMemcpyDeviceToHost));
   RW_CU(ctx, cudaMemcpy(fi_count, d_fi_count.p, nf * 4, cudaMemcpyDeviceToHost));

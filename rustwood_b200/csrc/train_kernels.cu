@@ -36,6 +36,15 @@
 
 namespace {
 
+// Programmatic dependent launch: the level loop is a chain of short kernels, each
+// launched with programmatic stream serialization so its launch and CTA setup overlap the
+// previous kernel's tail. Every kernel first waits for its predecessor grid to complete
+// (and its memory to be visible) and then lets its own successor launch.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 constexpr int kHistThreads = 1024;
 // Rows one histogram CTA accumulates into its 32-bit shared cells before adding them to
 // the global int64 cells: every |q| is at most 2^RW_QBITS, so a cell's partial sum
@@ -134,6 +143,7 @@ __device__ __forceinline__ void hist_add_row(uint32_t* hs, uint32_t bb, int2 qq,
 // 32+j feature 2j+1 -- and cleared.
 template <bool PACKED>
 __global__ void __launch_bounds__(kHistThreads) k_hist(HistLaunch a, uint32_t ftiles) {
+  pdl_enter();
   extern __shared__ __align__(16) uint32_t hs[];
   __shared__ __align__(8) uint64_t bar[kStreamStages];
   __shared__ int s_abort;
@@ -330,6 +340,7 @@ __device__ __forceinline__ double q_inv_scale(uint32_t maxbits) {
 constexpr uint32_t kGainCols = 4;
 
 __global__ void __launch_bounds__(kGainThreads) k_gain(SplitLaunch a) {
+  pdl_enter();
   __shared__ long long wsum[kGainThreads / 32][2 * kGainCols];
   __shared__ long long tot[2 * kGainCols];
   const uint32_t nd = blockIdx.x;
@@ -446,6 +457,7 @@ __global__ void __launch_bounds__(kGainThreads) k_gain(SplitLaunch a) {
 }
 
 __global__ void __launch_bounds__(kBestThreads) k_best(SplitLaunch a) {
+  pdl_enter();
   __shared__ double red_g[kBestThreads / 32];
   __shared__ uint32_t red_i[kBestThreads / 32];
   __shared__ uint32_t s_b;
@@ -632,6 +644,7 @@ __global__ void k_grad(const float* __restrict__ pred, const float* __restrict__
                        float* __restrict__ g, float* __restrict__ h, uint64_t n, uint64_t n_pad,
                        int logistic, uint64_t stride, uint64_t phase, uint64_t row_offset,
                        int compute_max, uint32_t* maxbits) {
+  pdl_enter();
   uint32_t mg = 0, mh = 0;
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_pad;
        i += (uint64_t)gridDim.x * blockDim.x) {
@@ -665,6 +678,7 @@ __global__ void k_quant(const float* __restrict__ g, const float* __restrict__ h
                         const uint32_t* __restrict__ maxbits, uint64_t n_pad,
                         int2* __restrict__ q, uint16_t* __restrict__ node,
                         long long* __restrict__ hb0, uint64_t hb0_words) {
+  pdl_enter();
   const float sg = rw_pow2f(rw_qscale_exp(maxbits[0]));
   const float sh = rw_pow2f(rw_qscale_exp(maxbits[1]));
   const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -687,7 +701,49 @@ __global__ void k_quant(const float* __restrict__ g, const float* __restrict__ h
 // final level adds the tree's leaf value to pred (src/cpu.rs:319-320).
 constexpr int kApplyThreads = 256;
 
+// The level's split from the per-feature records (every CTA), and by CTA 0 the model
+// slot and feature importance. Leaves (feature, bin) in s_ft.
+__device__ void choose_split(const ApplyLaunch& a, uint32_t* s_ft, double* red_g,
+                             uint32_t* red_i) {
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  double bk = -RW_INF;
+  uint32_t bf = 0xffffffffu;
+  for (uint32_t ff = threadIdx.x; ff < a.nf; ff += blockDim.x)
+    argmax_merge(bk, bf, __ldcg(&a.rec[ff].gain), ff);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const double g2 = __shfl_down_sync(0xffffffffu, bk, off);
+    const uint32_t i2 = __shfl_down_sync(0xffffffffu, bf, off);
+    if (lane + off < 32) argmax_merge(bk, bf, g2, i2);
+  }
+  if (lane == 0) {
+    red_g[warp] = bk;
+    red_i[warp] = bf;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (uint32_t w = 1; w < blockDim.x / 32; w++) argmax_merge(bk, bf, red_g[w], red_i[w]);
+    if (bk == -RW_INF) bf = 0;
+    const uint32_t bb = __ldcg(&a.rec[bf].bin);
+    s_ft[0] = bf;
+    s_ft[1] = bb;
+    if (blockIdx.x == 0) {
+      a.feat[a.slot] = bf;
+      a.thr[a.slot] = __ldcg(&a.rec[bf].thr);
+      if (a.thr_bin) a.thr_bin[a.slot] = (uint16_t)bb;
+      a.fi_gain[bf] += (float)(bk > 0.0 ? bk : 0.0);
+      a.fi_count[bf] += 1.0f;
+      if (a.split_out) {
+        a.split_out[0] = bf;
+        a.split_out[1] = bb;
+      }
+    }
+  }
+  __syncthreads();
+}
+
 __global__ void __launch_bounds__(kApplyThreads) k_apply(ApplyLaunch a) {
+  pdl_enter();
   extern __shared__ uint32_t s_cnt[];
   __shared__ double red_g[kApplyThreads / 32];
   __shared__ uint32_t red_i[kApplyThreads / 32];
@@ -696,42 +752,7 @@ __global__ void __launch_bounds__(kApplyThreads) k_apply(ApplyLaunch a) {
   const bool counting = !a.final_level && a.cnt;
   if (counting)
     for (uint32_t c = threadIdx.x; c < a.n_children; c += blockDim.x) s_cnt[c] = 0u;
-  {
-    double bk = -RW_INF;
-    uint32_t bf = 0xffffffffu;
-    for (uint32_t ff = threadIdx.x; ff < a.nf; ff += blockDim.x)
-      argmax_merge(bk, bf, __ldcg(&a.rec[ff].gain), ff);
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const double g2 = __shfl_down_sync(0xffffffffu, bk, off);
-      const uint32_t i2 = __shfl_down_sync(0xffffffffu, bf, off);
-      if (lane + off < 32) argmax_merge(bk, bf, g2, i2);
-    }
-    if (lane == 0) {
-      red_g[warp] = bk;
-      red_i[warp] = bf;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      for (int w = 1; w < kApplyThreads / 32; w++) argmax_merge(bk, bf, red_g[w], red_i[w]);
-      if (bk == -RW_INF) bf = 0;
-      const uint32_t bb = __ldcg(&a.rec[bf].bin);
-      s_ft[0] = bf;
-      s_ft[1] = bb;
-      if (blockIdx.x == 0) {
-        a.feat[a.slot] = bf;
-        a.thr[a.slot] = __ldcg(&a.rec[bf].thr);
-        if (a.thr_bin) a.thr_bin[a.slot] = (uint16_t)bb;
-        a.fi_gain[bf] += (float)(bk > 0.0 ? bk : 0.0);
-        a.fi_count[bf] += 1.0f;
-        if (a.split_out) {
-          a.split_out[0] = bf;
-          a.split_out[1] = bb;
-        }
-      }
-    }
-    __syncthreads();
-  }
+  choose_split(a, s_ft, red_g, red_i);
   const uint32_t f = s_ft[0], t = s_ft[1];
   const float* lv = a.final_level ? a.leafc + (size_t)f * a.n_leaves : nullptr;
   if (a.final_level && blockIdx.x == 0)
@@ -800,6 +821,7 @@ constexpr uint32_t kListRowsPerCta = kListThreads * 4;
 __global__ void __launch_bounds__(kListThreads)
     k_rowlist(const uint16_t* __restrict__ node, uint64_t n_pad, uint32_t n_children,
               int subtract, int force_odd, RowLists rl) {
+  pdl_enter();
   extern __shared__ uint32_t ls[];
   const uint32_t groups = subtract ? n_children / 2 : n_children;
   uint32_t* s_seg = ls;               // [groups + 1]
@@ -870,6 +892,7 @@ __global__ void __launch_bounds__(kListThreads)
 }
 
 __global__ void k_fill(float* p, float v, uint64_t n) {
+  pdl_enter();
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (uint64_t)gridDim.x * blockDim.x)
     p[i] = v;
@@ -878,6 +901,7 @@ __global__ void k_fill(float* p, float v, uint64_t n) {
 // ---- GOSS (src/cpu.rs:64-110): exact k-th largest |g| by MSB-first radix select ----
 
 __global__ void k_goss_init(uint32_t* sel, uint64_t k) {
+  pdl_enter();
   sel[0] = 0u;  // prefix
   sel[1] = 0u;  // mask of decided bits
   sel[2] = (uint32_t)k;
@@ -886,6 +910,7 @@ __global__ void k_goss_init(uint32_t* sel, uint64_t k) {
 
 __global__ void k_goss_digit_hist(const float* __restrict__ g, uint64_t n,
                                   unsigned long long* counts, const uint32_t* sel, int pass) {
+  pdl_enter();
   __shared__ uint32_t sc[256];
   for (int i = threadIdx.x; i < 256; i += blockDim.x) sc[i] = 0;
   __syncthreads();
@@ -904,6 +929,7 @@ __global__ void k_goss_digit_hist(const float* __restrict__ g, uint64_t n,
 // Walk digits from the largest down; the k-th largest (0-based) lies in the first
 // digit whose cumulative count exceeds k.
 __global__ void k_goss_digit_select(unsigned long long* counts, uint32_t* sel, int pass) {
+  pdl_enter();
   if (threadIdx.x != 0) return;
   const int shift = 24 - 8 * pass;
   unsigned long long k = sel[2], cum = 0;
@@ -927,6 +953,7 @@ __global__ void k_goss_digit_select(unsigned long long* counts, uint32_t* sel, i
 __global__ void k_goss_apply(float* __restrict__ g, float* __restrict__ h, uint64_t n,
                              uint64_t row_offset, const uint32_t* sel, double keep_prob,
                              float fact, uint64_t seed, uint32_t* maxbits) {
+  pdl_enter();
   const float thresh = __uint_as_float(sel[3]);
   uint32_t mg = 0, mh = 0;
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
@@ -966,6 +993,23 @@ int grid_for(uint64_t work, int threads) {
   if (b > (uint64_t)148 * 16) b = (uint64_t)148 * 16;
   if (b < 1) b = 1;
   return (int)b;
+}
+
+// Launches a level-loop kernel with programmatic stream serialization (see pdl_enter).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, args...);
 }
 
 }  // namespace
@@ -1042,9 +1086,8 @@ cudaError_t launch_hist(const HistLaunch& L, cudaStream_t s, int* n_launch) {
   if (n_launch) (*n_launch)++;
   RW_PREFER_SMEM(k_hist<true>);
   RW_PREFER_SMEM(k_hist<false>);
-  if (L.packed) k_hist<true><<<grid, kHistThreads, smem, s>>>(L, ftiles);
-  else k_hist<false><<<grid, kHistThreads, smem, s>>>(L, ftiles);
-  return cudaGetLastError();
+  return L.packed ? launch_pdl(k_hist<true>, dim3(grid), dim3(kHistThreads), smem, s, L, ftiles)
+                  : launch_pdl(k_hist<false>, dim3(grid), dim3(kHistThreads), smem, s, L, ftiles);
 }
 
 cudaError_t launch_split(const SplitLaunch& a, cudaStream_t s, int* nl) {
@@ -1052,8 +1095,10 @@ cudaError_t launch_split(const SplitLaunch& a, cudaStream_t s, int* nl) {
   RW_PREFER_SMEM(k_gain);
   RW_PREFER_SMEM(k_best);
   const uint32_t ftiles = (a.nf + kHistFeat - 1) / kHistFeat;
-  k_gain<<<dim3(a.n_nodes, ftiles * (kHistFeat / kGainCols)), kGainThreads, 0, s>>>(a);
-  k_best<<<a.nf, kBestThreads, 0, s>>>(a);
+  const uint32_t groups = ftiles * (kHistFeat / kGainCols);
+  cudaError_t e = launch_pdl(k_gain, dim3(a.n_nodes, groups), dim3(kGainThreads), 0, s, a);
+  if (e == cudaSuccess) e = launch_pdl(k_best, dim3(a.nf), dim3(kBestThreads), 0, s, a);
+  if (e != cudaSuccess) return e;
   if (nl) (*nl) += 2;
   return cudaGetLastError();
 }
@@ -1084,8 +1129,9 @@ cudaError_t launch_grad(const float* pred, const float* y, float* g, float* h, u
                         uint64_t row_offset, int compute_max, uint32_t* maxbits,
                         cudaStream_t s, int* nl) {
   RW_PREFER_SMEM(k_grad);
-  k_grad<<<grid_for(n_pad, 256), 256, 0, s>>>(pred, y, g, h, n, n_pad, logistic, stride, phase,
-                                               row_offset, compute_max, maxbits);
+  cudaError_t e = launch_pdl(k_grad, dim3(grid_for(n_pad, 256)), dim3(256), 0, s, pred, y, g, h, n,
+                             n_pad, logistic, stride, phase, row_offset, compute_max, maxbits);
+  if (e != cudaSuccess) return e;
   if (nl) (*nl)++;
   return cudaGetLastError();
 }
@@ -1094,7 +1140,9 @@ cudaError_t launch_quant(const float* g, const float* h, const uint32_t* maxbits
                          int2* q, uint16_t* node, long long* hb0, uint64_t hb0_words,
                          cudaStream_t s, int* nl) {
   RW_PREFER_SMEM(k_quant);
-  k_quant<<<grid_for(n_pad, 256), 256, 0, s>>>(g, h, maxbits, n_pad, q, node, hb0, hb0_words);
+  cudaError_t e = launch_pdl(k_quant, dim3(grid_for(n_pad, 256)), dim3(256), 0, s, g, h, maxbits,
+                             n_pad, q, node, hb0, hb0_words);
+  if (e != cudaSuccess) return e;
   if (nl) (*nl)++;
   return cudaGetLastError();
 }
@@ -1103,7 +1151,9 @@ cudaError_t launch_apply(const ApplyLaunch& a, cudaStream_t s, int* nl) {
   const uint64_t n4 = a.n_pad / 4;
   const size_t smem = a.final_level ? 0 : (size_t)a.n_children * 4;
   RW_PREFER_SMEM(k_apply);
-  k_apply<<<grid_for(n4, kApplyThreads), kApplyThreads, smem, s>>>(a);
+  cudaError_t e = launch_pdl(k_apply, dim3(grid_for(n4, kApplyThreads)), dim3(kApplyThreads), smem,
+                             s, a);
+  if (e != cudaSuccess) return e;
   if (nl) (*nl)++;
   return cudaGetLastError();
 }
@@ -1118,20 +1168,23 @@ cudaError_t launch_rowlist(const uint16_t* node, uint64_t n_pad, uint32_t n_chil
   uint64_t blocks = (n_pad + kListRowsPerCta - 1) / kListRowsPerCta;
   if (blocks > (uint64_t)sm_count() * 4) blocks = (uint64_t)sm_count() * 4;
   RW_PREFER_SMEM(k_rowlist);
-  k_rowlist<<<(unsigned)blocks, kListThreads, smem, s>>>(node, n_pad, n_children, subtract,
-                                                        force_odd, rl);
+  cudaError_t e = launch_pdl(k_rowlist, dim3((unsigned)blocks), dim3(kListThreads), smem, s, node,
+                             n_pad, n_children, subtract, force_odd, rl);
+  if (e != cudaSuccess) return e;
   if (nl) (*nl)++;
   return cudaGetLastError();
 }
 
 cudaError_t launch_fill_f32(float* p, float v, uint64_t n, cudaStream_t s, int* nl) {
-  k_fill<<<grid_for(n, 256), 256, 0, s>>>(p, v, n);
+  cudaError_t e = launch_pdl(k_fill, dim3(grid_for(n, 256)), dim3(256), 0, s, p, v, n);
+  if (e != cudaSuccess) return e;
   if (nl) (*nl)++;
   return cudaGetLastError();
 }
 
 cudaError_t launch_goss_init(const GossState& st, uint64_t k, cudaStream_t s, int* nl) {
-  k_goss_init<<<1, 1, 0, s>>>(st.sel, k);
+  cudaError_t e = launch_pdl(k_goss_init, dim3(1), dim3(1), 0, s, st.sel, k);
+  if (e != cudaSuccess) return e;
   if (nl) (*nl)++;
   return cudaGetLastError();
 }
@@ -1139,13 +1192,16 @@ cudaError_t launch_goss_init(const GossState& st, uint64_t k, cudaStream_t s, in
 cudaError_t launch_goss_digit_hist(const float* g, uint64_t n, const GossState& st, int pass,
                                    cudaStream_t s, int* nl) {
   RW_PREFER_SMEM(k_goss_digit_hist);
-  k_goss_digit_hist<<<grid_for(n, 256), 256, 0, s>>>(g, n, st.counts, st.sel, pass);
+  cudaError_t e = launch_pdl(k_goss_digit_hist, dim3(grid_for(n, 256)), dim3(256), 0, s, g, n,
+                             st.counts, st.sel, pass);
+  if (e != cudaSuccess) return e;
   if (nl) (*nl)++;
   return cudaGetLastError();
 }
 
 cudaError_t launch_goss_digit_select(const GossState& st, int pass, cudaStream_t s, int* nl) {
-  k_goss_digit_select<<<1, 32, 0, s>>>(st.counts, st.sel, pass);
+  cudaError_t e = launch_pdl(k_goss_digit_select, dim3(1), dim3(32), 0, s, st.counts, st.sel, pass);
+  if (e != cudaSuccess) return e;
   if (nl) (*nl)++;
   return cudaGetLastError();
 }
@@ -1154,8 +1210,9 @@ cudaError_t launch_goss_apply(float* g, float* h, uint64_t n, uint64_t row_offse
                               const GossState& st, double keep_prob, float fact, uint64_t seed,
                               uint32_t* maxbits, cudaStream_t s, int* nl) {
   RW_PREFER_SMEM(k_goss_apply);
-  k_goss_apply<<<grid_for(n, 256), 256, 0, s>>>(g, h, n, row_offset, st.sel, keep_prob, fact,
-                                                 seed, maxbits);
+  cudaError_t e = launch_pdl(k_goss_apply, dim3(grid_for(n, 256)), dim3(256), 0, s, g, h, n,
+                             row_offset, st.sel, keep_prob, fact, seed, maxbits);
+  if (e != cudaSuccess) return e;
   if (nl) (*nl)++;
   return cudaGetLastError();
 }

@@ -184,6 +184,35 @@ def test_predict_u8_random_model(ctx):
     np.testing.assert_array_equal(got32.view(np.uint32), want.view(np.uint32))
 
 
+def _raw_twin(bins, feat, thr_bin, nf, seed):
+    """Raw f32 rows and thresholds that bin to `bins` against a synthetic cut table."""
+    cuts = np.sort(np.random.default_rng(seed).standard_normal((nf, 255)).astype(np.float32),
+                   axis=1)
+    x = np.empty((bins.shape[1], nf), np.float32)
+    for f in range(nf):
+        x[:, f] = np.where(bins[f] < 255, cuts[f, np.minimum(bins[f], 254)], cuts[f, 254] + 1.0)
+    return x, cuts[feat, thr_bin]
+
+
+@pytest.mark.parametrize("depth,trees,nf,n", [
+    (1, 7, 3, 1), (4, 100, 20, 4097), (6, 500, 54, 2049), (8, 1200, 10, 5000),
+    (10, 50, 30, 3000), (6, 64, 120, 2000),
+])
+def test_predict_u8_shapes(ctx, depth, trees, nf, n):
+    """The u8 scorers (tiled shared-memory kernel for depth <= 8 with tree chunks, the
+    older byte-SIMD kernel for wide rows, the scalar kernel for depth > 8) against
+    predict_cpu on the raw-threshold twin of the same model."""
+    feat, thr_bin, leafval = synth.c5_model(n_trees=trees, depth=depth, nf=nf, seed=depth)
+    bins = synth.c5_bins(n, nf, seed=depth + 1)
+    x, thr = _raw_twin(bins, feat, thr_bin, nf, seed=depth + 2)
+    want = oracle.predict(x, feat, thr, leafval, -0.5, trees, depth)
+    b = rb.Booster(rb.Config(n_trees=trees, depth=depth), ctx)
+    b.n_features, b.base_score = nf, np.float32(-0.5)
+    b.feat, b.thr, b.thr_bin, b.leafval = feat, thr, thr_bin, leafval
+    got = b.predict_bins(bins)
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
 def test_fit_vs_faithful_cpu_rs(ctx):
     """Against oracle_ref (faithful cpu.rs, f32 histograms, glibc expf): identical splits
     except at near-ties, and test metrics within 1e-4."""
