@@ -66,16 +66,16 @@ struct rw_dmodel {
 // ---- kernel launchers (train_kernels.cu) ------------------------------------------
 
 // One level's histogram build. The rows to accumulate form a list grouped by histogram
-// group: group k's rows are rows[seg[k] .. seg[k+1]). Without a list, every row in
-// [0, n_ident) belongs to group 0.
+// group: group k's entries are entries[seg[k] .. seg[k+1]), each (row id, q(g), q(h), 0).
+// Without a list, every row in [0, n_ident) belongs to group 0 (q from `q`).
 struct HistLaunch {
   const uint8_t* rowbins;
   uint64_t n_pad;         // rows per tile in rowbins
   int packed;
   const int2* q;          // per row: (fixed-point g, fixed-point h), rw_quantize
-  const uint32_t* rows;   // row list, or nullptr for the identity list
+  const int4* entries;    // row list (row, qg, qh, 0), or nullptr for the identity list
   const uint32_t* seg;    // [groups + 1] list offsets (nullptr with the identity list)
-  uint32_t n_ident;       // identity list length, a multiple of 128 (rows past n have q = 0)
+  uint32_t n_ident;       // identity list length, a multiple of 512 (rows past n have q = 0)
   uint32_t groups;        // histogram groups written (out has `groups` slots)
   uint32_t nf, nb;
   long long* out;         // int64 [groups][nf][nb][2], zeroed by the caller
@@ -90,7 +90,8 @@ struct RowLists {
   uint32_t* cursor;     // [2^D] per-group scatter cursors
   uint32_t* seg;        // [2^D + 1] list offsets per group
   uint8_t* built_odd;   // [2^(D-1)] per node pair: 1 if the odd child's histogram is built
-  uint32_t* rows;       // [n_pad] the list
+  int4* entries;        // [n_pad] the list: (row, q(g), q(h), 0)
+  const int2* q;        // per row q, copied into the entries
 };
 
 // A feature's best split at one level: gain (-inf when no bin is feasible), threshold

@@ -471,7 +471,8 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
   WsBuf<float> pred, g, h, d_leafval, d_thr, d_fi_gain, d_fi_count;
   WsBuf<uint16_t> node, d_thr_bin;
   WsBuf<int2> q;
-  WsBuf<uint32_t> rl_rows, rl_counters, rl_seg;
+  WsBuf<uint32_t> rl_counters, rl_seg;
+  WsBuf<int4> rl_entries;
   WsBuf<uint8_t> rl_odd;
   WsBuf<long long> hb0, hb1, hf0, hf1;
   WsBuf<uint32_t> d_feat, maxbits;
@@ -487,7 +488,7 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
   RW_CU(ctx, h.get(ds, "h", n_pad));
   RW_CU(ctx, node.get(ds, "node", n_pad));
   RW_CU(ctx, q.get(ds, "q", n_pad));
-  RW_CU(ctx, rl_rows.get(ds, "rl_rows", n_pad));
+  RW_CU(ctx, rl_entries.get(ds, "rl_entries", n_pad));
   RW_CU(ctx, rl_counters.get(ds, "rl_counters", 2 * (size_t)NL));  // [cnt: NL][cursor: NL]
   RW_CU(ctx, rl_seg.get(ds, "rl_seg", (size_t)NL + 1));
   RW_CU(ctx, rl_odd.get(ds, "rl_odd", (size_t)NL / 2));
@@ -604,9 +605,9 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
       hl.n_pad = n_pad;
       hl.packed = ds->packed;
       hl.q = q.p;
-      hl.rows = d == 0 ? nullptr : rl_rows.p;  // level 0: every row
+      hl.entries = d == 0 ? nullptr : rl_entries.p;  // level 0: every row
       hl.seg = d == 0 ? nullptr : rl_seg.p;
-      hl.n_ident = (uint32_t)round_up(n, 128);  // rows past n carry q = 0
+      hl.n_ident = (uint32_t)round_up(n, 512);  // rows past n carry q = 0
       hl.err = kerr.p;
       hl.groups = groups;
       hl.nf = nf;
@@ -674,7 +675,7 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
       RW_CU(ctx, launch_apply(al, s, &nl));
       if (d + 1 < D) {
         // with several ranks every rank must build the same child of each pair
-        RowLists rl{rl_counters.p, rl_counters.p + NL, rl_seg.p, rl_odd.p, rl_rows.p};
+        RowLists rl{rl_counters.p, rl_counters.p + NL, rl_seg.p, rl_odd.p, rl_entries.p, q.p};
         RW_CU(ctx, launch_rowlist(node.p, n_pad, n_children, subtract ? 1 : 0,
                                   ctx->world > 1 ? 1 : 0, rl, s, &nl));
       }
@@ -990,23 +991,24 @@ extern "C" int rw_debug_level_hist(rw_dataset* ds, const int32_t* node, const fl
     seg[gi + 1]++;
   }
   for (uint32_t k = 0; k < groups; k++) seg[k + 1] += seg[k];
-  std::vector<uint32_t> rows(std::max<uint32_t>(seg[groups], 1));
+  std::vector<int4> rows(std::max<uint32_t>(seg[groups], 1), make_int4(0, 0, 0, 0));
   {
     std::vector<uint32_t> cur(seg.begin(), seg.end() - 1);
     for (uint64_t i = 0; i < n; i++)
-      if (grp[i] >= 0) rows[cur[grp[i]]++] = (uint32_t)i;
+      if (grp[i] >= 0) rows[cur[grp[i]]++] = make_int4((int)i, qv[i].x, qv[i].y, 0);
   }
   // device cells: [group][tile][bin][g|h][kHistFeat columns]; out: [group][nf][nb][2]
   const size_t words = (size_t)groups * ds->ftiles * ds->n_bins * 2 * kHistFeat;
   DBuf<int2> dq;
-  DBuf<uint32_t> drows, dseg;
+  DBuf<int4> drows;
+  DBuf<uint32_t> dseg;
   DBuf<long long> dout;
   RW_CU(ctx, dq.alloc(n_pad));
   RW_CU(ctx, drows.alloc(rows.size()));
   RW_CU(ctx, dseg.alloc(seg.size()));
   RW_CU(ctx, dout.alloc(words));
   RW_CU(ctx, cudaMemcpy(dq.p, qv.data(), n_pad * sizeof(int2), cudaMemcpyHostToDevice));
-  RW_CU(ctx, cudaMemcpy(drows.p, rows.data(), rows.size() * 4, cudaMemcpyHostToDevice));
+  RW_CU(ctx, cudaMemcpy(drows.p, rows.data(), rows.size() * sizeof(int4), cudaMemcpyHostToDevice));
   RW_CU(ctx, cudaMemcpy(dseg.p, seg.data(), seg.size() * 4, cudaMemcpyHostToDevice));
   RW_CU(ctx, cudaMemset(dout.p, 0, words * 8));
   HistLaunch hl;
@@ -1015,7 +1017,7 @@ extern "C" int rw_debug_level_hist(rw_dataset* ds, const int32_t* node, const fl
   hl.packed = ds->packed;
   hl.err = nullptr;
   hl.q = dq.p;
-  hl.rows = drows.p;
+  hl.entries = drows.p;
   hl.seg = dseg.p;
   hl.n_ident = 0;
   hl.groups = groups;

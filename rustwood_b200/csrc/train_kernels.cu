@@ -51,13 +51,18 @@ constexpr int kHistThreads = 1024;
 // stays within 2^30 in magnitude and the 32-bit word holds it exactly.
 constexpr uint32_t kMaxRowsPerCta = 1u << (30 - RW_QBITS);
 static_assert(kMaxRowsPerCta >= 1024, "quantisation too fine for the histogram row bound");
-// Row gathers in flight per warp step (32 warps per CTA keep 256 rows in flight per SM).
-constexpr int kHistU = 8;
+// A listed level gathers its rows through a ring of kListSlots shared-memory slots of
+// kListRows rows: the rows' list entries (row id, q) and their bin runs (cp.async 16-byte
+// copies, one per thread), issued two slots ahead of the slot being accumulated.
+constexpr uint32_t kListRows = 256;
+constexpr int kListSlots = 3;
+static_assert(kListRows * 4 == kHistThreads, "one 16-byte bin chunk per thread per slot");
 // The all-rows level streams its rows through shared memory in stages of kStreamRows
 // (one TMA bulk copy of the stage's bin rows and one of its q values), kStreamStages deep.
-constexpr uint32_t kStreamRows = 128;
-constexpr int kStreamStages = 4;
-static_assert(kStreamRows == (kHistThreads / 32) * 4, "one 4-row step per warp per stage");
+constexpr uint32_t kStreamRows = 512;
+constexpr int kStreamStages = 2;
+constexpr uint32_t kStreamRowsPerWarp = kStreamRows / (kHistThreads / 32);
+static_assert(kStreamRows % (kHistThreads / 32) == 0, "whole rows per warp per stage");
 
 // ---- TMA bulk copies and mbarriers (PTX) -------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -97,6 +102,19 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 }
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t bytes) {
+  // bytes < 16 zero-fills the rest (bytes == 0: nothing is read)
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 // Waits for the mbarrier phase with a ~1 s clock limit; false when the limit passed.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
@@ -153,7 +171,7 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(HistLaunch a, uint32_t ft
   const uint64_t total = (uint64_t)L * ftiles;
   // identity slices are whole stages (n_ident is a multiple of kStreamRows)
   uint64_t per = (total + gridDim.x - 1) / gridDim.x;
-  if (!a.rows) per = (per + kStreamRows - 1) / kStreamRows * kStreamRows;
+  if (!a.entries) per = (per + kStreamRows - 1) / kStreamRows * kStreamRows;
   uint64_t w = (uint64_t)blockIdx.x * per;
   const uint64_t w_end = min(total, w + per);
   if (w >= w_end) return;
@@ -163,7 +181,7 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(HistLaunch a, uint32_t ft
   for (uint32_t c = threadIdx.x; c < words; c += kHistThreads) hs[c] = 0u;
   if (threadIdx.x == 0) {
     s_abort = 0;
-    if (!a.rows) {
+    if (!a.entries) {
       for (int st = 0; st < kStreamStages; st++) mbar_init(&bar[st], 1);
       mbar_init_fence();
     }
@@ -190,7 +208,7 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(HistLaunch a, uint32_t ft
     const bool v0 = fbase + 2 * lane < a.nf, v1 = fbase + 2 * lane + 1 < a.nf;
     const unsigned char* tile = a.rowbins + (size_t)t * a.n_pad * TB;
     __syncthreads();  // cleared cells (and barrier init) are visible
-    if (!a.rows) {
+    if (!a.entries) {
       // ---- streamed: rows i0 .. i1 in stages of kStreamRows ----
       const uint32_t nst = (uint32_t)((i1 - i0) / kStreamRows);
       auto issue = [&](uint32_t k) {
@@ -214,8 +232,8 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(HistLaunch a, uint32_t ft
           const unsigned char* sp = stage0 + (size_t)st * kStageBytes;
           const int2* sq = reinterpret_cast<const int2*>(sp + kStreamRows * TB);
 #pragma unroll
-          for (int u = 0; u < 4; u++) {
-            const uint32_t r = warp * 4 + u;
+          for (int u = 0; u < (int)kStreamRowsPerWarp; u++) {
+            const uint32_t r = warp * kStreamRowsPerWarp + u;
             const uint32_t bb = PACKED ? (uint32_t)sp[r * TB + lane]
                                        : (uint32_t)*reinterpret_cast<const uint16_t*>(sp + r * TB + 2 * lane);
             hist_add_row<PACKED>(hs, bb, sq[r], lane, v0, v1, nb);
@@ -242,27 +260,56 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(HistLaunch a, uint32_t ft
       }
       phase_base += nst;
     } else {
-      // ---- gathered: the list's rows ----
-      const uint32_t boff = PACKED ? lane : 2 * lane;
-      for (uint32_t b = i0 + warp * kHistU; b < (uint32_t)i1; b += (kHistThreads / 32) * kHistU) {
-        // past the part's end a step reads row 0 and adds q = 0 (no divergent branches)
-        uint32_t rid[kHistU], bb[kHistU];
-        int2 qq[kHistU];
+      // ---- gathered: the list's rows, through the slot ring ----
+      // slot: [kListRows][TB] bin runs, then [kListRows] int4 entries (row, qg, qh, 0)
+      constexpr uint32_t kSlotBytes = kListRows * (TB + 16);
+      const uint32_t cnt = (uint32_t)(i1 - i0);
+      const uint32_t nsl = (cnt + kListRows - 1) / kListRows;
+      const uint32_t my_row = threadIdx.x / 4, my_part = threadIdx.x % 4;
+      auto load_entry = [&](uint32_t j) {  // this thread's entry of slot j (row my_row)
+        const uint32_t li = j * kListRows + my_row;
+        return li < cnt ? __ldg(a.entries + i0 + li) : make_int4(0, 0, 0, 0);
+      };
+      auto issue = [&](uint32_t j, int4 e) {
+        unsigned char* sp = stage0 + (size_t)(j % kListSlots) * kSlotBytes;
+        const bool live = j * kListRows + my_row < cnt;
+        if (my_part * 16 < TB)
+          cp_async16(sp + my_row * TB + my_part * 16,
+                     tile + (size_t)(live ? (uint32_t)e.x : 0u) * TB + my_part * 16,
+                     live ? 16u : 0u);
+        if (my_part == 0)
+          reinterpret_cast<int4*>(sp + kListRows * TB)[my_row] =
+              live ? e : make_int4(0, 0, 0, 0);
+        cp_async_commit();
+      };
+      int4 e_next = load_entry(0);
+      if (nsl > 0) issue(0, e_next);
+      else cp_async_commit();
+      e_next = load_entry(1);
+      if (nsl > 1) issue(1, e_next);
+      else cp_async_commit();
+      e_next = load_entry(2);
+      for (uint32_t j = 0; j < nsl; j++) {
+        cp_async_wait<1>();  // this thread's copies for slot j have landed
+        __syncthreads();     // ... and everyone else's
+        const unsigned char* sp = stage0 + (size_t)(j % kListSlots) * kSlotBytes;
+        const int4* se = reinterpret_cast<const int4*>(sp + kListRows * TB);
+        const uint32_t here = min(kListRows, cnt - j * kListRows);
 #pragma unroll
-        for (int u = 0; u < kHistU; u++) {
-          const uint32_t ii = b + u;
-          rid[u] = ii < (uint32_t)i1 ? __ldg(a.rows + ii) : 0u;
+        for (int u = 0; u < (int)(kListRows / (kHistThreads / 32)); u++) {
+          const uint32_t r = warp * (kListRows / (kHistThreads / 32)) + u;
+          if (r >= here) break;  // warp-uniform
+          const int4 e = se[r];
+          const uint32_t bb = PACKED ? (uint32_t)sp[r * TB + lane]
+                                     : (uint32_t)*reinterpret_cast<const uint16_t*>(sp + r * TB + 2 * lane);
+          hist_add_row<PACKED>(hs, bb, make_int2(e.y, e.z), lane, v0, v1, nb);
         }
-#pragma unroll
-        for (int u = 0; u < kHistU; u++) {
-          const unsigned char* rp = tile + (size_t)rid[u] * TB + boff;
-          bb[u] = PACKED ? (uint32_t)__ldg(rp) : (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(rp));
-          qq[u] = __ldg(a.q + rid[u]);
-          if (b + u >= (uint32_t)i1) qq[u] = make_int2(0, 0);
-        }
-#pragma unroll
-        for (int u = 0; u < kHistU; u++) hist_add_row<PACKED>(hs, bb[u], qq[u], lane, v0, v1, nb);
+        __syncthreads();  // slot j is free again
+        if (j + 2 < nsl) issue(j + 2, e_next);
+        else cp_async_commit();
+        e_next = load_entry(j + 3);
       }
+      cp_async_wait<0>();
     }
     __syncthreads();
     // the global cells of (grp, t) use the shared layout, so consecutive threads add
@@ -813,8 +860,8 @@ __global__ void __launch_bounds__(kApplyThreads) k_apply(ApplyLaunch a) {
 // list offsets from the child counts (identical in all CTAs); CTA 0 also publishes them
 // with the built-child flags. Then each CTA lists its slice of rows: warp-aggregated
 // shared-memory ranks per group, one global cursor reservation per nonempty group, and a
-// store of the row id at seg[group] + reservation + rank. Row order inside a group
-// depends on scheduling; the histograms it feeds do not.
+// store of the row's entry (row id and its q) at seg[group] + reservation + rank. Row
+// order inside a group depends on scheduling; the histograms it feeds do not.
 constexpr int kListThreads = 512;
 constexpr uint32_t kListRowsPerCta = kListThreads * 4;
 
@@ -885,7 +932,11 @@ __global__ void __launch_bounds__(kListThreads)
     for (int s = 0; s < 4; s++) {
       if (key[s] == 0xffffffffu) continue;
       const uint64_t at = (uint64_t)s_seg[key[s]] + s_base[key[s]] + rank[s];
-      if (at < n_pad) rl.rows[at] = (uint32_t)(r0 + (uint64_t)s * kListThreads + threadIdx.x);
+      if (at < n_pad) {
+        const uint32_t row = (uint32_t)(r0 + (uint64_t)s * kListThreads + threadIdx.x);
+        const int2 qv = rl.q[row];
+        rl.entries[at] = make_int4((int)row, qv.x, qv.y, 0);
+      }
     }
     __syncthreads();
   }
@@ -1076,8 +1127,9 @@ cudaError_t launch_hist(const HistLaunch& L, cudaStream_t s, int* n_launch) {
   const uint32_t ftiles = (L.nf + kHistFeat - 1) / kHistFeat;
   const uint32_t tb = L.packed ? kHistFeat / 2 : kHistFeat;
   const size_t smem = (size_t)(L.nb + 1) * 2 * kHistFeat * 4 +  // + the dummy bin row
-                      (L.rows ? 0 : (size_t)kStreamStages * kStreamRows * (tb + 8));
-  if (!L.rows && (L.n_ident % kStreamRows) != 0) return cudaErrorInvalidValue;
+                      (L.entries ? (size_t)kListSlots * kListRows * (tb + 16)
+                                 : (size_t)kStreamStages * kStreamRows * (tb + 8));
+  if (!L.entries && (L.n_ident % kStreamRows) != 0) return cudaErrorInvalidValue;
   const void* kfn = L.packed ? reinterpret_cast<const void*>(&k_hist<true>)
                              : reinterpret_cast<const void*>(&k_hist<false>);
   const int per_sm = set_smem_and_occupancy(kfn, kHistThreads, smem);
