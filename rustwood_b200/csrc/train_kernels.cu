@@ -488,9 +488,17 @@ __global__ void __launch_bounds__(kGainThreads) k_gain(SplitLaunch a) {
     const double parent = gt * gt / (ht + lambda);
     const double gl = (double)pgi * inv_g, hl = (double)phi * inv_h;
     const double gr = gt - gl, hr = ht - hl;
-    const double valid = (double)((hl >= mc) & (hr >= mc));
-    a.term[((size_t)f * a.n_nodes + nd) * nsplit + b] =
-        valid * (gl * gl / (hl + lambda) + gr * gr / (hr + lambda) - parent);
+    const double dl = hl + lambda, dr = hr + lambda;
+    // src/cpu.rs writes valid * (gl^2/(hl+lambda) + gr^2/(hr+lambda) - parent). FP64
+    // division is the costly part on this GPU, so an invalid threshold skips it when
+    // that product is a zero: both denominators nonzero (the quotients of these finite
+    // fixed-point sums are then finite). Its +0 in place of a possible -0 leaves the
+    // node-order sum unchanged (the sum starts at +0 and never becomes -0).
+    double term;
+    if ((hl >= mc) & (hr >= mc)) term = gl * gl / dl + gr * gr / dr - parent;
+    else if (dl != 0.0 && dr != 0.0 && parent - parent == 0.0) term = 0.0;
+    else term = 0.0 * (gl * gl / dl + gr * gr / dr - parent);
+    a.term[((size_t)f * a.n_nodes + nd) * nsplit + b] = term;
     if (a.mono && a.monotone[f] != 0) {
       // exact left/right (g, h) totals over all nodes for the monotone rule
       unsigned long long* m =
