@@ -65,33 +65,41 @@ struct rw_dmodel {
 
 // ---- kernel launchers (train_kernels.cu) ------------------------------------------
 
-// One level's histogram build. The rows to accumulate form a list grouped by histogram
-// group: group k's entries are entries[seg[k] .. seg[k+1]), each (row id, q(g), q(h), 0).
-// Without a list, every row in [0, n_ident) belongs to group 0 (q from `q`).
+// One level's histogram build. Without a list, every row in [0, n_ident) belongs to
+// group 0 (q from `q`). With a list, the entries (row id, q(g), q(h), 0) of the previous
+// level's node k occupy the region [cap(k), cap(k) + pcount[k]) of `entries`, cap = the
+// exclusive prefix of pcount (rows per node). With pairs != 0 group k is node k's built
+// child: its glen[k] entries start the region. With pairs == 0 group c is child c of node
+// c/2: the left child's glen[c] entries start the region, the right child's end it.
 struct HistLaunch {
   const uint8_t* rowbins;
   uint64_t n_pad;         // rows per tile in rowbins
   int packed;
   const int2* q;          // per row: (fixed-point g, fixed-point h), rw_quantize
-  const int4* entries;    // row list (row, qg, qh, 0), or nullptr for the identity list
-  const uint32_t* seg;    // [groups + 1] list offsets (nullptr with the identity list)
+  const int4* entries;    // the list, or nullptr for every row
+  const uint32_t* pcount; // [parents] non-excluded rows per previous-level node
+  const uint32_t* glen;   // [groups] entries per group
+  uint32_t parents;       // previous-level nodes
+  int pairs;              // 1: group k = node k's built child; 0: group c = child c
   uint32_t n_ident;       // identity list length, a multiple of 512 (rows past n have q = 0)
   uint32_t groups;        // histogram groups written (out has `groups` slots)
   uint32_t nf, nb;
-  long long* out;         // int64 [groups][nf][nb][2], zeroed by the caller
+  long long* out;         // int64 [groups][tile][nb][2][64], zeroed by the caller
   int* err;               // nullable: set to 1 if a bounded wait on a bulk copy gave up
 };
 cudaError_t launch_hist(const HistLaunch& a, cudaStream_t s, int* n_launch);
 
-// Per-level row lists: after a level's leaf-index update, the rows of the children that
-// the next level builds, grouped by histogram group.
-struct RowLists {
-  uint32_t* cnt;        // [2^D] rows per child node (non-excluded), counted by k_apply
-  uint32_t* cursor;     // [2^D] per-group scatter cursors
-  uint32_t* seg;        // [2^D + 1] list offsets per group
-  uint8_t* built_odd;   // [2^(D-1)] per node pair: 1 if the odd child's histogram is built
-  int4* entries;        // [n_pad] the list: (row, q(g), q(h), 0)
-  const int2* q;        // per row q, copied into the entries
+// Per-level row lists. At level d the leaf-index update writes, for the next level, the
+// entries of the rows to build into per-node regions sized by the node's row count
+// (ncount, known before the rows move), so no pass over all rows is needed to size them.
+struct LevelLists {
+  int4* entries;          // [n_pad] (row, q(g), q(h), 0)
+  const int2* q;          // per row q, copied into the entries
+  const uint32_t* ncount; // [n_nodes] non-excluded rows per node of this level
+  uint32_t* cursor;       // [groups] entries written per next-level group (zeroed before)
+  const uint8_t* choice;  // [nf][n_nodes] per feature: 1 = build the right (odd) child
+  uint8_t* built_odd;     // [n_nodes] out: the winning feature's choice row
+  int subtract;           // 1: list the built child of each pair; 0: list every child
 };
 
 // A feature's best split at one level: gain (-inf when no bin is feasible), threshold
@@ -111,8 +119,6 @@ struct SplitLaunch {
   uint32_t n_nodes, nf, nb;
   int mode;             // 0: hb holds every node; 1: hb holds one child per pair, keyed by parent
   const uint8_t* built_odd;  // mode 1: per pair, 1 if the odd child was built (else the even)
-  uint32_t* zero_u32;   // nullable: zero_words u32 zeroed here (next level's list counters)
-  uint32_t zero_words;
   const uint32_t* maxbits;
   double lambda, min_child, lr;
   const int32_t* monotone;  // device [nf] or null
@@ -125,6 +131,18 @@ struct SplitLaunch {
   SplitRec* rec;        // [nf] out
   int last_level;
   float* leafc;         // last level: [nf][2 * n_nodes] leaf values per candidate feature
+  uint8_t* choice;      // non-last levels, with subtraction: [nf][n_nodes] out, 1 = build
+                        // the right (odd) child of the node (the side with less hessian)
+  // per-node row counts of this level from the previous level's lists (level > 0):
+  // ncount[c] = cursor_prev[c/2] for the built child, pcount[c/2] - that for its sibling
+  // (with subtraction), or cursor_prev[c] (without); cursor_next is zeroed.
+  const uint32_t* pcount;
+  const uint32_t* cursor_prev;
+  const uint8_t* built_prev;
+  uint32_t* ncount;
+  uint32_t* cursor_next;
+  uint32_t cursor_next_words;
+  int subtract;
 };
 cudaError_t launch_split(const SplitLaunch& a, cudaStream_t s, int* nl);
 
@@ -138,15 +156,16 @@ cudaError_t launch_bin(const float* x_rowmajor, uint64_t n, uint32_t nf, const f
 // rowbins u8 -> 4-bit pairs (separate buffers).
 cudaError_t launch_pack4(const uint8_t* d_u8, uint64_t n_pad, uint32_t nf, uint8_t* d_packed,
                          cudaStream_t s, int* nl);
+// Also zeroes *zero_word (the level-0 row count k_quant accumulates), when non-null.
 cudaError_t launch_grad(const float* pred, const float* y, float* g, float* h, uint64_t n,
                         uint64_t n_pad, int logistic, uint64_t stride, uint64_t phase,
                         uint64_t row_offset, int compute_max, uint32_t* maxbits,
-                        cudaStream_t s, int* nl);
+                        uint32_t* zero_word, cudaStream_t s, int* nl);
 // Per round: fixed-point q = (qg, qh), the excluded flag (bit 15 of node) and node reset;
 // also zeroes the level-0 built histogram (hb0_words int64).
 cudaError_t launch_quant(const float* g, const float* h, const uint32_t* maxbits, uint64_t n_pad,
                          int2* q, uint16_t* node, long long* hb0, uint64_t hb0_words,
-                         cudaStream_t s, int* nl);
+                         uint32_t* ncount0, cudaStream_t s, int* nl);
 // The level's split (argmax over the per-feature records) and model slot, then
 // leaf = 2*leaf + (bin > t) keeping the excluded flag; counts the rows of every child
 // (cnt, non-final levels), or at the final level writes the leaf values and updates pred.
@@ -157,7 +176,7 @@ struct ApplyLaunch {
   const SplitRec* rec;
   uint32_t nf;
   uint32_t n_children;
-  uint32_t* cnt;
+  LevelLists lists;     // non-final levels: the next level's row list
   int final_level;
   const float* leafc;  // final level: [nf][n_leaves]
   uint32_t n_leaves;
@@ -173,12 +192,6 @@ struct ApplyLaunch {
   uint32_t* split_out;  // nullable: (feature, bin) of the chosen split
 };
 cudaError_t launch_apply(const ApplyLaunch& a, cudaStream_t s, int* nl);
-// The next level's row list from the child counts: with subtraction, per pair the child
-// with fewer rows is built (the odd one on ties, or always when force_odd), grouped by
-// pair; without, every child is its own group.
-cudaError_t launch_rowlist(const uint16_t* node, uint64_t n_pad, uint32_t n_children,
-                           int subtract, int force_odd, const RowLists& rl, cudaStream_t s,
-                           int* nl);
 cudaError_t launch_fill_f32(float* p, float v, uint64_t n, cudaStream_t s, int* nl);
 
 // GOSS: exact k-th largest |g| by radix selection (4 passes of 8-bit digits).

@@ -40,10 +40,15 @@ int cuda_fail(rw_ctx* ctx, cudaError_t e, const char* what) {
     if (_e != cudaSuccess) return cuda_fail((ctx), _e, #expr); \
   } while (0)
 
+// The communicator is non-blocking: a call may return ncclInProgress (e.g. while it
+// sets up connections on first use) and the communicator takes no further call until
+// its state reads ncclSuccess. nccl_settle polls that state, bounded by the context
+// timeout (then the communicator is aborted).
+ncclResult_t nccl_settle(rw_ctx* ctx, ncclResult_t r);
 #define RW_NC(ctx, expr)                                                        \
   do {                                                                          \
-    ncclResult_t _r = (expr);                                                   \
-    if (_r != ncclSuccess && _r != ncclInProgress)                              \
+    ncclResult_t _r = nccl_settle((ctx), (expr));                               \
+    if (_r != ncclSuccess)                                                      \
       return fail((ctx), RW_ERR_NCCL, std::string(#expr) + ": " + ncclGetErrorString(_r)); \
   } while (0)
 
@@ -113,6 +118,24 @@ struct WsBuf {
 };
 
 uint64_t round_up(uint64_t v, uint64_t m) { return (v + m - 1) / m * m; }
+
+ncclResult_t nccl_settle(rw_ctx* ctx, ncclResult_t r) {
+  if (r != ncclInProgress || !ctx->comm) return r;
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    ncclResult_t st = ncclInProgress;
+    ncclCommGetAsyncError(ctx->comm, &st);
+    if (st != ncclInProgress) return st;
+    const double ms = std::chrono::duration<double, std::milli>(
+                          std::chrono::steady_clock::now() - t0).count();
+    if (ctx->timeout_ms > 0 && ms > (double)ctx->timeout_ms) {
+      ncclCommAbort(ctx->comm);
+      ctx->comm = nullptr;
+      return ncclInternalError;
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+}
 
 // Wait for the context stream; with a communicator, bound the wait and abort the
 // communicator when the limit passes or NCCL reports an asynchronous error.
@@ -471,9 +494,9 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
   WsBuf<float> pred, g, h, d_leafval, d_thr, d_fi_gain, d_fi_count;
   WsBuf<uint16_t> node, d_thr_bin;
   WsBuf<int2> q;
-  WsBuf<uint32_t> rl_counters, rl_seg;
+  WsBuf<uint32_t> rl_counts;  // [ncount: 2][NL], [cursor: 2][NL] (alternating levels)
   WsBuf<int4> rl_entries;
-  WsBuf<uint8_t> rl_odd;
+  WsBuf<uint8_t> rl_built, rl_choice;
   WsBuf<long long> hb0, hb1, hf0, hf1;
   WsBuf<uint32_t> d_feat, maxbits;
   WsBuf<SplitRec> rec;
@@ -489,9 +512,11 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
   RW_CU(ctx, node.get(ds, "node", n_pad));
   RW_CU(ctx, q.get(ds, "q", n_pad));
   RW_CU(ctx, rl_entries.get(ds, "rl_entries", n_pad));
-  RW_CU(ctx, rl_counters.get(ds, "rl_counters", 2 * (size_t)NL));  // [cnt: NL][cursor: NL]
-  RW_CU(ctx, rl_seg.get(ds, "rl_seg", (size_t)NL + 1));
-  RW_CU(ctx, rl_odd.get(ds, "rl_odd", (size_t)NL / 2));
+  RW_CU(ctx, rl_counts.get(ds, "rl_counts", 4 * (size_t)NL));
+  RW_CU(ctx, rl_built.get(ds, "rl_built", (size_t)NL / 2));
+  RW_CU(ctx, rl_choice.get(ds, "rl_choice", (size_t)nf * NL / 2));
+  uint32_t* const ncount[2] = {rl_counts.p, rl_counts.p + NL};
+  uint32_t* const cursor[2] = {rl_counts.p + 2 * (size_t)NL, rl_counts.p + 3 * (size_t)NL};
   RW_CU(ctx, hb0.get(ds, "hb0", hb_groups * cell));
   RW_CU(ctx, hb1.get(ds, "hb1", hb_groups * cell));
   RW_CU(ctx, hf0.get(ds, "hf0", hf_nodes * cell));
@@ -572,7 +597,7 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
     uint32_t* mb = maxbits.p + 2 * (size_t)t;
     if (goss) {
       RW_CU(ctx, launch_grad(pred.p, ds->d_y, g.p, h.p, n, n_pad, logistic, 1, 0, ds->row_offset,
-                             0, mb, s, &nl));
+                             0, mb, ncount[0], s, &nl));
       RW_CU(ctx, launch_goss_init(gst, goss_k, s, &nl));
       for (int pass = 0; pass < 4; pass++) {
         RW_CU(ctx, launch_goss_digit_hist(g.p, n, gst, pass, s, &nl));
@@ -584,11 +609,11 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
                                    (uint64_t)t, mb, s, &nl));
     } else {
       RW_CU(ctx, launch_grad(pred.p, ds->d_y, g.p, h.p, n, n_pad, logistic, stride,
-                             stride > 1 ? (uint64_t)t % stride : 0, ds->row_offset, 1, mb, s,
-                             &nl));
+                             stride > 1 ? (uint64_t)t % stride : 0, ds->row_offset, 1, mb,
+                             ncount[0], s, &nl));
     }
     if (ctx->comm) RW_NC(ctx, ncclAllReduce(mb, mb, 2, ncclUint32, ncclMax, ctx->comm, s));
-    RW_CU(ctx, launch_quant(g.p, h.p, mb, n_pad, q.p, node.p, hb0.p, cell, s, &nl));
+    RW_CU(ctx, launch_quant(g.p, h.p, mb, n_pad, q.p, node.p, hb0.p, cell, ncount[0], s, &nl));
     pt.mark(RW_CAT_GRADIENTS);
 
     const uint32_t tree_seed = t * 2654435761u + 0x455A4B41u;  // src/booster.rs:351
@@ -605,8 +630,12 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
       hl.n_pad = n_pad;
       hl.packed = ds->packed;
       hl.q = q.p;
-      hl.entries = d == 0 ? nullptr : rl_entries.p;  // level 0: every row
-      hl.seg = d == 0 ? nullptr : rl_seg.p;
+      // level 0: every row; deeper: the list k_apply wrote (one group per built node)
+      hl.entries = d == 0 ? nullptr : rl_entries.p;
+      hl.pcount = d == 0 ? nullptr : ncount[(d - 1) & 1];
+      hl.glen = d == 0 ? nullptr : cursor[(d - 1) & 1];
+      hl.parents = n_nodes / 2;
+      hl.pairs = mode;
       hl.n_ident = (uint32_t)round_up(n, 512);  // rows past n carry q = 0
       hl.err = kerr.p;
       hl.groups = groups;
@@ -631,9 +660,15 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
       sl.nf = nf;
       sl.nb = nb;
       sl.mode = mode;
-      sl.built_odd = mode == 1 ? rl_odd.p : nullptr;
-      sl.zero_u32 = d + 1 < D ? rl_counters.p : nullptr;
-      sl.zero_words = 2 * NL;
+      sl.built_odd = mode == 1 ? rl_built.p : nullptr;
+      sl.choice = subtract && d + 1 < D ? rl_choice.p : nullptr;
+      sl.pcount = d == 0 ? nullptr : ncount[(d - 1) & 1];
+      sl.cursor_prev = d == 0 ? nullptr : cursor[(d - 1) & 1];
+      sl.built_prev = rl_built.p;
+      sl.ncount = ncount[d & 1];
+      sl.cursor_next = d + 1 < D ? cursor[d & 1] : nullptr;
+      sl.cursor_next_words = subtract ? n_nodes : 2 * n_nodes;
+      sl.subtract = subtract ? 1 : 0;
       sl.maxbits = mb;
       sl.lambda = (double)p->lambda;
       sl.min_child = (double)p->min_child_h;
@@ -658,7 +693,13 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
       al.rec = rec.p;
       al.nf = nf;
       al.n_children = n_children;
-      al.cnt = rl_counters.p;
+      al.lists.entries = d + 1 < D ? rl_entries.p : nullptr;
+      al.lists.q = q.p;
+      al.lists.ncount = ncount[d & 1];
+      al.lists.cursor = cursor[d & 1];
+      al.lists.choice = rl_choice.p;
+      al.lists.built_odd = rl_built.p;
+      al.lists.subtract = subtract ? 1 : 0;
       al.final_level = d == D - 1;
       al.leafc = leafc.p;
       al.n_leaves = NL;
@@ -673,12 +714,6 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
       al.leaf_base = t * NL;
       al.split_out = nullptr;
       RW_CU(ctx, launch_apply(al, s, &nl));
-      if (d + 1 < D) {
-        // with several ranks every rank must build the same child of each pair
-        RowLists rl{rl_counters.p, rl_counters.p + NL, rl_seg.p, rl_odd.p, rl_entries.p, q.p};
-        RW_CU(ctx, launch_rowlist(node.p, n_pad, n_children, subtract ? 1 : 0,
-                                  ctx->world > 1 ? 1 : 0, rl, s, &nl));
-      }
       pt.mark(d == D - 1 ? RW_CAT_UPDATE_PRED : RW_CAT_APPLY);
     }
   }
@@ -1001,15 +1036,17 @@ extern "C" int rw_debug_level_hist(rw_dataset* ds, const int32_t* node, const fl
   const size_t words = (size_t)groups * ds->ftiles * ds->n_bins * 2 * kHistFeat;
   DBuf<int2> dq;
   DBuf<int4> drows;
-  DBuf<uint32_t> dseg;
+  DBuf<uint32_t> dlen;  // group lengths (each group is its own region: pcount = glen)
   DBuf<long long> dout;
   RW_CU(ctx, dq.alloc(n_pad));
   RW_CU(ctx, drows.alloc(rows.size()));
-  RW_CU(ctx, dseg.alloc(seg.size()));
+  std::vector<uint32_t> len(groups);
+  for (uint32_t k = 0; k < groups; k++) len[k] = seg[k + 1] - seg[k];
+  RW_CU(ctx, dlen.alloc(groups));
   RW_CU(ctx, dout.alloc(words));
   RW_CU(ctx, cudaMemcpy(dq.p, qv.data(), n_pad * sizeof(int2), cudaMemcpyHostToDevice));
   RW_CU(ctx, cudaMemcpy(drows.p, rows.data(), rows.size() * sizeof(int4), cudaMemcpyHostToDevice));
-  RW_CU(ctx, cudaMemcpy(dseg.p, seg.data(), seg.size() * 4, cudaMemcpyHostToDevice));
+  RW_CU(ctx, cudaMemcpy(dlen.p, len.data(), groups * 4, cudaMemcpyHostToDevice));
   RW_CU(ctx, cudaMemset(dout.p, 0, words * 8));
   HistLaunch hl;
   hl.rowbins = ds->d_rowbins;
@@ -1018,7 +1055,10 @@ extern "C" int rw_debug_level_hist(rw_dataset* ds, const int32_t* node, const fl
   hl.err = nullptr;
   hl.q = dq.p;
   hl.entries = drows.p;
-  hl.seg = dseg.p;
+  hl.pcount = dlen.p;
+  hl.glen = dlen.p;
+  hl.parents = groups;
+  hl.pairs = 1;
   hl.n_ident = 0;
   hl.groups = groups;
   hl.nf = ds->nf;

@@ -10,10 +10,10 @@
 //     [ncclAllReduce]       multi-GPU: sum of the built histograms (int64, exact)
 //     k_split               derive sibling nodes, f64 gain scan, argmax, model write,
 //                           leaf values at the last level (no separate leaf pass)
-//     k_apply               leaf = 2*leaf + (bin > t) and per-child row counts;
+//     k_apply               leaf = 2*leaf + (bin > t) and the next level's row list
+//                           (per node the child with less hessian, or both children
+//                           without subtraction; the sibling is parent - built);
 //                           at the last level pred += leafval[leaf]
-//     k_rowlist             the next level's row list: per node pair the child with
-//                           fewer rows, grouped by pair (the sibling is parent - built)
 //
 // Exactness: histogram cells are int64 sums of per-row fixed-point values
 // q = round(x * 2^e) with |q| <= 2^RW_QBITS (rw_expf.h). A histogram CTA accumulates at
@@ -143,6 +143,50 @@ __device__ __forceinline__ void hist_add_row(uint32_t* hs, uint32_t bb, int2 qq,
   atomicAdd(&hs[c1 + kHistFeat], (uint32_t)qq.y);
 }
 
+// Exclusive prefix of n (<= 4 * blockDim.x) values in[i] (global, written by an earlier
+// kernel) into out[0..n], out[n] = the total; warp_sums has 33 words. All threads of
+// the block call it.
+__device__ void block_exclusive_scan(const uint32_t* in, uint32_t n, uint32_t* out,
+                                     uint32_t* warp_sums) {
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x / 32;
+  const uint32_t per = (n + blockDim.x - 1) / blockDim.x;
+  const uint32_t b0 = threadIdx.x * per;
+  uint32_t v[4], sum = 0;
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    v[k] = (k < (int)per && b0 + k < n) ? __ldcg(in + b0 + k) : 0u;
+    sum += v[k];
+  }
+  uint32_t incl = sum;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= (uint32_t)d) incl += y;
+  }
+  if (lane == 31) warp_sums[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t ws = lane < nw ? warp_sums[lane] : 0u, wi = ws;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, wi, d);
+      if (lane >= (uint32_t)d) wi += y;
+    }
+    if (lane < nw) warp_sums[lane] = wi - ws;  // exclusive warp offsets
+    if (lane == nw - 1) warp_sums[32] = wi;    // block total
+  }
+  __syncthreads();
+  uint32_t run = warp_sums[warp] + incl - sum;
+#pragma unroll
+  for (int k = 0; k < 4; k++)
+    if (k < (int)per && b0 + k < n) {
+      out[b0 + k] = run;
+      run += v[k];
+    }
+  if (threadIdx.x == 0) out[n] = warp_sums[32];
+  __syncthreads();
+}
+
 // Histogram of one level over a row list (or all rows), exact in fixed point.
 //
 // Row bins are tile-major: tile t's row r is the kHistFeat-byte (u8) or kHistFeat/2-byte
@@ -166,8 +210,28 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(HistLaunch a, uint32_t ft
   __shared__ __align__(8) uint64_t bar[kStreamStages];
   __shared__ int s_abort;
   constexpr uint32_t TB = PACKED ? kHistFeat / 2 : kHistFeat;  // tile bytes per row
+  __shared__ uint32_t warp_sums[33];
   const uint32_t nb = a.nb, words = nb * 2 * kHistFeat;
-  const uint32_t L = a.seg ? __ldg(a.seg + a.groups) : a.n_ident;
+  unsigned char* stage0 = reinterpret_cast<unsigned char*>(hs + words + 2 * kHistFeat);
+  // list segments: lpre = prefix of the group lengths (list index -> group), start = each
+  // group's first entry in `entries` (from the prefix of the parents' row counts)
+  uint32_t* s_lpre = reinterpret_cast<uint32_t*>(stage0 + (size_t)kListSlots * kListRows * (TB + 16));
+  uint32_t* s_start = s_lpre + a.groups + 1;
+  uint32_t* s_cap = s_start + a.groups;
+  if (a.entries) {
+    block_exclusive_scan(a.pcount, a.parents, s_cap, warp_sums);
+    block_exclusive_scan(a.glen, a.groups, s_lpre, warp_sums);
+    for (uint32_t g = threadIdx.x; g < a.groups; g += kHistThreads) {
+      if (a.pairs) {
+        s_start[g] = s_cap[g];
+      } else {
+        const uint32_t k = g >> 1;
+        s_start[g] = s_cap[k] + ((g & 1u) ? __ldcg(a.pcount + k) - __ldcg(a.glen + g) : 0u);
+      }
+    }
+    __syncthreads();
+  }
+  const uint32_t L = a.entries ? s_lpre[a.groups] : a.n_ident;
   const uint64_t total = (uint64_t)L * ftiles;
   // identity slices are whole stages (n_ident is a multiple of kStreamRows)
   uint64_t per = (total + gridDim.x - 1) / gridDim.x;
@@ -176,7 +240,6 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(HistLaunch a, uint32_t ft
   const uint64_t w_end = min(total, w + per);
   if (w >= w_end) return;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  unsigned char* stage0 = reinterpret_cast<unsigned char*>(hs + words + 2 * kHistFeat);
   constexpr uint32_t kStageBytes = kStreamRows * (TB + 8);
   for (uint32_t c = threadIdx.x; c < words; c += kHistThreads) hs[c] = 0u;
   if (threadIdx.x == 0) {
@@ -190,17 +253,18 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(HistLaunch a, uint32_t ft
   while (w < w_end) {
     const uint32_t t = (uint32_t)(w / L);
     const uint32_t i0 = (uint32_t)(w % L);
-    // the group holding list index i0: the last k with seg[k] <= i0
-    uint32_t grp = 0, g_end = L;
-    if (a.seg) {
+    // the group holding list index i0: the last k with lpre[k] <= i0
+    uint32_t grp = 0, g_end = L, ebase = 0;
+    if (a.entries) {
       uint32_t lo = 0, hi = a.groups;
       while (hi - lo > 1) {
         const uint32_t mid = (lo + hi) >> 1;
-        if (__ldg(a.seg + mid) <= i0) lo = mid;
+        if (s_lpre[mid] <= i0) lo = mid;
         else hi = mid;
       }
       grp = lo;
-      g_end = __ldg(a.seg + lo + 1);
+      g_end = s_lpre[lo + 1];
+      ebase = s_start[lo] + (i0 - s_lpre[lo]);  // entries of this part start here
     }
     uint64_t i1 = min((uint64_t)g_end, (uint64_t)i0 + kMaxRowsPerCta);
     i1 = min(i1, (uint64_t)i0 + (w_end - w));
@@ -268,11 +332,13 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(HistLaunch a, uint32_t ft
       const uint32_t my_row = threadIdx.x / 4, my_part = threadIdx.x % 4;
       auto load_entry = [&](uint32_t j) {  // this thread's entry of slot j (row my_row)
         const uint32_t li = j * kListRows + my_row;
-        return li < cnt ? __ldg(a.entries + i0 + li) : make_int4(0, 0, 0, 0);
+        return li < cnt && ebase + li < a.n_pad ? __ldcg(a.entries + ebase + li)
+                                                : make_int4(0, 0, 0, 0);
       };
       auto issue = [&](uint32_t j, int4 e) {
         unsigned char* sp = stage0 + (size_t)(j % kListSlots) * kSlotBytes;
-        const bool live = j * kListRows + my_row < cnt;
+        // rows outside the table never reach memory (defensive: lists hold rows < n_pad)
+        const bool live = j * kListRows + my_row < cnt && (uint32_t)e.x < a.n_pad;
         if (my_part * 16 < TB)
           cp_async16(sp + my_row * TB + my_part * 16,
                      tile + (size_t)(live ? (uint32_t)e.x : 0u) * TB + my_part * 16,
@@ -467,8 +533,9 @@ __global__ void __launch_bounds__(kGainThreads) k_gain(SplitLaunch a) {
   __syncthreads();
 #pragma unroll
   for (int i = 0; i < 2 * (int)kGainCols; i++) p[i] += wsum[warp][i];
-  if (a.last_level && b < nb) {
-    // prefixes for the leaf values of whichever threshold k_best picks
+  if (a.prefix && b < nb) {
+    // prefixes for k_best: the next level's built-child choice and, at the last level,
+    // the leaf values of whichever threshold it picks
 #pragma unroll
     for (int i = 0; i < (int)kGainCols; i++)
       if (fq[i] < nf)
@@ -525,8 +592,25 @@ __global__ void __launch_bounds__(kBestThreads) k_best(SplitLaunch a) {
     const uint64_t w1 = w0 + per < a.hb_next_words ? w0 + per : a.hb_next_words;
     for (uint64_t w = w0 + threadIdx.x; w < w1; w += kBestThreads) a.hb_next[w] = 0;
   }
-  if (a.zero_u32 && f == 0)
-    for (uint32_t w = threadIdx.x; w < a.zero_words; w += kBestThreads) a.zero_u32[w] = 0u;
+  if (f == 0) {
+    // this level's per-node row counts (from the previous level's lists) and the cursors
+    // the leaf-index update fills for the next level
+    if (a.ncount && a.cursor_prev)
+      for (uint32_t c = threadIdx.x; c < a.n_nodes; c += kBestThreads) {
+        uint32_t v;
+        if (a.subtract) {
+          const uint32_t k = c >> 1, built = __ldcg(a.cursor_prev + k);
+          v = ((c & 1u) == (uint32_t)__ldcg(a.built_prev + k)) ? built
+                                                                 : __ldcg(a.pcount + k) - built;
+        } else {
+          v = __ldcg(a.cursor_prev + c);
+        }
+        a.ncount[c] = v;
+      }
+    if (a.cursor_next)
+      for (uint32_t w = threadIdx.x; w < a.cursor_next_words; w += kBestThreads)
+        a.cursor_next[w] = 0u;
+  }
   const double inv_g = q_inv_scale(a.maxbits[0]), inv_h = q_inv_scale(a.maxbits[1]);
   const double lambda = a.lambda;
   double key = -RW_INF;
@@ -564,12 +648,25 @@ __global__ void __launch_bounds__(kBestThreads) k_best(SplitLaunch a) {
     r.thr = a.cuts[(size_t)f * nsplit + bb];
     a.rec[f] = r;
   }
-  if (!a.last_level) return;
   __syncthreads();
+  const uint32_t bs = s_b;
+  if (!a.last_level) {
+    // Which child of each node the next level builds if this feature wins: the side with
+    // less hessian (ties: the right, odd child); its sibling is derived by subtraction.
+    // Any choice gives the same exact histograms; this one reads allreduced sums, so
+    // every rank makes the same choice.
+    if (a.choice && a.prefix)
+      for (uint32_t nd = threadIdx.x; nd < a.n_nodes; nd += kBestThreads) {
+        const longlong2* pr =
+            reinterpret_cast<const longlong2*>(a.prefix) + ((size_t)f * a.n_nodes + nd) * nb;
+        const long long hl = __ldcg(pr + bs).y, ht = __ldcg(pr + nb - 1).y;
+        a.choice[(size_t)f * a.n_nodes + nd] = (ht - hl) <= hl ? 1 : 0;
+      }
+    return;
+  }
   // Last level: the leaf values this feature's best split would give (src/cpu.rs:286-318
   // from the exact per-node prefix sums k_gain kept), one thread per node; k_apply keeps
   // the winning feature's.
-  const uint32_t bs = s_b;
   for (uint32_t nd = threadIdx.x; nd < a.n_nodes; nd += kBestThreads) {
     const longlong2* pr = reinterpret_cast<const longlong2*>(a.prefix) + ((size_t)f * a.n_nodes + nd) * nb;
     const longlong2 l = __ldcg(pr + bs), tt = __ldcg(pr + nb - 1);
@@ -698,8 +795,9 @@ __device__ void block_max2_atomic(uint32_t mg, uint32_t mh, uint32_t* maxbits) {
 __global__ void k_grad(const float* __restrict__ pred, const float* __restrict__ y,
                        float* __restrict__ g, float* __restrict__ h, uint64_t n, uint64_t n_pad,
                        int logistic, uint64_t stride, uint64_t phase, uint64_t row_offset,
-                       int compute_max, uint32_t* maxbits) {
+                       int compute_max, uint32_t* maxbits, uint32_t* zero_word) {
   pdl_enter();
+  if (zero_word && blockIdx.x == 0 && threadIdx.x == 0) *zero_word = 0u;
   uint32_t mg = 0, mh = 0;
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_pad;
        i += (uint64_t)gridDim.x * blockDim.x) {
@@ -726,14 +824,20 @@ __global__ void k_grad(const float* __restrict__ pred, const float* __restrict__
 
 // Per round: q = round(x * 2^e) for g and h (scales from the final maxima), the row's
 // excluded flag (node bit 15; a row whose g and h both quantise to 0 adds nothing to any
-// sum) and node reset. Also zeroes the level-0 histogram.
+// sum) and node reset. Also zeroes the level-0 histogram and counts the rows that are
+// not excluded (the root's row count, for the level-0 leaf-index update's list).
 constexpr uint16_t kExcluded = 0x8000;
 
 __global__ void k_quant(const float* __restrict__ g, const float* __restrict__ h,
                         const uint32_t* __restrict__ maxbits, uint64_t n_pad,
                         int2* __restrict__ q, uint16_t* __restrict__ node,
-                        long long* __restrict__ hb0, uint64_t hb0_words) {
+                        long long* __restrict__ hb0, uint64_t hb0_words,
+                        uint32_t* __restrict__ ncount0) {
   pdl_enter();
+  __shared__ uint32_t s_rows;
+  if (threadIdx.x == 0) s_rows = 0u;
+  __syncthreads();
+  uint32_t rows = 0;
   const float sg = rw_pow2f(rw_qscale_exp(maxbits[0]));
   const float sh = rw_pow2f(rw_qscale_exp(maxbits[1]));
   const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -743,7 +847,13 @@ __global__ void k_quant(const float* __restrict__ g, const float* __restrict__ h
     const int32_t a = rw_quantize(g[i], sg), b = rw_quantize(h[i], sh);
     q[i] = make_int2(a, b);
     node[i] = (a | b) == 0 ? kExcluded : 0;
+    rows += (a | b) != 0;
   }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) rows += __shfl_down_sync(0xffffffffu, rows, off);
+  if ((threadIdx.x & 31) == 0 && rows) atomicAdd(&s_rows, rows);
+  __syncthreads();
+  if (threadIdx.x == 0 && s_rows && ncount0) atomicAdd(ncount0, s_rows);
 }
 
 // Every CTA first picks the level's split from the per-feature records (highest gain,
@@ -751,9 +861,13 @@ __global__ void k_quant(const float* __restrict__ g, const float* __restrict__ h
 // 0, bin 0); CTA 0 also writes the model slot and feature importance
 // (src/cpu.rs:272-276) and, at the last level, the tree's leaf values.
 // Then leaf = 2*leaf + (bin[f*] > t*) (src/cpu.rs:278-281) for 4 rows per thread, keeping
-// the excluded flag. Non-final levels count the non-excluded rows of every child (block
-// counts in shared memory, warp-aggregated, then one global add per nonzero child); the
-// final level adds the tree's leaf value to pred (src/cpu.rs:319-320).
+// the excluded flag. Non-final levels also write the next level's row list: node nd owns
+// the region [cap[nd], cap[nd+1]) of `entries` (cap = prefix of the nodes' row counts);
+// with subtraction it holds the rows of the child k_best chose to build, from its start;
+// without, the left child's rows from the start and the right child's from the end.
+// Each chunk of rows ranks its rows per group in shared memory (warp-aggregated) and
+// reserves space with one global add per nonzero group; the entry carries the row's q.
+// The final level adds the tree's leaf value to pred (src/cpu.rs:319-320).
 constexpr int kApplyThreads = 256;
 
 // The level's split from the per-feature records (every CTA), and by CTA 0 the model
@@ -799,30 +913,46 @@ __device__ void choose_split(const ApplyLaunch& a, uint32_t* s_ft, double* red_g
 
 __global__ void __launch_bounds__(kApplyThreads) k_apply(ApplyLaunch a) {
   pdl_enter();
-  extern __shared__ uint32_t s_cnt[];
+  extern __shared__ uint32_t lsm[];
   __shared__ double red_g[kApplyThreads / 32];
   __shared__ uint32_t red_i[kApplyThreads / 32];
   __shared__ uint32_t s_ft[2];
-  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const bool counting = !a.final_level && a.cnt;
-  if (counting)
-    for (uint32_t c = threadIdx.x; c < a.n_children; c += blockDim.x) s_cnt[c] = 0u;
+  __shared__ uint32_t warp_sums[33];
+  const uint32_t lane = threadIdx.x & 31;
+  const LevelLists& L = a.lists;
+  const bool listing = !a.final_level && L.entries;
+  const uint32_t n_nodes = a.n_children / 2;
+  const uint32_t G = L.subtract ? n_nodes : a.n_children;  // next-level groups
+  uint32_t* s_cap = lsm;                   // [n_nodes + 1] prefix of the node row counts
+  uint32_t* s_cnt = s_cap + n_nodes + 1;   // [G] this chunk's rows per group
+  uint32_t* s_base = s_cnt + G;            // [G] their reservation in the group's region
+  uint8_t* s_choice = reinterpret_cast<uint8_t*>(s_base + G);  // [n_nodes]
+  if (listing)
+    for (uint32_t g = threadIdx.x; g < G; g += blockDim.x) s_cnt[g] = 0u;
   choose_split(a, s_ft, red_g, red_i);
   const uint32_t f = s_ft[0], t = s_ft[1];
+  if (listing) {
+    block_exclusive_scan(L.ncount, n_nodes, s_cap, warp_sums);
+    if (L.subtract)
+      for (uint32_t nd = threadIdx.x; nd < n_nodes; nd += blockDim.x) {
+        const uint8_t c = __ldcg(L.choice + (size_t)f * n_nodes + nd);
+        s_choice[nd] = c;
+        if (blockIdx.x == 0) L.built_odd[nd] = c;
+      }
+    __syncthreads();
+  }
   const float* lv = a.final_level ? a.leafc + (size_t)f * a.n_leaves : nullptr;
   if (a.final_level && blockIdx.x == 0)
     for (uint32_t l = threadIdx.x; l < a.n_leaves; l += blockDim.x)
       a.leafval[a.leaf_base + l] = __ldcg(lv + l);
   const uint8_t* col = a.colbins + (size_t)f * a.n_pad;
   const uint64_t n4 = a.n_pad / 4;
-  // every lane of a warp runs the same number of iterations (match_any needs them all)
-  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-  const uint64_t warp_first = (uint64_t)blockIdx.x * blockDim.x + warp * 32;
-  for (uint64_t wq = warp_first; wq < n4; wq += stride) {
-    const uint64_t qi = wq + lane;
-    const bool live = qi < n4;
-    uint32_t nds[4] = {kExcluded, kExcluded, kExcluded, kExcluded};
-    if (live) {
+  // block-uniform chunks of blockDim.x row quads (the list phases synchronise the CTA)
+  for (uint64_t c0 = (uint64_t)blockIdx.x * blockDim.x; c0 < n4;
+       c0 += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t qi = c0 + threadIdx.x;
+    uint32_t nds[4] = {kExcluded, kExcluded, kExcluded, kExcluded}, par[4] = {0, 0, 0, 0};
+    if (qi < n4) {
       const uint64_t r = qi * 4;
       const uint32_t b4 = *reinterpret_cast<const uint32_t*>(col + r);
       uint2 nd2 = *reinterpret_cast<const uint2*>(a.node + r);
@@ -831,9 +961,10 @@ __global__ void __launch_bounds__(kApplyThreads) k_apply(ApplyLaunch a) {
       nds[2] = nd2.y & 0xffffu;
       nds[3] = nd2.y >> 16;
 #pragma unroll
-      for (int s = 0; s < 4; s++) {
-        const uint32_t ex = nds[s] & kExcluded;
-        nds[s] = ex | ((nds[s] & 0x7fffu) * 2u + (((b4 >> (8 * s)) & 0xffu) > t ? 1u : 0u));
+      for (int q = 0; q < 4; q++) {
+        const uint32_t ex = nds[q] & kExcluded;
+        par[q] = nds[q] & 0x7fffu;
+        nds[q] = ex | (par[q] * 2u + (((b4 >> (8 * q)) & 0xffu) > t ? 1u : 0u));
       }
       nd2.x = (nds[0] & 0xffffu) | (nds[1] << 16);
       nd2.y = (nds[2] & 0xffffu) | (nds[3] << 16);
@@ -847,106 +978,51 @@ __global__ void __launch_bounds__(kApplyThreads) k_apply(ApplyLaunch a) {
         *reinterpret_cast<float4*>(a.pred + r) = p4;
       }
     }
-    if (counting) {
-#pragma unroll
-      for (int s = 0; s < 4; s++) {
-        const uint32_t key = (nds[s] & kExcluded) ? 0xffffffffu : nds[s];
-        const uint32_t peers = __match_any_sync(0xffffffffu, key);
-        if (key != 0xffffffffu && lane == (uint32_t)(__ffs(peers) - 1))
-          atomicAdd(&s_cnt[key], (uint32_t)__popc(peers));
-      }
-    }
-  }
-  if (counting) {
-    __syncthreads();
-    for (uint32_t c = threadIdx.x; c < a.n_children; c += blockDim.x)
-      if (s_cnt[c]) atomicAdd(a.cnt + c, s_cnt[c]);
-  }
-}
-
-// The next level's row list (levels 0 .. D-2). Every CTA derives the groups' sizes and
-// list offsets from the child counts (identical in all CTAs); CTA 0 also publishes them
-// with the built-child flags. Then each CTA lists its slice of rows: warp-aggregated
-// shared-memory ranks per group, one global cursor reservation per nonempty group, and a
-// store of the row's entry (row id and its q) at seg[group] + reservation + rank. Row
-// order inside a group depends on scheduling; the histograms it feeds do not.
-constexpr int kListThreads = 512;
-constexpr uint32_t kListRowsPerCta = kListThreads * 4;
-
-__global__ void __launch_bounds__(kListThreads)
-    k_rowlist(const uint16_t* __restrict__ node, uint64_t n_pad, uint32_t n_children,
-              int subtract, int force_odd, RowLists rl) {
-  pdl_enter();
-  extern __shared__ uint32_t ls[];
-  const uint32_t groups = subtract ? n_children / 2 : n_children;
-  uint32_t* s_seg = ls;               // [groups + 1]
-  uint32_t* s_cnt = ls + groups + 1;  // [groups]
-  uint32_t* s_base = s_cnt + groups;  // [groups]
-  uint8_t* s_odd = reinterpret_cast<uint8_t*>(s_base + groups);  // [groups]
-  // group sizes -> exclusive offsets (sequential chunks per thread, then a serial pass
-  // over the chunk totals by thread 0; groups <= 2^11)
-  for (uint32_t k = threadIdx.x; k < groups; k += kListThreads) {
-    uint32_t sz;
-    if (subtract) {
-      const uint32_t ce = __ldcg(rl.cnt + 2 * k), co = __ldcg(rl.cnt + 2 * k + 1);
-      const uint8_t odd = (force_odd || co <= ce) ? 1 : 0;
-      s_odd[k] = odd;
-      sz = odd ? co : ce;
-    } else {
-      sz = __ldcg(rl.cnt + k);
-    }
-    s_seg[k + 1] = sz;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    s_seg[0] = 0u;
-    for (uint32_t k = 0; k < groups; k++) s_seg[k + 1] += s_seg[k];
-  }
-  __syncthreads();
-  if (blockIdx.x == 0) {
-    for (uint32_t k = threadIdx.x; k <= groups; k += kListThreads) rl.seg[k] = s_seg[k];
-    if (subtract)
-      for (uint32_t k = threadIdx.x; k < groups; k += kListThreads) rl.built_odd[k] = s_odd[k];
-  }
-  const uint32_t lane = threadIdx.x & 31;
-  for (uint64_t r0 = (uint64_t)blockIdx.x * kListRowsPerCta; r0 < n_pad;
-       r0 += (uint64_t)gridDim.x * kListRowsPerCta) {
-    for (uint32_t k = threadIdx.x; k < groups; k += kListThreads) s_cnt[k] = 0u;
-    __syncthreads();
+    if (!listing) continue;
+    // the next level's list: group key and the row's rank among this chunk's rows of
+    // the group (warp-aggregated shared counters)
     uint32_t key[4], rank[4];
 #pragma unroll
-    for (int s = 0; s < 4; s++) {
-      const uint64_t r = r0 + (uint64_t)s * kListThreads + threadIdx.x;
-      key[s] = 0xffffffffu;
-      if (r < n_pad) {
-        const uint32_t nd = node[r];
-        if (!(nd & kExcluded)) {
-          if (!subtract) key[s] = nd;
-          else if ((nd & 1u) == s_odd[nd >> 1]) key[s] = nd >> 1;
-        }
+    for (int q = 0; q < 4; q++) {
+      uint32_t k = 0xffffffffu;
+      if (!(nds[q] & kExcluded)) {
+        const uint32_t bit = nds[q] & 1u;
+        if (!L.subtract) k = nds[q];
+        else if (bit == s_choice[par[q]]) k = par[q];
       }
-      const uint32_t peers = __match_any_sync(0xffffffffu, key[s]);
+      const uint32_t peers = __match_any_sync(0xffffffffu, k);
       const uint32_t leader = (uint32_t)(__ffs(peers) - 1);
       uint32_t base = 0u;
-      if (key[s] != 0xffffffffu && lane == leader) base = atomicAdd(&s_cnt[key[s]], (uint32_t)__popc(peers));
+      if (k != 0xffffffffu && lane == leader) base = atomicAdd(&s_cnt[k], (uint32_t)__popc(peers));
       base = __shfl_sync(0xffffffffu, base, (int)leader);
-      rank[s] = base + (uint32_t)__popc(peers & ((1u << lane) - 1u));
+      key[q] = k;
+      rank[q] = base + (uint32_t)__popc(peers & ((1u << lane) - 1u));
     }
     __syncthreads();
-    for (uint32_t k = threadIdx.x; k < groups; k += kListThreads)
-      if (s_cnt[k]) s_base[k] = atomicAdd(rl.cursor + k, s_cnt[k]);
-    __syncthreads();
-#pragma unroll
-    for (int s = 0; s < 4; s++) {
-      if (key[s] == 0xffffffffu) continue;
-      const uint64_t at = (uint64_t)s_seg[key[s]] + s_base[key[s]] + rank[s];
-      if (at < n_pad) {
-        const uint32_t row = (uint32_t)(r0 + (uint64_t)s * kListThreads + threadIdx.x);
-        const int2 qv = rl.q[row];
-        rl.entries[at] = make_int4((int)row, qv.x, qv.y, 0);
+    for (uint32_t g = threadIdx.x; g < G; g += blockDim.x) {
+      const uint32_t c = s_cnt[g];
+      if (c) {
+        s_base[g] = atomicAdd(L.cursor + g, c);
+        s_cnt[g] = 0u;
       }
     }
     __syncthreads();
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const uint32_t k = key[q];
+      if (k == 0xffffffffu) continue;
+      const uint32_t rk = s_base[k] + rank[q];
+      uint32_t pos;
+      if (L.subtract) {
+        pos = s_cap[k] + rk;  // the built child fills its node's region from the start
+      } else {
+        const uint32_t pn = k >> 1;  // left child from the start, right child from the end
+        pos = (k & 1u) ? s_cap[pn + 1] - 1u - rk : s_cap[pn] + rk;
+      }
+      const uint32_t row = (uint32_t)(qi * 4 + q);
+      const int2 qv = __ldg(L.q + row);
+      if (pos < a.n_pad) L.entries[pos] = make_int4((int)row, qv.x, qv.y, 0);
+    }
   }
 }
 
@@ -1135,8 +1211,11 @@ cudaError_t launch_hist(const HistLaunch& L, cudaStream_t s, int* n_launch) {
   const uint32_t ftiles = (L.nf + kHistFeat - 1) / kHistFeat;
   const uint32_t tb = L.packed ? kHistFeat / 2 : kHistFeat;
   const size_t smem = (size_t)(L.nb + 1) * 2 * kHistFeat * 4 +  // + the dummy bin row
-                      (L.entries ? (size_t)kListSlots * kListRows * (tb + 16)
+                      (L.entries ? (size_t)kListSlots * kListRows * (tb + 16) +
+                                       ((size_t)L.groups * 2 + 2 + L.parents) * 4
                                  : (size_t)kStreamStages * kStreamRows * (tb + 8));
+  if (L.entries && (L.groups > 4 * kHistThreads || L.parents > 4 * kHistThreads))
+    return cudaErrorInvalidValue;
   if (!L.entries && (L.n_ident % kStreamRows) != 0) return cudaErrorInvalidValue;
   const void* kfn = L.packed ? reinterpret_cast<const void*>(&k_hist<true>)
                              : reinterpret_cast<const void*>(&k_hist<false>);
@@ -1187,10 +1266,11 @@ cudaError_t launch_pack4(const uint8_t* d_u8, uint64_t n_pad, uint32_t nf, uint8
 cudaError_t launch_grad(const float* pred, const float* y, float* g, float* h, uint64_t n,
                         uint64_t n_pad, int logistic, uint64_t stride, uint64_t phase,
                         uint64_t row_offset, int compute_max, uint32_t* maxbits,
-                        cudaStream_t s, int* nl) {
+                        uint32_t* zero_word, cudaStream_t s, int* nl) {
   RW_PREFER_SMEM(k_grad);
   cudaError_t e = launch_pdl(k_grad, dim3(grid_for(n_pad, 256)), dim3(256), 0, s, pred, y, g, h, n,
-                             n_pad, logistic, stride, phase, row_offset, compute_max, maxbits);
+                             n_pad, logistic, stride, phase, row_offset, compute_max, maxbits,
+                             zero_word);
   if (e != cudaSuccess) return e;
   if (nl) (*nl)++;
   return cudaGetLastError();
@@ -1198,10 +1278,10 @@ cudaError_t launch_grad(const float* pred, const float* y, float* g, float* h, u
 
 cudaError_t launch_quant(const float* g, const float* h, const uint32_t* maxbits, uint64_t n_pad,
                          int2* q, uint16_t* node, long long* hb0, uint64_t hb0_words,
-                         cudaStream_t s, int* nl) {
+                         uint32_t* ncount0, cudaStream_t s, int* nl) {
   RW_PREFER_SMEM(k_quant);
   cudaError_t e = launch_pdl(k_quant, dim3(grid_for(n_pad, 256)), dim3(256), 0, s, g, h, maxbits,
-                             n_pad, q, node, hb0, hb0_words);
+                             n_pad, q, node, hb0, hb0_words, ncount0);
   if (e != cudaSuccess) return e;
   if (nl) (*nl)++;
   return cudaGetLastError();
@@ -1209,27 +1289,17 @@ cudaError_t launch_quant(const float* g, const float* h, const uint32_t* maxbits
 
 cudaError_t launch_apply(const ApplyLaunch& a, cudaStream_t s, int* nl) {
   const uint64_t n4 = a.n_pad / 4;
-  const size_t smem = a.final_level ? 0 : (size_t)a.n_children * 4;
+  const uint32_t n_nodes = a.n_children / 2;
+  const uint32_t G = a.lists.subtract ? n_nodes : a.n_children;
+  const bool listing = !a.final_level && a.lists.entries;
+  if (listing && n_nodes > 4 * kApplyThreads) return cudaErrorInvalidValue;
+  const size_t smem = listing ? ((size_t)n_nodes + 1 + 2 * (size_t)G) * 4 + n_nodes : 0;
+  if (smem > 48 * 1024 &&
+      set_smem_and_occupancy(reinterpret_cast<const void*>(&k_apply), kApplyThreads, smem) < 1)
+    return cudaErrorInvalidConfiguration;
   RW_PREFER_SMEM(k_apply);
   cudaError_t e = launch_pdl(k_apply, dim3(grid_for(n4, kApplyThreads)), dim3(kApplyThreads), smem,
                              s, a);
-  if (e != cudaSuccess) return e;
-  if (nl) (*nl)++;
-  return cudaGetLastError();
-}
-
-cudaError_t launch_rowlist(const uint16_t* node, uint64_t n_pad, uint32_t n_children,
-                           int subtract, int force_odd, const RowLists& rl, cudaStream_t s,
-                           int* nl) {
-  const uint32_t groups = subtract ? n_children / 2 : n_children;
-  const size_t smem = ((size_t)groups * 3 + 1) * 4 + groups;
-  if (set_smem_and_occupancy(reinterpret_cast<const void*>(&k_rowlist), kListThreads, smem) < 1)
-    return cudaErrorInvalidConfiguration;
-  uint64_t blocks = (n_pad + kListRowsPerCta - 1) / kListRowsPerCta;
-  if (blocks > (uint64_t)sm_count() * 4) blocks = (uint64_t)sm_count() * 4;
-  RW_PREFER_SMEM(k_rowlist);
-  cudaError_t e = launch_pdl(k_rowlist, dim3((unsigned)blocks), dim3(kListThreads), smem, s, node,
-                             n_pad, n_children, subtract, force_odd, rl);
   if (e != cudaSuccess) return e;
   if (nl) (*nl)++;
   return cudaGetLastError();
