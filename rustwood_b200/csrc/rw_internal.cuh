@@ -11,6 +11,20 @@
 
 #include "../../include/rwgpu.h"
 
+// Cross-rank exchange over NVLink peer memory (peer_kernels.cu): every rank's symmetric
+// region, mapped into every rank. Layout: signal words, then the small-exchange slots,
+// then caller-placed buffers from kPeerDataOff.
+constexpr int kMaxPeers = 8;
+constexpr size_t kPeerHdr = 4096;
+constexpr int kPeerSmallWords = 256;
+constexpr size_t kPeerDataOff = kPeerHdr + 2 * (size_t)kMaxPeers * kPeerSmallWords * 8;
+enum { kPeerArrive = 0, kPeerDepart = 1, kPeerSmall = 2 };
+struct PeerSet {
+  char* base[kMaxPeers];  // each rank's region as mapped in this process (own at [rank])
+  int world, rank;
+  uint64_t timeout_ns;    // bound of every wait on a peer
+};
+
 struct rw_ctx {
   int device = 0;
   int rank = 0;
@@ -23,6 +37,13 @@ struct rw_ctx {
   int64_t timeout_ms = 60000;
   std::string last_error;
   uint64_t launches = 0;  // kernels launched on this context (all time)
+  // world > 1: the symmetric region (cudaMalloc, exported by IPC) and its peer mappings
+  char* sym = nullptr;
+  size_t sym_bytes = 0;
+  char* sym_peer[kMaxPeers] = {};
+  uint64_t peer_epoch = 0;   // exchanges issued on the region (identical on every rank)
+  int peer_mode = -1;        // -1 undecided, 0 NCCL, 1 peer memory
+  bool peer_failed = false;  // a bounded wait expired: the region's epochs are unusable
 };
 
 // Bins are stored twice in HBM:
@@ -193,6 +214,16 @@ struct ApplyLaunch {
 };
 cudaError_t launch_apply(const ApplyLaunch& a, cudaStream_t s, int* nl);
 cudaError_t launch_fill_f32(float* p, float v, uint64_t n, cudaStream_t s, int* nl);
+
+// ---- peer exchanges (peer_kernels.cu) ---------------------------------------------
+// Sum of `words` int64 (even) at src_off of every rank's region into dst_off of every
+// rank's region (16-byte aligned offsets).
+cudaError_t launch_peer_sum_i64(const PeerSet& ps, uint64_t src_off, uint64_t dst_off,
+                                uint64_t words, uint64_t epoch, int* err, cudaStream_t s,
+                                int* nl);
+// In place over `data` (local device memory): n u64 summed, or n u32 maxed (max_u32).
+cudaError_t launch_peer_small(const PeerSet& ps, void* data, uint32_t n, int max_u32,
+                              uint64_t epoch, int* err, cudaStream_t s, int* nl);
 
 // GOSS: exact k-th largest |g| by radix selection (4 passes of 8-bit digits).
 struct GossState {

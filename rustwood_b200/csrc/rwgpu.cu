@@ -6,6 +6,7 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <cstdlib>
 #include <cstring>
 
 #include <algorithm>
@@ -167,6 +168,119 @@ int wait_stream(rw_ctx* ctx) {
   }
 }
 
+// ---- symmetric region for peer exchanges (world > 1) ----------------------------------
+
+void sym_close(rw_ctx* ctx) {
+  for (int r = 0; r < kMaxPeers; r++)
+    if (ctx->sym_peer[r]) {
+      cudaIpcCloseMemHandle(ctx->sym_peer[r]);
+      ctx->sym_peer[r] = nullptr;
+    }
+  if (ctx->sym) cudaFree(ctx->sym);
+  ctx->sym = nullptr;
+  ctx->sym_bytes = 0;
+}
+
+// All ranks call this at the same point with the same size (a collective): makes every
+// rank's region at least `need` bytes, zeroed, and maps every peer's region. Decides
+// once per context between peer memory and NCCL: NCCL when RW_PEER_EXCHANGE=0 is set
+// (the same on every rank) or when any rank cannot map a peer's region.
+int sym_ensure(rw_ctx* ctx, size_t need) {
+  if (ctx->world < 2 || ctx->peer_mode == 0) return RW_OK;
+  if (ctx->peer_failed)
+    return fail(ctx, RW_ERR_CUDA, "an earlier peer exchange timed out; recreate the context");
+  if (ctx->world > kMaxPeers) {
+    ctx->peer_mode = 0;
+    return RW_OK;
+  }
+  if (ctx->peer_mode == -1) {
+    const char* env = std::getenv("RW_PEER_EXCHANGE");
+    if (env && env[0] == '0') {
+      ctx->peer_mode = 0;
+      return RW_OK;
+    }
+  }
+  if (ctx->peer_mode == 1 && ctx->sym_bytes >= need) return RW_OK;
+  int rc = wait_stream(ctx);
+  if (rc) return rc;
+  DBuf<int> flag;
+  RW_CU(ctx, flag.alloc(1));
+  auto all_ok = [&](int ok) -> int {  // min over ranks of ok, as a barrier
+    RW_CU(ctx, cudaMemcpyAsync(flag.p, &ok, 4, cudaMemcpyHostToDevice, ctx->stream));
+    RW_NC(ctx, ncclAllReduce(flag.p, flag.p, 1, ncclInt32, ncclMin, ctx->comm, ctx->stream));
+    RW_CU(ctx, cudaMemcpyAsync(&ok, flag.p, 4, cudaMemcpyDeviceToHost, ctx->stream));
+    int w = wait_stream(ctx);
+    if (w) return -1;
+    return ok;
+  };
+  // every rank unmaps the old regions before any rank frees its own
+  for (int r = 0; r < kMaxPeers; r++)
+    if (ctx->sym_peer[r]) {
+      cudaIpcCloseMemHandle(ctx->sym_peer[r]);
+      ctx->sym_peer[r] = nullptr;
+    }
+  if (all_ok(1) < 0) return RW_ERR_NCCL;
+  if (ctx->sym) cudaFree(ctx->sym);
+  ctx->sym = nullptr;
+  ctx->sym_bytes = 0;
+  const size_t bytes = round_up(need + need / 4, 2u << 20);
+  int ok = 1;
+  cudaIpcMemHandle_t mine = {};
+  if (cudaMalloc(reinterpret_cast<void**>(&ctx->sym), bytes) != cudaSuccess ||
+      cudaMemsetAsync(ctx->sym, 0, bytes, ctx->stream) != cudaSuccess ||
+      cudaStreamSynchronize(ctx->stream) != cudaSuccess ||
+      cudaIpcGetMemHandle(&mine, ctx->sym) != cudaSuccess) {
+    cudaGetLastError();
+    ok = 0;
+  }
+  // exchange the handles (a zeroed handle from a rank that failed is never opened)
+  DBuf<char> hbuf;
+  RW_CU(ctx, hbuf.alloc((size_t)ctx->world * sizeof(cudaIpcMemHandle_t)));
+  RW_CU(ctx, cudaMemcpyAsync(hbuf.p + (size_t)ctx->rank * sizeof mine, &mine, sizeof mine,
+                             cudaMemcpyHostToDevice, ctx->stream));
+  RW_NC(ctx, ncclAllGather(hbuf.p + (size_t)ctx->rank * sizeof mine, hbuf.p, sizeof mine, ncclChar,
+                           ctx->comm, ctx->stream));
+  std::vector<cudaIpcMemHandle_t> all(ctx->world);
+  RW_CU(ctx, cudaMemcpyAsync(all.data(), hbuf.p, (size_t)ctx->world * sizeof mine,
+                             cudaMemcpyDeviceToHost, ctx->stream));
+  rc = wait_stream(ctx);
+  if (rc) return rc;
+  ok = all_ok(ok);
+  if (ok < 0) return RW_ERR_NCCL;
+  if (ok)
+    for (int r = 0; r < ctx->world && ok; r++) {
+      if (r == ctx->rank) continue;
+      void* p = nullptr;
+      if (cudaIpcOpenMemHandle(&p, all[r], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        cudaGetLastError();
+        ok = 0;
+      } else {
+        ctx->sym_peer[r] = static_cast<char*>(p);
+      }
+    }
+  ok = all_ok(ok);
+  if (ok < 0) return RW_ERR_NCCL;
+  if (!ok) {  // some rank cannot use peer memory: every rank uses NCCL from now on
+    sym_close(ctx);
+    ctx->peer_mode = 0;
+    return RW_OK;
+  }
+  ctx->sym_bytes = bytes;
+  ctx->peer_epoch = 0;
+  ctx->peer_mode = 1;
+  return RW_OK;
+}
+
+PeerSet peer_set(const rw_ctx* ctx) {
+  PeerSet ps = {};
+  for (int r = 0; r < ctx->world; r++) ps.base[r] = r == ctx->rank ? ctx->sym : ctx->sym_peer[r];
+  ps.world = ctx->world;
+  ps.rank = ctx->rank;
+  const int64_t ms = ctx->timeout_ms > 0 ? std::min<int64_t>(ctx->timeout_ms, 10000) : 10000;
+  ps.timeout_ns = (uint64_t)ms * 1000000ull;
+  return ps;
+}
+
 // Phase timing with consecutive CUDA events on the context stream.
 struct PhaseTimer {
   bool on = false;
@@ -312,6 +426,17 @@ extern "C" void rw_ctx_destroy(rw_ctx* ctx) {
   if (!ctx) return;
   cudaSetDevice(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  if (ctx->sym && ctx->comm && !ctx->peer_failed) {
+    // no rank frees its region while another may still store into it (bounded wait)
+    int* one = nullptr;
+    if (cudaMalloc(reinterpret_cast<void**>(&one), 4) == cudaSuccess) {
+      if (nccl_settle(ctx, ncclAllReduce(one, one, 1, ncclInt32, ncclSum, ctx->comm,
+                                         ctx->stream)) == ncclSuccess)
+        wait_stream(ctx);
+      cudaFree(one);
+    }
+  }
+  sym_close(ctx);
   if (ctx->comm) ncclCommDestroy(ctx->comm);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
   if (ctx->pool) cudaMemPoolDestroy(ctx->pool);
@@ -517,8 +642,29 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
   RW_CU(ctx, rl_choice.get(ds, "rl_choice", (size_t)nf * NL / 2));
   uint32_t* const ncount[2] = {rl_counts.p, rl_counts.p + NL};
   uint32_t* const cursor[2] = {rl_counts.p + 2 * (size_t)NL, rl_counts.p + 3 * (size_t)NL};
-  RW_CU(ctx, hb0.get(ds, "hb0", hb_groups * cell));
-  RW_CU(ctx, hb1.get(ds, "hb1", hb_groups * cell));
+  // Built histograms (alternating levels). With several ranks exchanging over peer
+  // memory they, and their all-rank sum, live in the symmetric region instead.
+  const uint64_t hb_bytes = round_up(hb_groups * cell * 8, 256);
+  if (ctx->world > 1) {
+    rc = sym_ensure(ctx, kPeerDataOff + 3 * hb_bytes);
+    if (rc) return rc;
+  }
+  const bool peer = ctx->world > 1 && ctx->peer_mode == 1;
+  const PeerSet ps = peer ? peer_set(ctx) : PeerSet{};
+  const uint64_t off_hb[2] = {kPeerDataOff, kPeerDataOff + hb_bytes};
+  const uint64_t off_hsum = kPeerDataOff + 2 * hb_bytes;
+  long long* hbp[2];
+  long long* hsum = nullptr;
+  if (peer) {
+    hbp[0] = reinterpret_cast<long long*>(ctx->sym + off_hb[0]);
+    hbp[1] = reinterpret_cast<long long*>(ctx->sym + off_hb[1]);
+    hsum = reinterpret_cast<long long*>(ctx->sym + off_hsum);
+  } else {
+    RW_CU(ctx, hb0.get(ds, "hb0", hb_groups * cell));
+    RW_CU(ctx, hb1.get(ds, "hb1", hb_groups * cell));
+    hbp[0] = hb0.p;
+    hbp[1] = hb1.p;
+  }
   RW_CU(ctx, hf0.get(ds, "hf0", hf_nodes * cell));
   RW_CU(ctx, hf1.get(ds, "hf1", hf_nodes * cell));
   RW_CU(ctx, d_feat.get(ds, "feat", (size_t)T * D));
@@ -601,7 +747,9 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
       RW_CU(ctx, launch_goss_init(gst, goss_k, s, &nl));
       for (int pass = 0; pass < 4; pass++) {
         RW_CU(ctx, launch_goss_digit_hist(g.p, n, gst, pass, s, &nl));
-        if (ctx->comm)
+        if (peer)
+          RW_CU(ctx, launch_peer_small(ps, gst.counts, 256, 0, ++ctx->peer_epoch, kerr.p, s, &nl));
+        else if (ctx->comm)
           RW_NC(ctx, ncclAllReduce(gst.counts, gst.counts, 256, ncclUint64, ncclSum, ctx->comm, s));
         RW_CU(ctx, launch_goss_digit_select(gst, pass, s, &nl));
       }
@@ -612,8 +760,11 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
                              stride > 1 ? (uint64_t)t % stride : 0, ds->row_offset, 1, mb,
                              ncount[0], s, &nl));
     }
-    if (ctx->comm) RW_NC(ctx, ncclAllReduce(mb, mb, 2, ncclUint32, ncclMax, ctx->comm, s));
-    RW_CU(ctx, launch_quant(g.p, h.p, mb, n_pad, q.p, node.p, hb0.p, cell, ncount[0], s, &nl));
+    if (peer)
+      RW_CU(ctx, launch_peer_small(ps, mb, 2, 1, ++ctx->peer_epoch, kerr.p, s, &nl));
+    else if (ctx->comm)
+      RW_NC(ctx, ncclAllReduce(mb, mb, 2, ncclUint32, ncclMax, ctx->comm, s));
+    RW_CU(ctx, launch_quant(g.p, h.p, mb, n_pad, q.p, node.p, hbp[0], cell, ncount[0], s, &nl));
     pt.mark(RW_CAT_GRADIENTS);
 
     const uint32_t tree_seed = t * 2654435761u + 0x455A4B41u;  // src/booster.rs:351
@@ -621,8 +772,8 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
       const uint32_t n_nodes = 1u << d;
       const int mode = (d == 0 || !subtract) ? 0 : 1;
       const uint32_t groups = mode == 0 ? n_nodes : n_nodes / 2;
-      long long* hb = (d & 1) ? hb1.p : hb0.p;
-      long long* hb_next = (d & 1) ? hb0.p : hb1.p;
+      long long* hb = hbp[d & 1];
+      long long* hb_next = hbp[(d + 1) & 1];
       const uint32_t groups_next =
           d + 1 < D ? (subtract ? (1u << d) : (1u << (d + 1))) : 0u;
       HistLaunch hl;
@@ -646,12 +797,16 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
       hist_launches++;
       alg_bytes += (double)n * nf * bin_bytes + 12.0 * (double)n + 8.0 * nf * nb * groups;
       pt.mark(RW_CAT_BUILD_HIST);
-      if (ctx->comm) {
+      if (peer) {
+        RW_CU(ctx, launch_peer_sum_i64(ps, off_hb[d & 1], off_hsum, (uint64_t)groups * cell,
+                                       ++ctx->peer_epoch, kerr.p, s, &nl));
+        pt.mark(RW_CAT_ALLREDUCE);
+      } else if (ctx->comm) {
         RW_NC(ctx, ncclAllReduce(hb, hb, (size_t)groups * cell, ncclInt64, ncclSum, ctx->comm, s));
         pt.mark(RW_CAT_ALLREDUCE);
       }
       SplitLaunch sl;
-      sl.hb = hb;
+      sl.hb = peer ? hsum : hb;
       sl.hp = (d & 1) ? hf0.p : hf1.p;
       sl.hf = (d & 1) ? hf1.p : hf0.p;
       sl.hb_next = groups_next ? hb_next : nullptr;
@@ -734,8 +889,11 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
   if (kerr_h) {
     cudaEventDestroy(ev0);
     cudaEventDestroy(ev1);
+    if (kerr_h == 2) ctx->peer_failed = true;
     return fail(ctx, RW_ERR_TIMEOUT,
-                "a histogram bulk-copy wait gave up (bounded wait expired)");
+                kerr_h == 1   ? "a histogram bulk-copy wait gave up (bounded wait expired)"
+                : kerr_h == 2 ? "a wait on a peer rank expired (peer exchange)"
+                              : "a peer rank reported a failed wait");
   }
   RW_CU(ctx, cudaMemcpy(fi_gain, d_fi_gain.p, nf * 4, cudaMemcpyDeviceToHost));
   RW_CU(ctx, cudaMemcpy(fi_count, d_fi_count.p, nf * 4, cudaMemcpyDeviceToHost));

@@ -2,7 +2,8 @@
 
 Each rank builds its contiguous row shard with rw_dataset_create (n_global, row_offset)
 on its own GPU and runs rw_fit_dataset; the library all-reduces the int64 histograms,
-the fixed-point scale maxima and the GOSS digit counts. Every rank's model must be
+the fixed-point scale maxima and the GOSS digit counts, over NVLink peer memory by
+default and over NCCL with RW_PEER_EXCHANGE=0 (one case). Every rank's model must be
 bit-identical to the single-process exact oracle on all rows (the same bar as the
 1-GPU parity tests), for ragged shards too. Needs at least 2 GPUs; skipped otherwise.
 """
@@ -46,6 +47,7 @@ def _cfg(case):
 
 
 def _rank_main(rank, world, q, case, bounds, cuts, base, out_dir):
+    os.environ["RW_PEER_EXCHANGE"] = case.get("peer", "1")
     from rustwood_b200 import Context
     from rustwood_b200.booster import Dataset, fit_dataset
     if rank == 0:
@@ -73,6 +75,8 @@ CASES = [
          objective="l2", pack4=True, goss_top=0.2, goss_other=0.1, split=(0.5,)),
     dict(id="c1_subsample", data="c1", n=150_000, seed=7, nb=64, trees=5, depth=5,
          objective="logistic", subsample=0.5, split=(0.5,)),
+    dict(id="c1_nccl_transport", data="c1", n=120_001, seed=9, nb=255, trees=4, depth=6,
+         objective="logistic", split=(0.61,), peer="0"),
 ]
 
 
