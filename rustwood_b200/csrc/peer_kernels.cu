@@ -93,9 +93,13 @@ __device__ __forceinline__ void pdl_wait_only() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
+// W ranks known at compile time: each thread sums U = 16 / W vectors per step with all
+// W * U loads in flight before the adds.
+template <int W>
 __global__ void __launch_bounds__(kPeerThreads) k_peer_sum_i64(PeerSet ps, uint64_t src_off,
                                                                uint64_t dst_off, uint64_t words,
                                                                uint64_t epoch, int* err) {
+  constexpr int U = 16 / W;
   // Waits for the producing kernel; does not let the next kernel start early, so every
   // CTA of this grid is resident before a dependent grid can take SM resources.
   pdl_wait_only();
@@ -108,27 +112,40 @@ __global__ void __launch_bounds__(kPeerThreads) k_peer_sum_i64(PeerSet ps, uint6
   if (s_ok) {
     // slice of 2-word vectors owned by this rank
     const uint64_t nvec = words / 2;
-    const uint64_t per = (nvec + ps.world - 1) / ps.world;
+    const uint64_t per = (nvec + W - 1) / W;
     const uint64_t v0 = per * ps.rank, v1 = min(nvec, v0 + per);
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-    for (uint64_t v = v0 + (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; v < v1; v += stride) {
-      longlong2 x[kMaxPeers];
+    const longlong2* src[W];
+    longlong2* dst[W];
 #pragma unroll
-      for (int r = 0; r < kMaxPeers; r++)
-        if (r < ps.world) {
-          const longlong2* p = reinterpret_cast<const longlong2*>(ps.base[r] + src_off) + v;
-          x[r] = r == ps.rank ? __ldcg(p) : __ldcv(p);
+    for (int r = 0; r < W; r++) {
+      src[r] = reinterpret_cast<const longlong2*>(ps.base[r] + src_off);
+      dst[r] = reinterpret_cast<longlong2*>(ps.base[r] + dst_off);
+    }
+    for (uint64_t v = v0 + (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; v < v1;
+         v += U * stride) {
+      longlong2 x[U][W];
+#pragma unroll
+      for (int u = 0; u < U; u++)
+#pragma unroll
+        for (int r = 0; r < W; r++) {
+          const uint64_t vu = v + u * stride;
+          x[u][r] = vu < v1 ? (r == ps.rank ? __ldcg(src[r] + vu) : __ldcv(src[r] + vu))
+                            : make_longlong2(0, 0);
         }
-      longlong2 s = make_longlong2(0, 0);
 #pragma unroll
-      for (int r = 0; r < kMaxPeers; r++)
-        if (r < ps.world) {
-          s.x += x[r].x;
-          s.y += x[r].y;
+      for (int u = 0; u < U; u++) {
+        const uint64_t vu = v + u * stride;
+        if (vu >= v1) break;
+        longlong2 sum = make_longlong2(0, 0);
+#pragma unroll
+        for (int r = 0; r < W; r++) {
+          sum.x += x[u][r].x;
+          sum.y += x[u][r].y;
         }
 #pragma unroll
-      for (int r = 0; r < kMaxPeers; r++)
-        if (r < ps.world) reinterpret_cast<longlong2*>(ps.base[r] + dst_off)[v] = s;
+        for (int r = 0; r < W; r++) dst[r][vu] = sum;
+      }
     }
   }
   // Every thread's stores are made visible system-wide before its CTA counts itself
@@ -207,10 +224,19 @@ cudaError_t launch_peer_sum_i64(const PeerSet& ps, uint64_t src_off, uint64_t ds
     return cudaErrorInvalidValue;
   const uint64_t per = (words / 2 + ps.world - 1) / ps.world;
   uint64_t blocks = (per + kPeerThreads - 1) / kPeerThreads;
-  // one wave: every CTA is resident while the first one waits for the peers
-  blocks = blocks < 1 ? 1 : (blocks > 148 ? 148 : blocks);
-  cudaError_t e = launch_after(k_peer_sum_i64, dim3((unsigned)blocks), dim3(kPeerThreads), s, ps,
-                               src_off, dst_off, words, epoch, err);
+  // one wave (two CTAs per SM at most): every CTA is resident while CTA 0 signals
+  blocks = blocks < 1 ? 1 : (blocks > 296 ? 296 : blocks);
+  const dim3 g((unsigned)blocks), b(kPeerThreads);
+  cudaError_t e;
+  switch (ps.world) {
+    case 2: e = launch_after(k_peer_sum_i64<2>, g, b, s, ps, src_off, dst_off, words, epoch, err); break;
+    case 3: e = launch_after(k_peer_sum_i64<3>, g, b, s, ps, src_off, dst_off, words, epoch, err); break;
+    case 4: e = launch_after(k_peer_sum_i64<4>, g, b, s, ps, src_off, dst_off, words, epoch, err); break;
+    case 5: e = launch_after(k_peer_sum_i64<5>, g, b, s, ps, src_off, dst_off, words, epoch, err); break;
+    case 6: e = launch_after(k_peer_sum_i64<6>, g, b, s, ps, src_off, dst_off, words, epoch, err); break;
+    case 7: e = launch_after(k_peer_sum_i64<7>, g, b, s, ps, src_off, dst_off, words, epoch, err); break;
+    default: e = launch_after(k_peer_sum_i64<8>, g, b, s, ps, src_off, dst_off, words, epoch, err); break;
+  }
   if (e == cudaSuccess && nl) (*nl)++;
   return e;
 }

@@ -489,15 +489,18 @@ __global__ void __launch_bounds__(kGainThreads) k_gain(SplitLaunch a) {
     const size_t k = (a.mode == 0 ? nd : (nd >> 1)) * node_words + cell;
     load4(a.hb + k, x);
     load4(a.hb + k + kHistFeat, x + kGainCols);
-    // mode 1: the pair's built child is in hb (keyed by the parent); its sibling is
-    // parent - built
-    if (a.mode == 1 &&
-        (a.built_odd ? a.built_odd[nd >> 1] != 0 : true) != ((nd & 1u) != 0)) {
+    if (a.mode == 1) {
+      // the pair's built child is in hb (keyed by the parent); its sibling is
+      // parent - built. The parent's loads go out with the built child's (one round
+      // trip) and are dropped by the built child.
       long long pp[2 * kGainCols];
       load4(a.hp + k, pp);
       load4(a.hp + k + kHistFeat, pp + kGainCols);
+      const bool built_here =
+          (a.built_odd ? a.built_odd[nd >> 1] != 0 : true) == ((nd & 1u) != 0);
+      if (!built_here)
 #pragma unroll
-      for (int i = 0; i < 2 * (int)kGainCols; i++) x[i] = pp[i] - x[i];
+        for (int i = 0; i < 2 * (int)kGainCols; i++) x[i] = pp[i] - x[i];
     }
     long long* o = a.hf + nd * node_words + cell;
     reinterpret_cast<longlong2*>(o)[0] = make_longlong2(x[0], x[1]);
@@ -929,6 +932,11 @@ __global__ void __launch_bounds__(kApplyThreads) k_apply(ApplyLaunch a) {
   uint8_t* s_choice = reinterpret_cast<uint8_t*>(s_base + G);  // [n_nodes]
   if (listing)
     for (uint32_t g = threadIdx.x; g < G; g += blockDim.x) s_cnt[g] = 0u;
+  const uint64_t n4 = a.n_pad / 4;
+  // the first chunk's leaf indices do not depend on the split: load them first
+  const uint64_t qi0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  uint2 nd_first = make_uint2(0u, 0u);
+  if (qi0 < n4) nd_first = *reinterpret_cast<const uint2*>(a.node + qi0 * 4);
   choose_split(a, s_ft, red_g, red_i);
   const uint32_t f = s_ft[0], t = s_ft[1];
   if (listing) {
@@ -946,7 +954,6 @@ __global__ void __launch_bounds__(kApplyThreads) k_apply(ApplyLaunch a) {
     for (uint32_t l = threadIdx.x; l < a.n_leaves; l += blockDim.x)
       a.leafval[a.leaf_base + l] = __ldcg(lv + l);
   const uint8_t* col = a.colbins + (size_t)f * a.n_pad;
-  const uint64_t n4 = a.n_pad / 4;
   // block-uniform chunks of blockDim.x row quads (the list phases synchronise the CTA)
   for (uint64_t c0 = (uint64_t)blockIdx.x * blockDim.x; c0 < n4;
        c0 += (uint64_t)gridDim.x * blockDim.x) {
@@ -955,7 +962,7 @@ __global__ void __launch_bounds__(kApplyThreads) k_apply(ApplyLaunch a) {
     if (qi < n4) {
       const uint64_t r = qi * 4;
       const uint32_t b4 = *reinterpret_cast<const uint32_t*>(col + r);
-      uint2 nd2 = *reinterpret_cast<const uint2*>(a.node + r);
+      uint2 nd2 = qi == qi0 ? nd_first : *reinterpret_cast<const uint2*>(a.node + r);
       nds[0] = nd2.x & 0xffffu;
       nds[1] = nd2.x >> 16;
       nds[2] = nd2.y & 0xffffu;
@@ -998,6 +1005,11 @@ __global__ void __launch_bounds__(kApplyThreads) k_apply(ApplyLaunch a) {
       key[q] = k;
       rank[q] = base + (uint32_t)__popc(peers & ((1u << lane) - 1u));
     }
+    // the listed rows' q go out before the space reservation
+    int2 qv[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++)
+      qv[q] = key[q] != 0xffffffffu ? __ldg(L.q + qi * 4 + q) : make_int2(0, 0);
     __syncthreads();
     for (uint32_t g = threadIdx.x; g < G; g += blockDim.x) {
       const uint32_t c = s_cnt[g];
@@ -1020,8 +1032,7 @@ __global__ void __launch_bounds__(kApplyThreads) k_apply(ApplyLaunch a) {
         pos = (k & 1u) ? s_cap[pn + 1] - 1u - rk : s_cap[pn] + rk;
       }
       const uint32_t row = (uint32_t)(qi * 4 + q);
-      const int2 qv = __ldg(L.q + row);
-      if (pos < a.n_pad) L.entries[pos] = make_int4((int)row, qv.x, qv.y, 0);
+      if (pos < a.n_pad) L.entries[pos] = make_int4((int)row, qv[q].x, qv[q].y, 0);
     }
   }
 }
