@@ -12,6 +12,7 @@
 // byte-SIMD compare (__vcmpgtu4) against the broadcast threshold produces the 4 split
 // bits, and the 4 leaf indices advance in the bytes of one register
 // (leaf4 = 2*leaf4 + bits; depth <= 8 keeps every byte below 256).
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -79,31 +80,54 @@ __global__ void __launch_bounds__(kPredThreads) k_predict_u8_simd(
 }
 
 // Tiled u8 scorer (depth D <= 8 known at compile time): a persistent CTA stages its tree
-// chunk in shared memory once, then walks row blocks of kTileRows rows. Per block the
-// rows' bins are staged feature-major in shared memory as one 32-bit word per (feature,
-// thread) -- the thread's 4 rows -- so every split's bins come from a conflict-free shared
-// load; a byte-SIMD compare gives the 4 rows' bits and one LOP3 places them at bit D-1-d of
-// each row's byte. Trees are scored in order and each row's sum is sequential f32 (the
-// same order as predict_cpu).
-constexpr uint32_t kTileRows = kPredThreads * 4;
-
-template <int D>
-__global__ void __launch_bounds__(kPredThreads) k_predict_u8_tiled(
+// chunk in shared memory once, then walks row blocks of kTileRows rows, 4 rows per
+// thread. Per block the rows' bins are staged feature-major as one 32-bit word per
+// (feature, thread) -- the thread's 4 rows -- so every split's bins come from one
+// conflict-free shared load. The split test runs on the FMA pipe in half precision: two
+// byte permutes turn the 4 bins into half values 1024 + bin (exact), and per pair of rows
+// c = sat((1024 + bin) - (1024 + t)) is 1.0 exactly when bin > t (the difference is an
+// exact integer in [-255, 255]); leaf = 2 * leaf + c is exact too: the leaf starts at
+// 2^(10-D), so after D levels it holds 1024 + index < 2048, whose low byte is the index.
+// The split table holds two levels per 16-byte entry (feature word offset, -(1024 + t) as
+// half2), and two trees are walked together for four independent leaf chains per thread.
+// Trees are scored in order and each row's sum is sequential f32 (the same order as
+// predict_cpu).
+// T threads per CTA (512, or 256 when the rows of 512 threads would not fit)
+template <int D, int T>
+__global__ void __launch_bounds__(T) k_predict_u8_tiled(
     const uint8_t* __restrict__ bins, uint64_t n, uint64_t ld, uint32_t nf, uint32_t t0,
     uint32_t tc, const uint32_t* __restrict__ split8, const float* __restrict__ leafval,
     float base, int first_chunk, float* __restrict__ out) {
+  constexpr int DP = (D + 1) & ~1;  // levels per tree in the table, padded to pairs
   extern __shared__ __align__(16) unsigned char pred_raw[];
-  float* s_leaf = reinterpret_cast<float*>(pred_raw);
-  uint32_t* s_split = reinterpret_cast<uint32_t*>(pred_raw + ((size_t)tc << D) * 4);
-  uint32_t* s_rows = s_split + (size_t)tc * D;  // [nf][kPredThreads]
-  stage_model(t0, tc, D, split8, leafval, s_split, s_leaf);
+  uint2* s_sx = reinterpret_cast<uint2*>(pred_raw);  // [tc][DP]
+  float* s_leaf = reinterpret_cast<float*>(pred_raw + (size_t)tc * DP * 8);
+  uint32_t* s_rows = reinterpret_cast<uint32_t*>(s_leaf + ((size_t)tc << D));  // [nf][T]
+  for (uint32_t i = threadIdx.x; i < tc * DP; i += blockDim.x) {
+    const uint32_t tt = i / DP, d = i % DP;
+    uint2 e = make_uint2(0u, 0u);
+    if (d < (uint32_t)D) {
+      const uint32_t sv = split8[((size_t)t0 + tt) * D + d];
+      const uint32_t f = (sv >> 8) < nf ? (sv >> 8) : 0u;  // the host checks feature < nf
+      const uint32_t nt16 =
+          (uint32_t)__half_as_ushort(__float2half_rn(-(1024.0f + (float)(sv & 0xffu))));
+      e = make_uint2(f * T * 4, nt16 | (nt16 << 16));
+    }
+    s_sx[i] = e;
+  }
+  for (uint32_t i = threadIdx.x; i < (tc << D); i += blockDim.x)
+    s_leaf[i] = leafval[((size_t)t0 << D) + i];
   const uint32_t tid = threadIdx.x;
+  constexpr uint32_t kTileRows = T * 4;
   const uint64_t nblk = (n + kTileRows - 1) / kTileRows;
+  const unsigned char* my_rows = reinterpret_cast<const unsigned char*>(s_rows + tid);
+  const __half2 two = __float2half2_rn(2.0f);
+  const __half2 leaf0 = __float2half2_rn((float)(1u << (10 - D)));
   for (uint64_t blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
     const uint64_t r0 = blk * kTileRows + (uint64_t)tid * 4;  // this thread's 4 rows
     __syncthreads();  // the previous block's rows (and the model) are settled
     for (uint32_t f = 0; f < nf; f++)
-      s_rows[f * kPredThreads + tid] =
+      s_rows[f * T + tid] =
           r0 + 3 < ld ? __ldg(reinterpret_cast<const uint32_t*>(bins + (size_t)f * ld + r0)) : 0u;
     __syncthreads();
     float acc[4];
@@ -113,21 +137,47 @@ __global__ void __launch_bounds__(kPredThreads) k_predict_u8_tiled(
 #pragma unroll
       for (int k = 0; k < 4; k++) acc[k] = r0 + k < n ? out[r0 + k] : 0.0f;
     }
-    const uint32_t* rows = s_rows + tid;
-    for (uint32_t t = 0; t < tc; t++) {
-      const uint32_t* sp = s_split + t * D;
-      uint32_t leaf4 = 0;
+    // two trees per step; the sums still add tree t before tree t + 1
+    for (uint32_t t = 0; t < tc; t += 2) {
+      const bool second = t + 1 < tc;
+      const uint4* sp0 = reinterpret_cast<const uint4*>(s_sx + (size_t)t * DP);
+      const uint4* sp1 = reinterpret_cast<const uint4*>(s_sx + (size_t)(second ? t + 1 : t) * DP);
+      __half2 la0 = leaf0, lb0 = leaf0, la1 = leaf0, lb1 = leaf0;  // rows (0, 1), (2, 3)
 #pragma unroll
       for (int d = 0; d < D; d++) {
-        const uint32_t sv = sp[d];
-        const uint32_t m = __vcmpgtu4(rows[(sv >> 8) * kPredThreads], (sv & 0xffu) * 0x01010101u);
-        leaf4 |= m & (0x01010101u << (D - 1 - d));
+        // one 16-byte entry serves levels d and d + 1 (the repeated load folds away)
+        const uint4 q0 = sp0[d / 2], q1 = sp1[d / 2];
+        const uint32_t off0 = (d & 1) ? q0.z : q0.x, nt0 = (d & 1) ? q0.w : q0.y;
+        const uint32_t off1 = (d & 1) ? q1.z : q1.x, nt1 = (d & 1) ? q1.w : q1.y;
+        const uint32_t w0 = *reinterpret_cast<const uint32_t*>(my_rows + off0);
+        const uint32_t w1 = *reinterpret_cast<const uint32_t*>(my_rows + off1);
+        const uint32_t a0 = __byte_perm(w0, 0x64u, 0x4140), b0 = __byte_perm(w0, 0x64u, 0x4342);
+        const uint32_t a1 = __byte_perm(w1, 0x64u, 0x4140), b1 = __byte_perm(w1, 0x64u, 0x4342);
+        const __half2 n0 = *reinterpret_cast<const __half2*>(&nt0);
+        const __half2 n1 = *reinterpret_cast<const __half2*>(&nt1);
+        la0 = __hfma2(la0, two, __hadd2_sat(*reinterpret_cast<const __half2*>(&a0), n0));
+        lb0 = __hfma2(lb0, two, __hadd2_sat(*reinterpret_cast<const __half2*>(&b0), n0));
+        la1 = __hfma2(la1, two, __hadd2_sat(*reinterpret_cast<const __half2*>(&a1), n1));
+        lb1 = __hfma2(lb1, two, __hadd2_sat(*reinterpret_cast<const __half2*>(&b1), n1));
       }
-      const float* lv = s_leaf + ((size_t)t << D);
-      acc[0] += lv[leaf4 & 0xffu];
-      acc[1] += lv[(leaf4 >> 8) & 0xffu];
-      acc[2] += lv[(leaf4 >> 16) & 0xffu];
-      acc[3] += lv[leaf4 >> 24];
+      {
+        const uint32_t ia = *reinterpret_cast<const uint32_t*>(&la0);
+        const uint32_t ib = *reinterpret_cast<const uint32_t*>(&lb0);
+        const float* lv = s_leaf + ((size_t)t << D);
+        acc[0] += lv[ia & 0xffu];
+        acc[1] += lv[(ia >> 16) & 0xffu];
+        acc[2] += lv[ib & 0xffu];
+        acc[3] += lv[(ib >> 16) & 0xffu];
+      }
+      if (second) {
+        const uint32_t ia = *reinterpret_cast<const uint32_t*>(&la1);
+        const uint32_t ib = *reinterpret_cast<const uint32_t*>(&lb1);
+        const float* lv = s_leaf + ((size_t)(t + 1) << D);
+        acc[0] += lv[ia & 0xffu];
+        acc[1] += lv[(ia >> 16) & 0xffu];
+        acc[2] += lv[ib & 0xffu];
+        acc[3] += lv[(ib >> 16) & 0xffu];
+      }
     }
 #pragma unroll
     for (int k = 0; k < 4; k++)
@@ -136,8 +186,9 @@ __global__ void __launch_bounds__(kPredThreads) k_predict_u8_tiled(
 }
 
 template <int D>
-const void* tiled_fn() {
-  return reinterpret_cast<const void*>(&k_predict_u8_tiled<D>);
+const void* tiled_fn(int threads) {
+  return threads == 512 ? reinterpret_cast<const void*>(&k_predict_u8_tiled<D, 512>)
+                        : reinterpret_cast<const void*>(&k_predict_u8_tiled<D, 256>);
 }
 
 // One row per thread, any depth and any row stride.
@@ -220,26 +271,32 @@ static cudaError_t launch_predict_u8_tiled(const uint8_t* bins, uint64_t n, uint
                                            const rw_dmodel& m, float* out, cudaStream_t s,
                                            bool* used) {
   *used = false;
-  const size_t rows_bytes = (size_t)m.nf * kPredThreads * 4;
-  if (m.depth < 1 || m.depth > 8 || rows_bytes > 96 * 1024) return cudaSuccess;
-  const size_t per_tree = ((size_t)4 << m.depth) + 4 * (size_t)m.depth;
+  // 512 threads when their rows take at most 128 KB of shared memory, else 256
+  const int T = (size_t)m.nf * 512 * 4 <= 128 * 1024 ? 512 : 256;
+  const size_t rows_bytes = (size_t)m.nf * T * 4;
+  if (m.depth < 1 || m.depth > 8 || rows_bytes > 128 * 1024) return cudaSuccess;
+  const size_t per_tree = ((size_t)4 << m.depth) + 8 * (size_t)((m.depth + 1) & ~1u);
   const size_t budget = 220 * 1024 - rows_bytes;
   uint32_t tc = (uint32_t)std::min<size_t>(m.n_trees, budget / per_tree);
   if (tc < 1) return cudaSuccess;
-  const void* fns[9] = {nullptr,          tiled_fn<1>(), tiled_fn<2>(), tiled_fn<3>(), tiled_fn<4>(),
-                        tiled_fn<5>(),    tiled_fn<6>(), tiled_fn<7>(), tiled_fn<8>()};
+  // chunks of equal size (each chunk is one more pass over the rows)
+  const uint32_t n_chunks = (m.n_trees + tc - 1) / tc;
+  tc = (m.n_trees + n_chunks - 1) / n_chunks;
+  const void* fns[9] = {nullptr,         tiled_fn<1>(T), tiled_fn<2>(T), tiled_fn<3>(T),
+                        tiled_fn<4>(T),  tiled_fn<5>(T), tiled_fn<6>(T), tiled_fn<7>(T),
+                        tiled_fn<8>(T)};
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const uint64_t nblk = (n + kTileRows - 1) / kTileRows;
+  const uint64_t nblk = (n + (uint64_t)T * 4 - 1) / ((uint64_t)T * 4);
   for (uint32_t t0 = 0; t0 < m.n_trees; t0 += tc) {
     const uint32_t c = m.n_trees - t0 < tc ? m.n_trees - t0 : tc;
-    const size_t smem = ((size_t)c << m.depth) * 4 + (size_t)c * m.depth * 4 + rows_bytes;
+    const size_t smem = ((size_t)c << m.depth) * 4 + (size_t)c * ((m.depth + 1) & ~1u) * 8 + rows_bytes;
     cudaError_t e = cudaFuncSetAttribute(fns[m.depth], cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return e;
     int per_sm = 1;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fns[m.depth], kPredThreads, smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fns[m.depth], T, smem);
     const uint64_t grid = std::max<uint64_t>(1, std::min<uint64_t>(nblk, (uint64_t)sms * std::max(per_sm, 1)));
     int first = t0 == 0;
     uint64_t nn = n, ll = ld;
@@ -250,7 +307,7 @@ static cudaError_t launch_predict_u8_tiled(const uint8_t* bins, uint64_t n, uint
     const uint8_t* bp = bins;
     float* op = out;
     void* args[] = {&bp, &nn, &ll, &nf, &tt0, &cc, &sp, &lp, &b, &first, &op};
-    e = cudaLaunchKernel(fns[m.depth], dim3((unsigned)grid), dim3(kPredThreads), args, smem, s);
+    e = cudaLaunchKernel(fns[m.depth], dim3((unsigned)grid), dim3(T), args, smem, s);
     if (e != cudaSuccess) return e;
   }
   *used = true;
