@@ -148,12 +148,14 @@ __global__ void __launch_bounds__(kPeerThreads) k_peer_sum_i64(PeerSet ps, uint6
       }
     }
   }
-  // Every thread's stores are made visible system-wide before its CTA counts itself
-  // done; the last CTA of this rank tells every rank that its slice has landed, then
-  // waits for all ranks' slices.
-  __threadfence_system();
+  // The next kernel may launch now; it waits for this grid to complete before it reads.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // The CTA's stores are ordered before its count by the barrier and one system-scope
+  // fence (cumulative); the last CTA of this rank tells every rank that its slice has
+  // landed, then waits for all ranks' slices.
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence_system();
     unsigned int* done = done_counter(ps.base[ps.rank]);
     if (atomicAdd(done, 1u) == gridDim.x - 1) {
       atomicExch(done, 0u);
@@ -180,13 +182,13 @@ __global__ void __launch_bounds__(kPeerThreads) k_peer_small(PeerSet ps, void* d
                                : reinterpret_cast<const uint64_t*>(data)[i];
     for (int r = 0; r < ps.world; r++) slot(r, ps.rank)[i] = v;
   }
-  __threadfence_system();
-  __syncthreads();
+  __syncthreads();  // the slot stores precede thread 0's release (signal_all fences)
   if (threadIdx.x == 0) {
     signal_all(ps, kPeerSmall, epoch, err);
     s_ok = wait_all(ps, kPeerSmall, epoch, err);
   }
   __syncthreads();
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (!s_ok) return;
   for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
     uint64_t acc = 0;

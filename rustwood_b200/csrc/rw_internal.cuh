@@ -135,8 +135,6 @@ struct SplitLaunch {
   const long long* hb;  // built histogram
   const long long* hp;  // parent level full histogram (mode 1)
   long long* hf;        // this level's full histogram (out)
-  long long* hb_next;   // built-histogram buffer of the next level, zeroed here (nullable)
-  uint64_t hb_next_words;
   uint32_t n_nodes, nf, nb;
   int mode;             // 0: hb holds every node; 1: hb holds one child per pair, keyed by parent
   const uint8_t* built_odd;  // mode 1: per pair, 1 if the odd child was built (else the even)
@@ -211,6 +209,8 @@ struct ApplyLaunch {
   float* leafval;
   uint32_t leaf_base;
   uint32_t* split_out;  // nullable: (feature, bin) of the chosen split
+  long long* hb_next;   // built-histogram buffer of the next level, zeroed here (nullable)
+  uint64_t hb_next_words;  // even
 };
 cudaError_t launch_apply(const ApplyLaunch& a, cudaStream_t s, int* nl);
 cudaError_t launch_fill_f32(float* p, float v, uint64_t n, cudaStream_t s, int* nl);

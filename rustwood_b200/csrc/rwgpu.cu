@@ -809,8 +809,6 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
       sl.hb = peer ? hsum : hb;
       sl.hp = (d & 1) ? hf0.p : hf1.p;
       sl.hf = (d & 1) ? hf1.p : hf0.p;
-      sl.hb_next = groups_next ? hb_next : nullptr;
-      sl.hb_next_words = (uint64_t)groups_next * cell;
       sl.n_nodes = n_nodes;
       sl.nf = nf;
       sl.nb = nb;
@@ -868,6 +866,8 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
       al.leafval = d_leafval.p;
       al.leaf_base = t * NL;
       al.split_out = nullptr;
+      al.hb_next = groups_next ? hb_next : nullptr;
+      al.hb_next_words = (uint64_t)groups_next * cell;
       RW_CU(ctx, launch_apply(al, s, &nl));
       pt.mark(d == D - 1 ? RW_CAT_UPDATE_PRED : RW_CAT_APPLY);
     }

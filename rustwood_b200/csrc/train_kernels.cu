@@ -443,8 +443,9 @@ __device__ void block_argmax256(double& g, uint32_t& i, double* red_g, uint32_t*
     for (int w = 1; w < kBestThreads / 32; w++) argmax_merge(g, i, red_g[w], red_i[w]);
 }
 
+// 2^-e for the round's fixed-point exponent e (exact; built from the exponent bits).
 __device__ __forceinline__ double q_inv_scale(uint32_t maxbits) {
-  return 1.0 / (double)rw_pow2f(rw_qscale_exp(maxbits));
+  return __longlong_as_double((long long)(1023 - rw_qscale_exp(maxbits)) << 52);
 }
 
 // One CTA per (node, tile, group of 4 columns); thread b owns bin b of the 4 features in
@@ -587,14 +588,7 @@ __global__ void __launch_bounds__(kBestThreads) k_best(SplitLaunch a) {
   __shared__ uint32_t red_i[kBestThreads / 32];
   __shared__ uint32_t s_b;
   const uint32_t f = blockIdx.x;
-  const uint32_t nf = a.nf, nb = a.nb, nsplit = nb - 1, b = threadIdx.x;
-  // zero the next level's built-histogram buffer (this CTA's slice) and list counters
-  if (a.hb_next) {
-    const uint64_t per = (a.hb_next_words + nf - 1) / nf;
-    const uint64_t w0 = (uint64_t)f * per;
-    const uint64_t w1 = w0 + per < a.hb_next_words ? w0 + per : a.hb_next_words;
-    for (uint64_t w = w0 + threadIdx.x; w < w1; w += kBestThreads) a.hb_next[w] = 0;
-  }
+  const uint32_t nb = a.nb, nsplit = nb - 1, b = threadIdx.x;
   if (f == 0) {
     // this level's per-node row counts (from the previous level's lists) and the cursors
     // the leaf-index update fills for the next level
@@ -617,6 +611,7 @@ __global__ void __launch_bounds__(kBestThreads) k_best(SplitLaunch a) {
   const double inv_g = q_inv_scale(a.maxbits[0]), inv_h = q_inv_scale(a.maxbits[1]);
   const double lambda = a.lambda;
   double key = -RW_INF;
+  const float thr_own = b < nsplit ? __ldg(a.cuts + (size_t)f * nsplit + b) : 0.0f;
   if (b < nsplit) {
     double gain = 0.0;
     const double* t = a.term + (size_t)f * a.n_nodes * nsplit + b;
@@ -639,16 +634,21 @@ __global__ void __launch_bounds__(kBestThreads) k_best(SplitLaunch a) {
     if (dropped) key = -1e30;
     if (key != key) key = -RW_INF;  // NaN never wins (cpu.rs: `gv > bg`)
   }
+  const double key_own = key;
   uint32_t idx = b;
   block_argmax256(key, idx, red_g, red_i);
   if (threadIdx.x == 0) {
     // ties: the lowest bin; an all-infeasible feature reports bin 0
     const uint32_t bb = key == -RW_INF ? 0u : idx;
     s_b = bb;
+  }
+  __syncthreads();
+  if (threadIdx.x == s_b) {
+    // the winning bin's thread writes the record (its cut value is in its own reach)
     SplitRec r;
-    r.gain = key;
-    r.bin = bb;
-    r.thr = a.cuts[(size_t)f * nsplit + bb];
+    r.gain = key_own;
+    r.bin = s_b;
+    r.thr = thr_own;
     a.rec[f] = r;
   }
   __syncthreads();
@@ -932,6 +932,12 @@ __global__ void __launch_bounds__(kApplyThreads) k_apply(ApplyLaunch a) {
   uint8_t* s_choice = reinterpret_cast<uint8_t*>(s_base + G);  // [n_nodes]
   if (listing)
     for (uint32_t g = threadIdx.x; g < G; g += blockDim.x) s_cnt[g] = 0u;
+  if (a.hb_next) {
+    // zero the next level's built-histogram buffer, spread over the grid
+    const uint64_t vec = a.hb_next_words / 2, stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t v = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; v < vec; v += stride)
+      reinterpret_cast<longlong2*>(a.hb_next)[v] = make_longlong2(0, 0);
+  }
   const uint64_t n4 = a.n_pad / 4;
   // the first chunk's leaf indices do not depend on the split: load them first
   const uint64_t qi0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
