@@ -4,26 +4,34 @@
 // into every other rank by CUDA IPC (rwgpu.cu sets it up). It holds the per-level
 // built histograms, the reduced copy, small exchange slots and the signal words:
 //
-//   [0, kPeerHdr)    signal words: arrive[kMaxPeers], depart[kMaxPeers], small[kMaxPeers]
-//                    (u64 epochs written by the peers), done counter (u32, local)
+//   [0, kPeerHdr)    signal words (u64 epochs written by the peers): small[kMaxPeers],
+//                    arrive[kPeerMaxCtas][kMaxPeers], depart[kPeerMaxCtas][kMaxPeers]
 //   [kPeerHdr, ...)  small slots [2 parities][kMaxPeers][kPeerSmallWords] u64
 //   then             the buffers the caller places (built histograms, the sum)
 //
 // Each exchange carries an epoch, one higher than the last exchange on the context,
-// identical on every rank because every rank issues the same exchanges in order. A
-// rank signals a peer by storing 2*epoch + e into the peer's word for this rank (release
-// at system scope; e = 1 when this rank's error word is set, so an error on one rank
-// reaches every rank) and waits until all its words have reached the epoch (acquire).
-// Waits are bounded by a %globaltimer limit; on expiry the kernel sets the error word
-// to 2 and returns (the host reports RW_ERR_TIMEOUT), and later exchanges skip their
-// waits. Error word: 1 a histogram copy wait expired, 2 a peer wait expired, 3 a peer
-// reported an error.
+// identical on every rank because every rank issues the same exchanges in order. A rank
+// signals a peer by storing 2*epoch + e into the peer's word for this rank (after a
+// release fence at system scope; e = 1 when this rank's error word is set, so an error
+// on one rank reaches every rank), and waits by polling its own words with relaxed loads
+// until all reach the epoch, then an acquire fence. (On B200 a relaxed poll plus one
+// fence costs about 0.6 us over an empty launch; acquire loads in the poll loop and a
+// counter shared by all CTAs cost several microseconds more.) Waits are bounded by a
+// %globaltimer limit; on expiry the kernel sets the error word to 2 and returns (the
+// host reports RW_ERR_TIMEOUT), and later exchanges skip their waits. Error word: 1 a
+// histogram copy wait expired, 2 a peer wait expired, 3 a peer reported an error.
 //
-//   k_peer_sum_i64   two-shot all-reduce (sum) of int64 words, src -> dst on every rank:
-//                    rank r reduces slice r of the words over all ranks (its own copy
-//                    and W-1 peer loads) and stores the sums into every rank's dst.
-//                    The per-level histograms: (W-1)/W of the bytes cross NVLink in
-//                    each direction, as in a ring all-reduce, in one launch.
+//   k_peer_sum_i64   two-shot all-reduce (sum) of int64 words, src -> dst on every rank,
+//                    by stores only: rank q pushes its copy of slice r into rank r's
+//                    receive area, rank r adds the W copies of slice r and pushes the
+//                    sums into every rank's dst; (W-1)/W of the bytes cross NVLink in
+//                    each direction, as in a ring all-reduce, in one launch. CTA b of
+//                    every rank meets CTA b of every other rank only: after the scatter
+//                    (every rank's part b of the copies has landed here) and after the
+//                    gather (every rank's part b of the sums has landed here), so no CTA
+//                    waits for another CTA of its own grid. The receive area is doubled
+//                    by epoch parity, so a rank that runs one exchange ahead never
+//                    overwrites copies a slower rank is still adding.
 //   k_peer_small     one-shot all-reduce of up to kPeerSmallWords words (u64 sum or u32
 //                    max): each rank stores its words into slot [rank] of every rank,
 //                    then reduces the W slots in rank order. The round's fixed-point
@@ -39,20 +47,22 @@ namespace {
 
 constexpr int kPeerThreads = 256;
 
-__device__ __forceinline__ uint64_t* sig(char* base, int kind) {
-  return reinterpret_cast<uint64_t*>(base) + kind * kMaxPeers;
-}
-__device__ __forceinline__ unsigned int* done_counter(char* base) {
-  return reinterpret_cast<unsigned int*>(base + 3 * kMaxPeers * sizeof(uint64_t));
+// signal words: kind 0 small (one per rank), 1 arrive and 2 depart (per CTA and rank)
+__device__ __forceinline__ uint64_t* sig(char* base, int kind, uint32_t cta) {
+  uint64_t* w = reinterpret_cast<uint64_t*>(base);
+  return kind == 0 ? w : w + kMaxPeers * (1 + (size_t)(kind - 1) * kPeerMaxCtas + cta);
 }
 
-__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+__device__ __forceinline__ uint64_t ld_relaxed_sys(const uint64_t* p) {
   uint64_t v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
+}
+__device__ __forceinline__ void fence_acq_rel_sys() {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
 }
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
@@ -60,31 +70,33 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
-// Tell every rank that this rank has reached `epoch` (kind: which signal words).
-__device__ void signal_all(const PeerSet& ps, int kind, uint64_t epoch, const int* err) {
-  __threadfence_system();
+// Tell every rank that this rank has reached `epoch`: a release fence (this thread's
+// prior writes, and those ordered before them by the CTA barrier), then the stores.
+__device__ void signal_all(const PeerSet& ps, int kind, uint32_t cta, uint64_t epoch,
+                           const int* err) {
+  fence_acq_rel_sys();
   const uint64_t v = 2 * epoch + (*reinterpret_cast<const volatile int*>(err) != 0 ? 1u : 0u);
-  for (int r = 0; r < ps.world; r++) st_release_sys(sig(ps.base[r], kind) + ps.rank, v);
+  for (int r = 0; r < ps.world; r++) st_relaxed_sys(sig(ps.base[r], kind, cta) + ps.rank, v);
 }
 
-// Wait until every rank has signalled `epoch` into this rank's words; false when the
-// wait expires (error word 2) or an earlier one did.
-__device__ bool wait_all(const PeerSet& ps, int kind, uint64_t epoch, int* err) {
+// Wait until every rank has signalled `epoch` into this rank's words (then an acquire
+// fence); false when the wait expires (error word 2) or an earlier one did.
+__device__ bool wait_all(const PeerSet& ps, int kind, uint32_t cta, uint64_t epoch, int* err) {
   if (*reinterpret_cast<volatile int*>(err) == 2) return false;
-  const uint64_t* w = sig(ps.base[ps.rank], kind);
+  const uint64_t* w = sig(ps.base[ps.rank], kind, cta);
   const uint64_t t0 = globaltimer_ns();
   bool peer_err = false;
   for (int r = 0; r < ps.world; r++) {
     uint64_t v;
-    while (((v = ld_acquire_sys(w + r)) >> 1) < epoch) {
+    while (((v = ld_relaxed_sys(w + r)) >> 1) < epoch) {
       if (globaltimer_ns() - t0 > ps.timeout_ns) {
         atomicExch(err, 2);
         return false;
       }
-      __nanosleep(64);
     }
     peer_err |= (v & 1u) != 0;
   }
+  fence_acq_rel_sys();
   if (peer_err) atomicCAS(err, 0, 3);
   return true;
 }
@@ -93,76 +105,165 @@ __device__ __forceinline__ void pdl_wait_only() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
-// W ranks known at compile time: each thread sums U = 16 / W vectors per step with all
-// W * U loads in flight before the adds.
+// W ranks known at compile time. Push-only two-shot: rank q stores its src slice r into
+// rank r's receive area [parity][q] (remote stores, posted), CTA b of every rank meets
+// CTA b of every other rank, then rank r adds its own slice r to the W - 1 received
+// copies (local loads) and stores the sums into every rank's dst; a second meeting of
+// the CTAs b ends it. No NVLink loads: every byte crosses as a store. Each thread moves
+// U = 16 / W vectors per step.
 template <int W>
 __global__ void __launch_bounds__(kPeerThreads) k_peer_sum_i64(PeerSet ps, uint64_t src_off,
-                                                               uint64_t dst_off, uint64_t words,
-                                                               uint64_t epoch, int* err) {
+                                                               uint64_t dst_off, uint64_t recv_off,
+                                                               uint64_t words, uint64_t epoch,
+                                                               int* err) {
   constexpr int U = 16 / W;
-  // Waits for the producing kernel; does not let the next kernel start early, so every
-  // CTA of this grid is resident before a dependent grid can take SM resources.
-  pdl_wait_only();
+  pdl_wait_only();  // this rank's src is complete
   __shared__ int s_ok;
+  const uint64_t nvec = words / 2;
+  const uint64_t per = (nvec + W - 1) / W;  // vectors of one slice
+  const uint32_t me = (uint32_t)ps.rank;
+  const uint64_t parity = epoch & 1u;
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  const uint64_t j0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const longlong2* src = reinterpret_cast<const longlong2*>(ps.base[me] + src_off);
+  // rank r's receive area for the copy from rank q
+  auto recv = [&](uint32_t q, uint32_t r) {
+    return reinterpret_cast<longlong2*>(ps.base[r] + recv_off) + ((parity * W + q) * per);
+  };
+  // phase 1: scatter the other ranks' slices
+  for (uint64_t j = j0; j < per; j += U * stride) {
+    longlong2 x[U][W];
+#pragma unroll
+    for (int u = 0; u < U; u++)
+#pragma unroll
+      for (int r = 0; r < W; r++) {
+        const uint64_t ju = j + u * stride, v = (uint64_t)r * per + ju;
+        x[u][r] = (r != (int)me && ju < per && v < nvec) ? __ldcg(src + v) : make_longlong2(0, 0);
+      }
+#pragma unroll
+    for (int u = 0; u < U; u++)
+#pragma unroll
+      for (int r = 0; r < W; r++) {
+        const uint64_t ju = j + u * stride, v = (uint64_t)r * per + ju;
+        if (r != (int)me && ju < per && v < nvec) recv(me, r)[ju] = x[u][r];
+      }
+  }
+  __syncthreads();
   if (threadIdx.x == 0) {
-    if (blockIdx.x == 0) signal_all(ps, kPeerArrive, epoch, err);  // this rank's src is complete
-    s_ok = wait_all(ps, kPeerArrive, epoch, err);
+    signal_all(ps, 1, blockIdx.x, epoch, err);
+    s_ok = wait_all(ps, 1, blockIdx.x, epoch, err);
   }
   __syncthreads();
   if (s_ok) {
-    // slice of 2-word vectors owned by this rank
-    const uint64_t nvec = words / 2;
-    const uint64_t per = (nvec + W - 1) / W;
-    const uint64_t v0 = per * ps.rank, v1 = min(nvec, v0 + per);
-    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-    const longlong2* src[W];
+    // phase 2: this rank's slice, its own copy plus the received ones, to every rank
     longlong2* dst[W];
 #pragma unroll
-    for (int r = 0; r < W; r++) {
-      src[r] = reinterpret_cast<const longlong2*>(ps.base[r] + src_off);
-      dst[r] = reinterpret_cast<longlong2*>(ps.base[r] + dst_off);
-    }
-    for (uint64_t v = v0 + (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; v < v1;
-         v += U * stride) {
+    for (int r = 0; r < W; r++) dst[r] = reinterpret_cast<longlong2*>(ps.base[r] + dst_off);
+    for (uint64_t j = j0; j < per; j += U * stride) {
       longlong2 x[U][W];
 #pragma unroll
       for (int u = 0; u < U; u++)
 #pragma unroll
-        for (int r = 0; r < W; r++) {
-          const uint64_t vu = v + u * stride;
-          x[u][r] = vu < v1 ? (r == ps.rank ? __ldcg(src[r] + vu) : __ldcv(src[r] + vu))
-                            : make_longlong2(0, 0);
+        for (int q = 0; q < W; q++) {
+          const uint64_t ju = j + u * stride, v = (uint64_t)me * per + ju;
+          x[u][q] = (ju < per && v < nvec)
+                        ? (q == (int)me ? __ldcg(src + v) : __ldcv(recv(q, me) + ju))
+                        : make_longlong2(0, 0);
         }
 #pragma unroll
       for (int u = 0; u < U; u++) {
-        const uint64_t vu = v + u * stride;
-        if (vu >= v1) break;
+        const uint64_t ju = j + u * stride, v = (uint64_t)me * per + ju;
+        if (ju >= per || v >= nvec) break;
         longlong2 sum = make_longlong2(0, 0);
 #pragma unroll
-        for (int r = 0; r < W; r++) {
-          sum.x += x[u][r].x;
-          sum.y += x[u][r].y;
+        for (int q = 0; q < W; q++) {
+          sum.x += x[u][q].x;
+          sum.y += x[u][q].y;
         }
 #pragma unroll
-        for (int r = 0; r < W; r++) dst[r][vu] = sum;
+        for (int r = 0; r < W; r++) dst[r][v] = sum;
       }
     }
   }
   // The next kernel may launch now; it waits for this grid to complete before it reads.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  // The CTA's stores are ordered before its count by the barrier and one system-scope
-  // fence (cumulative); the last CTA of this rank tells every rank that its slice has
-  // landed, then waits for all ranks' slices.
+  // The CTA's stores are ordered before thread 0's release by the barrier; CTA b then
+  // tells every rank that its part b has landed and waits for every rank's part b.
+  __syncthreads();
+  if (threadIdx.x == 0 && s_ok) {
+    signal_all(ps, 2, blockIdx.x, epoch, err);
+    wait_all(ps, 2, blockIdx.x, epoch, err);
+  }
+}
+
+// One-shot variant for 2 ranks and small exchanges: rank q pushes its whole src into
+// every rank's receive area [parity][q], CTA b of every rank meets CTA b of every other
+// rank once, and every rank adds the W copies itself (local loads, local dst). One
+// barrier instead of two; (W-1) x the bytes leave each rank, so it is used only where
+// that is at most the two-shot's 2 (W-1)/W x, or small.
+template <int W>
+__global__ void __launch_bounds__(kPeerThreads) k_peer_sum1_i64(PeerSet ps, uint64_t src_off,
+                                                                uint64_t dst_off, uint64_t recv_off,
+                                                                uint64_t words, uint64_t epoch,
+                                                                int* err) {
+  constexpr int U = 16 / W;
+  pdl_wait_only();  // this rank's src is complete
+  __shared__ int s_ok;
+  const uint64_t nvec = words / 2;
+  const uint32_t me = (uint32_t)ps.rank;
+  const uint64_t parity = epoch & 1u;
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  const uint64_t j0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const longlong2* src = reinterpret_cast<const longlong2*>(ps.base[me] + src_off);
+  auto recv = [&](uint32_t q, uint32_t r) {
+    return reinterpret_cast<longlong2*>(ps.base[r] + recv_off) + ((parity * W + q) * nvec);
+  };
+  for (uint64_t j = j0; j < nvec; j += U * stride) {
+    longlong2 x[U];
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const uint64_t ju = j + u * stride;
+      x[u] = ju < nvec ? __ldcg(src + ju) : make_longlong2(0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const uint64_t ju = j + u * stride;
+      if (ju >= nvec) break;
+#pragma unroll
+      for (int r = 0; r < W; r++)
+        if (r != (int)me) recv(me, r)[ju] = x[u];
+    }
+  }
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();
-    unsigned int* done = done_counter(ps.base[ps.rank]);
-    if (atomicAdd(done, 1u) == gridDim.x - 1) {
-      atomicExch(done, 0u);
-      if (s_ok) {
-        signal_all(ps, kPeerDepart, epoch, err);
-        wait_all(ps, kPeerDepart, epoch, err);
+    signal_all(ps, 1, blockIdx.x, epoch, err);
+    s_ok = wait_all(ps, 1, blockIdx.x, epoch, err);
+  }
+  __syncthreads();
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (!s_ok) return;
+  longlong2* dst = reinterpret_cast<longlong2*>(ps.base[me] + dst_off);
+  for (uint64_t j = j0; j < nvec; j += U * stride) {
+    longlong2 x[U][W];
+#pragma unroll
+    for (int u = 0; u < U; u++)
+#pragma unroll
+      for (int q = 0; q < W; q++) {
+        const uint64_t ju = j + u * stride;
+        x[u][q] = ju < nvec ? (q == (int)me ? __ldcg(src + ju) : __ldcv(recv(q, me) + ju))
+                            : make_longlong2(0, 0);
       }
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const uint64_t ju = j + u * stride;
+      if (ju >= nvec) break;
+      longlong2 sum = make_longlong2(0, 0);
+#pragma unroll
+      for (int q = 0; q < W; q++) {
+        sum.x += x[u][q].x;
+        sum.y += x[u][q].y;
+      }
+      dst[ju] = sum;
     }
   }
 }
@@ -184,8 +285,8 @@ __global__ void __launch_bounds__(kPeerThreads) k_peer_small(PeerSet ps, void* d
   }
   __syncthreads();  // the slot stores precede thread 0's release (signal_all fences)
   if (threadIdx.x == 0) {
-    signal_all(ps, kPeerSmall, epoch, err);
-    s_ok = wait_all(ps, kPeerSmall, epoch, err);
+    signal_all(ps, 0, 0, epoch, err);
+    s_ok = wait_all(ps, 0, 0, epoch, err);
   }
   __syncthreads();
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -220,25 +321,61 @@ cudaError_t launch_after(void (*k)(KArgs...), dim3 grid, dim3 block, cudaStream_
 }  // namespace
 
 cudaError_t launch_peer_sum_i64(const PeerSet& ps, uint64_t src_off, uint64_t dst_off,
-                                uint64_t words, uint64_t epoch, int* err, cudaStream_t s,
-                                int* nl) {
-  if (ps.world < 2 || ps.world > kMaxPeers || (words & 1u) || (src_off | dst_off) % 16)
+                                uint64_t recv_off, uint64_t words, uint64_t epoch, int* err,
+                                cudaStream_t s, int* nl) {
+  if (ps.world < 2 || ps.world > kMaxPeers || (words & 1u) || (src_off | dst_off | recv_off) % 16)
     return cudaErrorInvalidValue;
-  const uint64_t per = (words / 2 + ps.world - 1) / ps.world;
-  uint64_t blocks = (per + kPeerThreads - 1) / kPeerThreads;
-  // one wave (two CTAs per SM at most): every CTA is resident while CTA 0 signals
-  blocks = blocks < 1 ? 1 : (blocks > 296 ? 296 : blocks);
+  // one-shot for 2 ranks (the same bytes as two-shot, one barrier) and where the
+  // (W-1) copies stay small
+  const bool one_shot = ps.world == 2 || (uint64_t)(ps.world - 1) * words * 8 <= (2u << 20);
+  const uint64_t per = one_shot ? words / 2 : (words / 2 + ps.world - 1) / ps.world;
+  // 16 / W vectors per thread per step; at most kPeerMaxCtas CTAs (each with its signal
+  // words), fewer for small exchanges
+  const uint64_t per_cta = (uint64_t)kPeerThreads * (16 / ps.world);
+  uint64_t blocks = (per + per_cta - 1) / per_cta;
+  blocks = blocks < 1 ? 1 : (blocks > (uint64_t)kPeerMaxCtas ? (uint64_t)kPeerMaxCtas : blocks);
   const dim3 g((unsigned)blocks), b(kPeerThreads);
   cudaError_t e;
-  switch (ps.world) {
-    case 2: e = launch_after(k_peer_sum_i64<2>, g, b, s, ps, src_off, dst_off, words, epoch, err); break;
-    case 3: e = launch_after(k_peer_sum_i64<3>, g, b, s, ps, src_off, dst_off, words, epoch, err); break;
-    case 4: e = launch_after(k_peer_sum_i64<4>, g, b, s, ps, src_off, dst_off, words, epoch, err); break;
-    case 5: e = launch_after(k_peer_sum_i64<5>, g, b, s, ps, src_off, dst_off, words, epoch, err); break;
-    case 6: e = launch_after(k_peer_sum_i64<6>, g, b, s, ps, src_off, dst_off, words, epoch, err); break;
-    case 7: e = launch_after(k_peer_sum_i64<7>, g, b, s, ps, src_off, dst_off, words, epoch, err); break;
-    default: e = launch_after(k_peer_sum_i64<8>, g, b, s, ps, src_off, dst_off, words, epoch, err); break;
+  if (one_shot) {
+#define RW_PEER_CASE1(w)                                                                  \
+  case w:                                                                               \
+    e = launch_after(k_peer_sum1_i64<w>, g, b, s, ps, src_off, dst_off, recv_off, words, \
+                     epoch, err);                                                       \
+    break;
+    switch (ps.world) {
+      RW_PEER_CASE1(2)
+      RW_PEER_CASE1(3)
+      RW_PEER_CASE1(4)
+      RW_PEER_CASE1(5)
+      RW_PEER_CASE1(6)
+      RW_PEER_CASE1(7)
+      default:
+        e = launch_after(k_peer_sum1_i64<8>, g, b, s, ps, src_off, dst_off, recv_off, words,
+                         epoch, err);
+        break;
+    }
+#undef RW_PEER_CASE1
+    if (e == cudaSuccess && nl) (*nl)++;
+    return e;
   }
+#define RW_PEER_CASE(w)                                                                  \
+  case w:                                                                              \
+    e = launch_after(k_peer_sum_i64<w>, g, b, s, ps, src_off, dst_off, recv_off, words, \
+                     epoch, err);                                                      \
+    break;
+  switch (ps.world) {
+    RW_PEER_CASE(2)
+    RW_PEER_CASE(3)
+    RW_PEER_CASE(4)
+    RW_PEER_CASE(5)
+    RW_PEER_CASE(6)
+    RW_PEER_CASE(7)
+    default:
+      e = launch_after(k_peer_sum_i64<8>, g, b, s, ps, src_off, dst_off, recv_off, words, epoch,
+                       err);
+      break;
+  }
+#undef RW_PEER_CASE
   if (e == cudaSuccess && nl) (*nl)++;
   return e;
 }

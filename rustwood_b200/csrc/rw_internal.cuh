@@ -15,10 +15,12 @@
 // region, mapped into every rank. Layout: signal words, then the small-exchange slots,
 // then caller-placed buffers from kPeerDataOff.
 constexpr int kMaxPeers = 8;
-constexpr size_t kPeerHdr = 4096;
+constexpr int kPeerMaxCtas = 148;  // CTAs of one all-reduce (each has its own signal words)
+// signal words: small[kMaxPeers], then arrive and depart [kPeerMaxCtas][kMaxPeers] (u64)
+constexpr size_t kPeerHdr = 64 * 1024;
+static_assert((1 + 2 * (size_t)kPeerMaxCtas) * kMaxPeers * 8 <= kPeerHdr, "signal words fit");
 constexpr int kPeerSmallWords = 256;
 constexpr size_t kPeerDataOff = kPeerHdr + 2 * (size_t)kMaxPeers * kPeerSmallWords * 8;
-enum { kPeerArrive = 0, kPeerDepart = 1, kPeerSmall = 2 };
 struct PeerSet {
   char* base[kMaxPeers];  // each rank's region as mapped in this process (own at [rank])
   int world, rank;
@@ -217,10 +219,18 @@ cudaError_t launch_fill_f32(float* p, float v, uint64_t n, cudaStream_t s, int* 
 
 // ---- peer exchanges (peer_kernels.cu) ---------------------------------------------
 // Sum of `words` int64 (even) at src_off of every rank's region into dst_off of every
-// rank's region (16-byte aligned offsets).
+// rank's region (16-byte aligned offsets); recv_off: a receive area of at least
+// peer_recv_bytes(W, words) bytes.
 cudaError_t launch_peer_sum_i64(const PeerSet& ps, uint64_t src_off, uint64_t dst_off,
-                                uint64_t words, uint64_t epoch, int* err, cudaStream_t s,
-                                int* nl);
+                                uint64_t recv_off, uint64_t words, uint64_t epoch, int* err,
+                                cudaStream_t s, int* nl);
+inline uint64_t peer_recv_bytes(int world, uint64_t words) {
+  // two parities x W copies: whole (one-shot: 2 ranks, or (W-1) x words x 8 <= 2 MB)
+  // or of a 1/W slice (two-shot); the larger, so either fits
+  const uint64_t whole = 2ull * world * (words / 2) * 16;
+  const uint64_t slice = 2ull * world * ((words / 2 + world - 1) / world) * 16;
+  return whole > slice ? whole : slice;
+}
 // In place over `data` (local device memory): n u64 summed, or n u32 maxed (max_u32).
 cudaError_t launch_peer_small(const PeerSet& ps, void* data, uint32_t n, int max_u32,
                               uint64_t epoch, int* err, cudaStream_t s, int* nl);

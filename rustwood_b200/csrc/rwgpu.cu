@@ -645,14 +645,18 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
   // Built histograms (alternating levels). With several ranks exchanging over peer
   // memory they, and their all-rank sum, live in the symmetric region instead.
   const uint64_t hb_bytes = round_up(hb_groups * cell * 8, 256);
+  // receive area of the peer all-reduce: 2 parities x W copies of a 1/W slice
+  const uint64_t recv_bytes =
+      ctx->world > 1 ? round_up(peer_recv_bytes(ctx->world, hb_groups * cell), 256) : 0;
   if (ctx->world > 1) {
-    rc = sym_ensure(ctx, kPeerDataOff + 3 * hb_bytes);
+    rc = sym_ensure(ctx, kPeerDataOff + 3 * hb_bytes + recv_bytes);
     if (rc) return rc;
   }
   const bool peer = ctx->world > 1 && ctx->peer_mode == 1;
   const PeerSet ps = peer ? peer_set(ctx) : PeerSet{};
   const uint64_t off_hb[2] = {kPeerDataOff, kPeerDataOff + hb_bytes};
   const uint64_t off_hsum = kPeerDataOff + 2 * hb_bytes;
+  const uint64_t off_recv = kPeerDataOff + 3 * hb_bytes;
   long long* hbp[2];
   long long* hsum = nullptr;
   if (peer) {
@@ -798,8 +802,9 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
       alg_bytes += (double)n * nf * bin_bytes + 12.0 * (double)n + 8.0 * nf * nb * groups;
       pt.mark(RW_CAT_BUILD_HIST);
       if (peer) {
-        RW_CU(ctx, launch_peer_sum_i64(ps, off_hb[d & 1], off_hsum, (uint64_t)groups * cell,
-                                       ++ctx->peer_epoch, kerr.p, s, &nl));
+        RW_CU(ctx, launch_peer_sum_i64(ps, off_hb[d & 1], off_hsum, off_recv,
+                                       (uint64_t)groups * cell, ++ctx->peer_epoch, kerr.p, s,
+                                       &nl));
         pt.mark(RW_CAT_ALLREDUCE);
       } else if (ctx->comm) {
         RW_NC(ctx, ncclAllReduce(hb, hb, (size_t)groups * cell, ncclInt64, ncclSum, ctx->comm, s));
