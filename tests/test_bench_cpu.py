@@ -1,0 +1,40 @@
+"""The CPU side of bench.py: the reference arm's JSON line and the scoring baseline.
+
+The reference arm times the oracle's restatement of src/cpu.rs on host cores and must
+print one JSON line with the keys the driver reads; the scoring baseline restates
+predict_cpu on a C5 sample. Both run here at tiny sizes (no GPU needed).
+"""
+import json
+import os
+import subprocess
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_reference_arm_prints_contract_line():
+    out = subprocess.run(
+        [sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--rows",
+         "20000", "--trees", "4", "--steps", "2", "--warmup", "1", "--cpu-trees", "2"],
+        capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert out.returncode == 0, out.stderr
+    lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    for k in ("impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+              "higher_is_better", "scaling", "vs_baseline", "dtype", "data", "config",
+              "cpu_baseline", "e2e"):
+        assert k in d, k
+    assert d["impl"] == "reference"
+    assert d["higher_is_better"] is False
+    assert d["value"] > 0 and d["cpu_baseline"]["value"] == d["value"]
+    assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
+    assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
+
+
+def test_predict_cpu_baseline_small_sample():
+    sys.path.insert(0, ROOT)
+    import bench
+    r = bench.predict_cpu_baseline(rows=2000)
+    assert r["rows_per_s"] > 0
+    assert r["cores"] == 1 and r["kind"] == "port"
