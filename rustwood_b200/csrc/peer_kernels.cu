@@ -32,6 +32,10 @@
 //                    waits for another CTA of its own grid. The receive area is doubled
 //                    by epoch parity, so a rank that runs one exchange ahead never
 //                    overwrites copies a slower rank is still adding.
+//   k_peer_sum1_i64  one-shot all-reduce for 2 ranks and small exchanges: every rank
+//                    pushes its whole src into every rank's receive area, CTA b of every
+//                    rank meets CTA b of every other rank once, and every rank adds the
+//                    W copies into its own dst (one barrier instead of two).
 //   k_peer_small     one-shot all-reduce of up to kPeerSmallWords words (u64 sum or u32
 //                    max): each rank stores its words into slot [rank] of every rank,
 //                    then reduces the W slots in rank order. The round's fixed-point
