@@ -188,8 +188,9 @@ cudaError_t launch_quant(const float* g, const float* h, const uint32_t* maxbits
                          int2* q, uint16_t* node, long long* hb0, uint64_t hb0_words,
                          uint32_t* ncount0, cudaStream_t s, int* nl);
 // The level's split (argmax over the per-feature records) and model slot, then
-// leaf = 2*leaf + (bin > t) keeping the excluded flag; counts the rows of every child
-// (cnt, non-final levels), or at the final level writes the leaf values and updates pred.
+// leaf = 2*leaf + (bin > t) keeping the excluded flag; at non-final levels it writes the
+// next level's row list (`lists`) and zeroes the next level's built histogram, at the
+// final level it writes the tree's leaf values and updates pred.
 struct ApplyLaunch {
   const uint8_t* colbins;
   uint64_t n_pad;
