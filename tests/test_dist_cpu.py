@@ -5,7 +5,8 @@ the collectives librwgpu issues over NCCL (all-reduce of the fixed-point scale m
 of the GOSS radix-select digit counts, of every level's int64 histogram and of the leaf
 sums). The models of all ranks must be bit-identical to each other and to the
 single-process exact oracle on the concatenated rows, including ragged shards, stride
-subsampling, GOSS and both objectives.
+subsampling, GOSS and both objectives. A rank that leaves between steps makes the
+survivor's next exchange fail with an error within the group timeout.
 """
 import multiprocessing as mp
 import os
@@ -125,3 +126,57 @@ def test_radix_select_matches_sorted_order():
     for k in (0, 1, 17, 999, 4096, 4999):
         bits = sp.kth_largest_abs_bits(g, k, sp.Exchange())
         assert np.array([bits], np.uint32).view(np.float32)[0] == srt[k]
+
+
+def _failing_rank_main(rank, world, port, out_dir):
+    """Rank 1 leaves right after joining (between steps, nothing in flight); rank 0 runs
+    the protocol and must get an error from its next collective instead of waiting."""
+    import datetime
+    import time
+
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        os._exit(3)
+    case = CASES[0]
+    x, y, cuts = _data(case["n"], case["nf"], case["nb"], case["seed"], case["objective"])
+    base = oracle.base_score(y, case["objective"])
+    bins = oracle.bin_rowmajor(x[:1000], cuts, case["nb"])
+    t0 = time.monotonic()
+    try:
+        sp.train_shard(bins, y[:1000], cuts, base, row_offset=0, n_global=case["n"],
+                       n_trees=2, depth=3, n_bins=case["nb"], ex=sp.Exchange(dist),
+                       expf=oracle.rw_expf)
+        status = "completed"
+    except Exception as e:  # the collective reports the lost rank
+        status = "error: " + type(e).__name__
+    with open(os.path.join(out_dir, "rank0.txt"), "w") as f:
+        f.write(f"{status}\n{time.monotonic() - t0:.3f}\n")
+    os._exit(0)
+
+
+def test_lost_rank_is_reported_not_waited_for():
+    """A rank that exits between steps: the surviving rank's next exchange fails within
+    the process group's timeout and the failure reaches the caller as an exception."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    with tempfile.TemporaryDirectory() as out_dir:
+        port = _free_port()
+        procs = [ctx.Process(target=_failing_rank_main, args=(r, world, port, out_dir))
+                 for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=120)
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+                p.join()
+        assert procs[1].exitcode == 3
+        assert procs[0].exitcode == 0, procs[0].exitcode
+        status, seconds = open(os.path.join(out_dir, "rank0.txt")).read().splitlines()[:2]
+    assert status.startswith("error"), status
+    assert float(seconds) < 60.0
