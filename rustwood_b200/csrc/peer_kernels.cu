@@ -32,7 +32,7 @@
 //                    waits for another CTA of its own grid. The receive area is doubled
 //                    by epoch parity, so a rank that runs one exchange ahead never
 //                    overwrites copies a slower rank is still adding.
-//   k_peer_sum1_i64  one-shot all-reduce for 2 ranks and small exchanges: every rank
+//   k_peer_sum1_i64  one-shot all-reduce for 2 ranks: every rank
 //                    pushes its whole src into every rank's receive area, CTA b of every
 //                    rank meets CTA b of every other rank once, and every rank adds the
 //                    W copies into its own dst (one barrier instead of two).
@@ -118,8 +118,8 @@ __device__ __forceinline__ void pdl_wait_only() {
 template <int W>
 __global__ void __launch_bounds__(kPeerThreads) k_peer_sum_i64(PeerSet ps, uint64_t src_off,
                                                                uint64_t dst_off, uint64_t recv_off,
-                                                               uint64_t words, uint64_t epoch,
-                                                               int* err) {
+                                                               uint64_t recv_half, uint64_t words,
+                                                               uint64_t epoch, int* err) {
   constexpr int U = 16 / W;
   pdl_wait_only();  // this rank's src is complete
   __shared__ int s_ok;
@@ -132,7 +132,7 @@ __global__ void __launch_bounds__(kPeerThreads) k_peer_sum_i64(PeerSet ps, uint6
   const longlong2* src = reinterpret_cast<const longlong2*>(ps.base[me] + src_off);
   // rank r's receive area for the copy from rank q
   auto recv = [&](uint32_t q, uint32_t r) {
-    return reinterpret_cast<longlong2*>(ps.base[r] + recv_off) + ((parity * W + q) * per);
+    return reinterpret_cast<longlong2*>(ps.base[r] + recv_off) + parity * recv_half + q * per;
   };
   // phase 1: scatter the other ranks' slices
   for (uint64_t j = j0; j < per; j += U * stride) {
@@ -200,16 +200,15 @@ __global__ void __launch_bounds__(kPeerThreads) k_peer_sum_i64(PeerSet ps, uint6
   }
 }
 
-// One-shot variant for 2 ranks and small exchanges: rank q pushes its whole src into
-// every rank's receive area [parity][q], CTA b of every rank meets CTA b of every other
-// rank once, and every rank adds the W copies itself (local loads, local dst). One
-// barrier instead of two; (W-1) x the bytes leave each rank, so it is used only where
-// that is at most the two-shot's 2 (W-1)/W x, or small.
+// One-shot variant for 2 ranks: rank q pushes its whole src into every rank's receive
+// area [parity][q], CTA b of every rank meets CTA b of every other rank once, and every
+// rank adds the W copies itself (local loads, local dst). One barrier instead of two;
+// (W-1) x the bytes leave each rank, the same as the two-shot's 2 (W-1)/W x at W = 2.
 template <int W>
 __global__ void __launch_bounds__(kPeerThreads) k_peer_sum1_i64(PeerSet ps, uint64_t src_off,
                                                                 uint64_t dst_off, uint64_t recv_off,
-                                                                uint64_t words, uint64_t epoch,
-                                                                int* err) {
+                                                                uint64_t recv_half, uint64_t words,
+                                                                uint64_t epoch, int* err) {
   constexpr int U = 16 / W;
   pdl_wait_only();  // this rank's src is complete
   __shared__ int s_ok;
@@ -220,7 +219,7 @@ __global__ void __launch_bounds__(kPeerThreads) k_peer_sum1_i64(PeerSet ps, uint
   const uint64_t j0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const longlong2* src = reinterpret_cast<const longlong2*>(ps.base[me] + src_off);
   auto recv = [&](uint32_t q, uint32_t r) {
-    return reinterpret_cast<longlong2*>(ps.base[r] + recv_off) + ((parity * W + q) * nvec);
+    return reinterpret_cast<longlong2*>(ps.base[r] + recv_off) + parity * recv_half + q * nvec;
   };
   for (uint64_t j = j0; j < nvec; j += U * stride) {
     longlong2 x[U];
@@ -325,14 +324,18 @@ cudaError_t launch_after(void (*k)(KArgs...), dim3 grid, dim3 block, cudaStream_
 }  // namespace
 
 cudaError_t launch_peer_sum_i64(const PeerSet& ps, uint64_t src_off, uint64_t dst_off,
-                                uint64_t recv_off, uint64_t words, uint64_t epoch, int* err,
-                                cudaStream_t s, int* nl) {
+                                uint64_t recv_off, uint64_t recv_half, uint64_t words,
+                                uint64_t epoch, int* err, cudaStream_t s, int* nl) {
   if (ps.world < 2 || ps.world > kMaxPeers || (words & 1u) || (src_off | dst_off | recv_off) % 16)
     return cudaErrorInvalidValue;
-  // one-shot for 2 ranks (the same bytes as two-shot, one barrier) and where the
-  // (W-1) copies stay small
-  const bool one_shot = ps.world == 2 || (uint64_t)(ps.world - 1) * words * 8 <= (2u << 20);
+  // One-shot for 2 ranks (the same bytes as two-shot, one barrier), two-shot for more.
+  // A context keeps one kind: the two lay out the receive area differently, and the
+  // one-shot ends without a second barrier, so mixing them would let a fast rank's next
+  // copies land where a slow rank is still adding.
+  const bool one_shot = ps.world == 2;
   const uint64_t per = one_shot ? words / 2 : (words / 2 + ps.world - 1) / ps.world;
+  // the W copies of this exchange fit in one parity half of the receive area
+  if ((uint64_t)ps.world * per > recv_half) return cudaErrorInvalidValue;
   // 16 / W vectors per thread per step; at most kPeerMaxCtas CTAs (each with its signal
   // words), fewer for small exchanges
   const uint64_t per_cta = (uint64_t)kPeerThreads * (16 / ps.world);
@@ -341,45 +344,27 @@ cudaError_t launch_peer_sum_i64(const PeerSet& ps, uint64_t src_off, uint64_t ds
   const dim3 g((unsigned)blocks), b(kPeerThreads);
   cudaError_t e;
   if (one_shot) {
-#define RW_PEER_CASE1(w)                                                                  \
+    e = launch_after(k_peer_sum1_i64<2>, g, b, s, ps, src_off, dst_off, recv_off, recv_half,
+                     words, epoch, err);
+  } else {
+#define RW_PEER_CASE(w)                                                                   \
   case w:                                                                               \
-    e = launch_after(k_peer_sum1_i64<w>, g, b, s, ps, src_off, dst_off, recv_off, words, \
-                     epoch, err);                                                       \
+    e = launch_after(k_peer_sum_i64<w>, g, b, s, ps, src_off, dst_off, recv_off, recv_half, \
+                     words, epoch, err);                                                \
     break;
     switch (ps.world) {
-      RW_PEER_CASE1(2)
-      RW_PEER_CASE1(3)
-      RW_PEER_CASE1(4)
-      RW_PEER_CASE1(5)
-      RW_PEER_CASE1(6)
-      RW_PEER_CASE1(7)
+      RW_PEER_CASE(3)
+      RW_PEER_CASE(4)
+      RW_PEER_CASE(5)
+      RW_PEER_CASE(6)
+      RW_PEER_CASE(7)
       default:
-        e = launch_after(k_peer_sum1_i64<8>, g, b, s, ps, src_off, dst_off, recv_off, words,
-                         epoch, err);
+        e = launch_after(k_peer_sum_i64<8>, g, b, s, ps, src_off, dst_off, recv_off, recv_half,
+                         words, epoch, err);
         break;
     }
-#undef RW_PEER_CASE1
-    if (e == cudaSuccess && nl) (*nl)++;
-    return e;
-  }
-#define RW_PEER_CASE(w)                                                                  \
-  case w:                                                                              \
-    e = launch_after(k_peer_sum_i64<w>, g, b, s, ps, src_off, dst_off, recv_off, words, \
-                     epoch, err);                                                      \
-    break;
-  switch (ps.world) {
-    RW_PEER_CASE(2)
-    RW_PEER_CASE(3)
-    RW_PEER_CASE(4)
-    RW_PEER_CASE(5)
-    RW_PEER_CASE(6)
-    RW_PEER_CASE(7)
-    default:
-      e = launch_after(k_peer_sum_i64<8>, g, b, s, ps, src_off, dst_off, recv_off, words, epoch,
-                       err);
-      break;
-  }
 #undef RW_PEER_CASE
+  }
   if (e == cudaSuccess && nl) (*nl)++;
   return e;
 }

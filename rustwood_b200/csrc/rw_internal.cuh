@@ -220,14 +220,18 @@ cudaError_t launch_fill_f32(float* p, float v, uint64_t n, cudaStream_t s, int* 
 
 // ---- peer exchanges (peer_kernels.cu) ---------------------------------------------
 // Sum of `words` int64 (even) at src_off of every rank's region into dst_off of every
-// rank's region (16-byte aligned offsets); recv_off: a receive area of at least
-// peer_recv_bytes(W, words) bytes.
+// rank's region (16-byte aligned offsets). recv_off: a receive area in two halves of
+// recv_half 16-byte vectors each (one per epoch parity), recv_half fixed for the context's
+// exchanges and at least peer_recv_bytes(W, words) / 32 for the largest of them: with
+// halves that do not move, an exchange never writes where the previous one (the other
+// parity) may still be read, and the one before that is ordered by the previous
+// exchange's barrier.
 cudaError_t launch_peer_sum_i64(const PeerSet& ps, uint64_t src_off, uint64_t dst_off,
-                                uint64_t recv_off, uint64_t words, uint64_t epoch, int* err,
-                                cudaStream_t s, int* nl);
+                                uint64_t recv_off, uint64_t recv_half, uint64_t words,
+                                uint64_t epoch, int* err, cudaStream_t s, int* nl);
 inline uint64_t peer_recv_bytes(int world, uint64_t words) {
-  // two parities x W copies: whole (one-shot: 2 ranks, or (W-1) x words x 8 <= 2 MB)
-  // or of a 1/W slice (two-shot); the larger, so either fits
+  // two parities x W copies: whole (one-shot, 2 ranks) or of a 1/W slice (two-shot,
+  // more ranks); the larger, so either fits
   const uint64_t whole = 2ull * world * (words / 2) * 16;
   const uint64_t slice = 2ull * world * ((words / 2 + world - 1) / world) * 16;
   return whole > slice ? whole : slice;

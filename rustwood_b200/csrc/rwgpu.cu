@@ -657,6 +657,10 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
   const uint64_t off_hb[2] = {kPeerDataOff, kPeerDataOff + hb_bytes};
   const uint64_t off_hsum = kPeerDataOff + 2 * hb_bytes;
   const uint64_t off_recv = kPeerDataOff + 3 * hb_bytes;
+  // one parity half of the receive area, in 16-byte vectors, sized by the fit's largest
+  // exchange and the same for all of them
+  const uint64_t recv_half =
+      ctx->world > 1 ? peer_recv_bytes(ctx->world, hb_groups * cell) / 32 : 0;
   long long* hbp[2];
   long long* hsum = nullptr;
   if (peer) {
@@ -802,7 +806,7 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
       alg_bytes += (double)n * nf * bin_bytes + 12.0 * (double)n + 8.0 * nf * nb * groups;
       pt.mark(RW_CAT_BUILD_HIST);
       if (peer) {
-        RW_CU(ctx, launch_peer_sum_i64(ps, off_hb[d & 1], off_hsum, off_recv,
+        RW_CU(ctx, launch_peer_sum_i64(ps, off_hb[d & 1], off_hsum, off_recv, recv_half,
                                        (uint64_t)groups * cell, ++ctx->peer_epoch, kerr.p, s,
                                        &nl));
         pt.mark(RW_CAT_ALLREDUCE);
