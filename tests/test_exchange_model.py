@@ -115,3 +115,90 @@ def test_two_shot_departure_barrier_orders_reuse(W):
     read their copies, so even size-scaled halves would be safe there."""
     for seed in range(300):
         assert run(W, SIZES, layout_scaled(W), seed) is None
+
+
+def run_full(W, trees, depth, seed, small_layout_parity=True):
+    """Both exchange kinds of a fit in their real order: per tree one small exchange (the
+    scale maxima: every rank stores into slot [parity][me] of every rank, signal, wait,
+    read all slots), then per level the histogram exchange; with 3+ ranks its sums are
+    pushed into every rank's reduced copy, which the split scan reads after the exchange.
+    Returns the first overwrite-before-read of any resource, or None."""
+    rng = random.Random(seed)
+    one_shot = W == 2
+    sizes = [4 << max(d - 1, 0) for d in range(depth)]
+    big = max(sizes, default=1)
+    half = W * (big if one_shot else (big + W - 1) // W)
+    signals = [[0] * W for _ in range(W)]
+    departs = [[0] * W for _ in range(W)]
+    pending = [dict() for _ in range(W)]  # (resource, index) -> epoch still to be read
+    plans = []
+    for r in range(W):
+        steps, e = [], 0
+        for _t in range(trees):
+            e += 1
+            par = (e & 1) if small_layout_parity else 0
+            steps.append(("push", e, [(t, ("slot", par, r)) for t in range(W)]))
+            steps.append(("signal", e))
+            steps.append(("wait", e))
+            steps.append(("read", e, [("slot", par, q) for q in range(W)]))
+            for n in sizes:
+                e += 1
+                par = e & 1
+                stride = n if one_shot else (n + W - 1) // W
+                steps.append(("push", e, [(t, ("recv", par * half + r * stride + j))
+                                          for t in range(W) if t != r for j in range(stride)]))
+                steps.append(("signal", e))
+                steps.append(("wait", e))
+                steps.append(("read", e, [("recv", par * half + q * stride + j)
+                                          for q in range(W) if q != r for j in range(stride)]))
+                if not one_shot:
+                    lo = r * stride
+                    steps.append(("push", e, [(t, ("sum", v)) for t in range(W)
+                                              for v in range(lo, min(n, lo + stride))]))
+                    steps.append(("depart", e))
+                    steps.append(("wait_depart", e))
+                    steps.append(("read", e, [("sum", v) for v in range(n)]))  # split scan
+        plans.append(steps)
+    pos = [0] * W
+    while any(pos[r] < len(plans[r]) for r in range(W)):
+        ready = [r for r in range(W) if pos[r] < len(plans[r]) and not (
+            (plans[r][pos[r]][0] == "wait" and min(signals[r]) < plans[r][pos[r]][1]) or
+            (plans[r][pos[r]][0] == "wait_depart" and min(departs[r]) < plans[r][pos[r]][1]))]
+        assert ready, "the schedule deadlocked"
+        r = rng.choice(ready)
+        st = plans[r][pos[r]]
+        pos[r] += 1
+        if st[0] == "push":
+            for t, key in st[2]:
+                if key in pending[t] and pending[t][key] < st[1]:
+                    return (r, t, key, pending[t][key], st[1])
+                pending[t][key] = st[1]
+        elif st[0] == "signal":
+            for t in range(W):
+                signals[t][r] = st[1]
+        elif st[0] == "depart":
+            for t in range(W):
+                departs[t][r] = st[1]
+        elif st[0] == "read":
+            for key in st[2]:
+                if pending[r].get(key) == st[1]:
+                    del pending[r][key]
+    return None
+
+
+@pytest.mark.parametrize("W", [2, 3, 4, 8])
+def test_fit_sequence_never_overwrites_unread_data(W):
+    """Small slots, receive area and reduced copy together, over two depth-6 trees."""
+    for seed in range(150):
+        assert run_full(W, trees=2, depth=6, seed=seed) is None
+
+
+def test_small_slots_need_their_parity():
+    """Back-to-back small exchanges (the GOSS radix passes) have no other barrier between
+    them: without the parity doubling a fast rank's next values could overwrite slots a
+    slower rank has not read; the model sees it (depth 0: small exchanges only)."""
+    hits = [run_full(2, trees=4, depth=0, seed=s, small_layout_parity=False)
+            for s in range(300)]
+    assert any(h is not None for h in hits)
+    for s in range(300):
+        assert run_full(2, trees=4, depth=0, seed=s) is None
