@@ -181,3 +181,67 @@ def test_target_encoding_product_matches_oracle():
         _, gmp = encoding.fit_transform_train(xp, y, cats, 10.0, 5, hb)
         assert np.float32(gmp) == np.float32(gmo)
         np.testing.assert_array_equal(xp.view(np.uint32), xo.view(np.uint32))
+
+
+def _exact_level_choice(bins, node, qscale, g, h, n_nodes, nb, lam, mc):
+    """cpu.rs's split choice for one level (src/cpu.rs:235-271: gains summed in node
+    order, lowest flat (f, b) among the maxima) from exact fixed-point histograms."""
+    e_g, e_h = qscale
+    hist = oracle.level_hist_exact(bins, node, g, h, e_g, e_h, n_nodes, False, nb)
+    cs = np.cumsum(hist, axis=2)
+    pg = cs[..., 0].astype(np.float64) * 2.0 ** -e_g
+    ph = cs[..., 1].astype(np.float64) * 2.0 ** -e_h
+    nb1 = nb - 1
+    gain = np.zeros((hist.shape[1], nb1))
+    for nd in range(n_nodes):
+        gt, ht = pg[nd, :, nb1:], ph[nd, :, nb1:]
+        parent = gt * gt / (ht + lam)
+        gl, hl = pg[nd, :, :nb1], ph[nd, :, :nb1]
+        gr, hr = gt - gl, ht - hl
+        valid = ((hl >= mc) & (hr >= mc)).astype(np.float64)
+        with np.errstate(divide="ignore", invalid="ignore"):
+            gain += valid * (gl * gl / (hl + lam) + gr * gr / (hr + lam) - parent)
+    flat = int(np.argmax(gain.reshape(-1)))
+    return flat // nb1, flat % nb1, gain
+
+
+def test_teacher_forced_exact_levels_choose_cpu_rs_splits():
+    """Teacher forcing: at every level of every tree of a faithful cpu.rs fit (oracle_ref,
+    f32 histograms), the exact fixed-point level step -- the arithmetic the CUDA path
+    matches bit for bit -- is fed the faithful model's own gradients and must choose the
+    same split, or one whose gain is within a near-tie (relative gap < 1e-4) of it."""
+    import shard_protocol as sp
+    from rustwood_b200 import synth
+    x, y, _, _ = synth.c1(20_000, seed=5)
+    nb, T, D, lr = 64, 12, 6, 0.2
+    lam, mc = 1.0, float(np.float32(1e-3))
+    cuts = oracle.compute_boundaries(x, nb)
+    base = oracle.base_score(y)
+    ref = oracle.train(x, y, cuts, base, n_trees=T, depth=D, n_bins=nb, learning_rate=lr,
+                       exact=False, n_threads=4)
+    bins = oracle.bin_rowmajor(x, cuts, nb)
+    feat = ref.feat.reshape(T, D)
+    tbin = ref.thr_bin.reshape(T, D)
+    nl = 1 << D
+    pred = np.full(len(y), np.float32(base), np.float32)
+    checked = near_ties = 0
+    for t in range(T):
+        p = (np.float32(1.0) / (np.float32(1.0) + np.exp(-pred))).astype(np.float32)
+        g = (p - y).astype(np.float32)
+        h = np.maximum((p * (np.float32(1.0) - p)).astype(np.float32), np.float32(1e-6))
+        qs = (sp.qscale_exp(int(sp.f32_bits(np.abs(g)).max())),
+              sp.qscale_exp(int(sp.f32_bits(h).max())))
+        node = np.zeros(len(y), np.int64)
+        for d in range(D):
+            f, b, gain = _exact_level_choice(bins, node.astype(np.int32), qs, g, h, 1 << d,
+                                             nb, lam, mc)
+            fr, br = int(feat[t, d]), int(tbin[t, d])
+            checked += 1
+            if (f, b) != (fr, br):
+                best, theirs = gain[f, b], gain[fr, br]
+                assert best - theirs <= 1e-4 * max(abs(best), 1e-12), (t, d, best, theirs)
+                near_ties += 1
+            node = node * 2 + (bins[:, fr] > br)  # follow the faithful tree
+        pred = (pred + ref.leafval[t * nl:(t + 1) * nl][node]).astype(np.float32)
+    assert checked == T * D
+    assert near_ties <= checked // 10
