@@ -205,15 +205,20 @@ def _exact_level_choice(bins, node, qscale, g, h, n_nodes, nb, lam, mc):
     return flat // nb1, flat % nb1, gain
 
 
-def test_teacher_forced_exact_levels_choose_cpu_rs_splits():
+@pytest.mark.parametrize("shape", ["c1_64bins", "c2_255bins"])
+def test_teacher_forced_exact_levels_choose_cpu_rs_splits(shape):
     """Teacher forcing: at every level of every tree of a faithful cpu.rs fit (oracle_ref,
     f32 histograms), the exact fixed-point level step -- the arithmetic the CUDA path
     matches bit for bit -- is fed the faithful model's own gradients and must choose the
     same split, or one whose gain is within a near-tie (relative gap < 1e-4) of it."""
     import shard_protocol as sp
     from rustwood_b200 import synth
-    x, y, _, _ = synth.c1(20_000, seed=5)
-    nb, T, D, lr = 64, 12, 6, 0.2
+    if shape == "c1_64bins":
+        x, y, _, _ = synth.c1(20_000, seed=5)
+        nb, T, D, lr = 64, 12, 6, 0.2
+    else:  # C2-shaped: integer-valued and binary features, many tied bins
+        x, y, _, _ = synth.c2(30_000, seed=6)
+        nb, T, D, lr = 255, 10, 6, 0.3
     lam, mc = 1.0, float(np.float32(1e-3))
     cuts = oracle.compute_boundaries(x, nb)
     base = oracle.base_score(y)
