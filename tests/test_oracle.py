@@ -250,3 +250,21 @@ def test_teacher_forced_exact_levels_choose_cpu_rs_splits(shape):
         pred = (pred + ref.leafval[t * nl:(t + 1) * nl][node]).astype(np.float32)
     assert checked == T * D
     assert near_ties <= checked // 10
+
+
+def test_fixed_point_scale_bounds():
+    """The round's scale keeps every |q| within 2^17 (so 8192 rows sum exactly in a 32-bit
+    shared cell: 2^13 * 2^17 = 2^30) and uses the range: the largest |q| is at least 2^16.
+    Restated from rw_expf.h (rw_qscale_exp, rw_quantize) in tests/shard_protocol.py."""
+    import shard_protocol as sp
+    rng = np.random.default_rng(9)
+    for mag in (1e-30, 1e-8, 1e-3, 0.25, 1.0, 3.0, 1e6, 1e30, 3.4e38):
+        x = (rng.uniform(-1.0, 1.0, 4097) * mag).astype(np.float32)
+        x[0] = np.float32(mag)  # make the maximum exact
+        e = sp.qscale_exp(int(sp.f32_bits(np.abs(x)).max()))
+        q = sp.quantize(x, e)
+        top = int(np.abs(q).max())
+        assert top <= 1 << sp.QBITS, (mag, top)
+        if -126 < e < 100:  # not clamped at the exponent limits
+            assert top >= 1 << (sp.QBITS - 1), (mag, top)
+    assert (8192 << sp.QBITS) <= 1 << 30
