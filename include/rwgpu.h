@@ -191,10 +191,12 @@ int rw_predict_f32_device(rw_ctx* ctx, const rw_dmodel* dm, const float* d_x, ui
  * each rounded up to 256 bytes) must fit in 4 MiB, otherwise RW_ERR_ARG is returned
  * with the size in the message. The first call on each device looks up the array's
  * device address (cudaGetSymbolAddress, with that device current), so make the first
- * call on a device before any CUDA stream capture. Every call on a device shares the
- * array: calls that overlap on the GPU (from other threads or contexts on the same
- * device) race and must be serialised by the caller. Nothing in the array has to start
- * at zero: each call overwrites the regions it reads before reading them. */
+ * call on a device before any CUDA stream capture; the address is kept for the life of
+ * the process, so a caller that resets a device (cudaDeviceReset) must reload the
+ * library before scoring on it again. Every call on a device shares the array: calls
+ * that overlap on the GPU (from other threads or contexts on the same device) race and
+ * must be serialised by the caller. Nothing in the array has to start at zero: each
+ * call overwrites the regions it reads before reading them. */
 int rw_predict_f32_noalloc(rw_ctx* ctx, const rw_model* m, const float* x_rowmajor,
                            uint64_t n, uint32_t nf, float* out);
 
@@ -214,6 +216,19 @@ float rw_base_score(const float* y, uint64_t n, int32_t objective);
 int rw_debug_level_hist(rw_dataset* ds, const int32_t* node, const float* g, const float* h,
                         int32_t e_g, int32_t e_h, uint32_t groups, int32_t odd_only,
                         int64_t* out);
+/* Runs the production split search for one level on caller data (teacher forcing):
+ * node[n] in [0, n_nodes) (< 0 excluded), g/h[n] f32, quantised with the scales the
+ * trainer takes from their maxima; every node's histogram is built (k_hist over a row
+ * list) and scanned (k_gain, k_best) with p's lambda/min_child_h/colsample/monotone and
+ * tree index `tree` (the colsample seed). Out: each feature's best gain and bin
+ * (gain_out/bin_out [nf]) and the level's choice chosen[2] = (feature, bin), picked as
+ * the trainer picks it (highest gain, ties to the lowest feature). */
+int rw_debug_level_step(rw_dataset* ds, const rw_train_params* p, const int32_t* node,
+                        const float* g, const float* h, uint32_t n_nodes, uint32_t tree,
+                        double* gain_out, uint32_t* bin_out, uint32_t* chosen);
+/* The architecture the library's kernels run as on the context's device
+ * (cudaFuncAttributes::binaryVersion: 100 for sm_100a code). */
+int rw_debug_binary_version(rw_ctx* ctx, int32_t* out);
 /* Evaluates the device exponential on n inputs (tests compare it with the host). */
 int rw_debug_expf(rw_ctx* ctx, const float* x, uint64_t n, float* out_rw, float* out_cuda);
 

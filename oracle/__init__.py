@@ -35,7 +35,8 @@ class _Params(C.Structure):
 class _Trace(C.Structure):
     _fields_ = [("level_hist", C.c_void_p * 16), ("e_g", C.c_int32), ("e_h", C.c_int32),
                 ("split_f", C.c_uint32 * 16), ("split_b", C.c_uint32 * 16),
-                ("loop_seconds", C.c_double)]
+                ("loop_seconds", C.c_double), ("trace_trees", C.c_uint32),
+                ("tree_g", C.c_void_p), ("tree_h", C.c_void_p), ("tree_leaf", C.c_void_p)]
 
 
 _lib = None
@@ -109,9 +110,10 @@ class OracleFit:
 def train(x, y, cuts, base, *, n_trees, depth, n_bins, learning_rate=0.1, lambda_=1.0,
           min_child_h=1e-3, subsample=1.0, colsample=1.0, goss_top=0.0, goss_other=0.1,
           objective="logistic", subtract=True, monotone=(), exact=True, n_threads=0,
-          trace_levels=False) -> OracleFit:
+          trace_levels=False, trace_trees=0) -> OracleFit:
     """orc_train: exact=True is oracle_exact (the GPU's arithmetic), False is oracle_ref
-    (faithful src/cpu.rs with n_threads rayon chunks)."""
+    (faithful src/cpu.rs with n_threads rayon chunks). trace_trees > 0 records the first
+    trees' g, h ([k][n] f32, 0 outside the sample) and final leaves ([k][n] u16)."""
     x = np.ascontiguousarray(x, np.float32)
     y = np.ascontiguousarray(y, np.float32)
     cuts = np.ascontiguousarray(cuts, np.float32)
@@ -140,6 +142,14 @@ def train(x, y, cuts, base, *, n_trees, depth, n_bins, learning_rate=0.1, lambda
             h = np.zeros(((1 << d), nf, n_bins, 2), np.int64)
             hists.append(h)
             tr.level_hist[d] = h.ctypes.data
+    k = min(int(trace_trees), n_trees)
+    if k:
+        r.tree_g = np.zeros((k, n), np.float32)
+        r.tree_h = np.zeros((k, n), np.float32)
+        r.tree_leaf = np.zeros((k, n), np.uint16)
+        tr.trace_trees = k
+        tr.tree_g, tr.tree_h = r.tree_g.ctypes.data, r.tree_h.ctypes.data
+        tr.tree_leaf = r.tree_leaf.ctypes.data
     rc = lib().orc_train(C.byref(p), _p(x), _p(y), n, nf, _p(cuts), base, _p(r.feat), _p(r.thr),
                          _p(r.thr_bin), _p(r.leafval), _p(r.fi_gain), _p(r.fi_count),
                          C.byref(tr))

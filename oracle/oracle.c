@@ -662,7 +662,17 @@ int orc_train(const orc_params* p, const float* x, const float* y, uint64_t n, u
       m = n;
     }
 
-    int e_g = 0, e_h = 0;
+    if (trace && t < trace->trace_trees && trace->tree_g && trace->tree_h) {
+      float* tg = trace->tree_g + (size_t)t * n;
+      float* th = trace->tree_h + (size_t)t * n;
+      memset(tg, 0, n * sizeof(float));
+      memset(th, 0, n * sizeof(float));
+      for (uint64_t q = 0; q < m; q++) {
+        tg[samp[q]] = g[samp[q]];
+        th[samp[q]] = hess[samp[q]];
+      }
+    }
+    int e_g = 0, e_h = 0, w_g = 0, w_h = 0;
     if (exact) {
       /* per-round fixed-point scales from the maxima over the sampled rows */
       float mg = 0.0f, mh = 0.0f;
@@ -677,6 +687,8 @@ int orc_train(const orc_params* p, const float* x, const float* y, uint64_t n, u
       memcpy(&bh, &mh, 4);
       e_g = rw_qscale_exp(bg);
       e_h = rw_qscale_exp(bh);
+      w_g = rw_wscale_exp(bg, n);
+      w_h = rw_wscale_exp(bh, n);
       float sg = rw_pow2f(e_g), sh = rw_pow2f(e_h);
       memset(qg, 0, n * sizeof(int32_t));
       memset(qh, 0, n * sizeof(int32_t));
@@ -794,22 +806,26 @@ int orc_train(const orc_params* p, const float* x, const float* y, uint64_t n, u
     free(prev_f);
     free(prev_i);
 
+    if (trace && t < trace->trace_trees && trace->tree_leaf)
+      for (uint64_t r = 0; r < n; r++) trace->tree_leaf[(size_t)t * n + r] = (uint16_t)node[r];
     /* leaf values (cpu.rs:286-318) */
     double* lg;
     double* lc;
     if (exact) {
+      /* exact int64 sums of the unquantised f32 g/h in the wide fixed point
+       * (rw_wquantize), so the leaf values do not depend on the histogram's 17-bit q */
       int64_t* sg = (int64_t*)calloc(leaves, sizeof(int64_t));
       int64_t* sh = (int64_t*)calloc(leaves, sizeof(int64_t));
       for (uint64_t q = 0; q < m; q++) {
         uint32_t r = samp[q];
-        sg[node[r]] += qg[r];
-        sh[node[r]] += qh[r];
+        sg[node[r]] += rw_wquantize(g[r], w_g);
+        sh[node[r]] += rw_wquantize(hess[r], w_h);
       }
       lg = (double*)malloc(leaves * sizeof(double));
       lc = (double*)malloc(leaves * sizeof(double));
       for (uint32_t l = 0; l < leaves; l++) {
-        lg[l] = (double)sg[l] * inv_g;
-        lc[l] = (double)sh[l] * inv_h;
+        lg[l] = rw_wvalue(sg[l], w_g);
+        lc[l] = rw_wvalue(sh[l], w_h);
       }
       free(sg);
       free(sh);

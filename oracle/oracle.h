@@ -17,9 +17,12 @@
  *     chunks of ceil(m/nt) sampled rows, combined by rayon's reduce tree (midpoint
  *     split down to single chunks), f64 gains, f64 leaf sums, glibc expf.
  *   exact = 1 ("oracle_exact"): the same algorithm with the GPU library's
- *     deterministic arithmetic: per-round fixed-point quantisation of g/h
- *     (rw_qscale_exp / rw_quantize), exact int64 histogram and leaf sums, and the
- *     library's rw_expf. The CUDA path must match this mode bit-for-bit.
+ *     deterministic arithmetic: per-round 17-bit fixed-point quantisation of g/h for
+ *     the histograms (rw_qscale_exp / rw_quantize), exact int64 histogram sums, leaf
+ *     sums of the unquantised f32 g/h as exact int64 sums in a wide fixed point
+ *     (rw_wscale_exp / rw_wquantize, <= 2^-43 of the round's maximum per value at 1M
+ *     rows), and the library's rw_expf. The CUDA path must match this mode
+ *     bit-for-bit.
  *
  * Parity pinning: the reference ships no tests, fixtures or golden vectors, and
  * its Rust sources cannot be built in this environment (no cargo/rustc). This
@@ -55,6 +58,14 @@ typedef struct orc_trace {
   int32_t e_g, e_h;
   uint32_t split_f[16], split_b[16];
   double loop_seconds; /* out: wall time of the tree loop (after binning) */
+  /* Optional record of the first trace_trees trees (either mode), for teacher-forced
+   * checks of one level at a time: each tree's g and h as its histograms use them
+   * ([trace_trees][n]; 0 for rows outside the tree's sample) and every row's final leaf
+   * index ([trace_trees][n]; the node at level d is leaf >> (depth - d)). */
+  uint32_t trace_trees;
+  float* tree_g;
+  float* tree_h;
+  uint16_t* tree_leaf;
 } orc_trace;
 
 int orc_default_threads(void);

@@ -92,6 +92,8 @@ def _load() -> C.CDLL:
         "rw_base_score": (f32, [vp, u64, i32]),
         "rw_debug_level_hist": (i32, [vp, vp, vp, vp, i32, i32, u32, i32, vp]),
         "rw_debug_expf": (i32, [vp, vp, u64, vp, vp]),
+        "rw_debug_binary_version": (i32, [vp, P(i32)]),
+        "rw_debug_level_step": (i32, [vp, P(TrainParams), vp, vp, vp, u32, u32, vp, vp, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -106,8 +108,8 @@ EXPORTED = [
     "rw_last_error", "rw_ctx_set_timeout", "rw_ctx_stream", "rw_dataset_create", "rw_dataset_create_device",
     "rw_dataset_destroy", "rw_dataset_bins", "rw_fit_dataset", "rw_fit", "rw_predict_f32",
     "rw_predict_u8", "rw_model_upload", "rw_model_free", "rw_predict_u8_device",
-    "rw_predict_f32_device", "rw_predict_f32_noalloc", "rw_compute_boundaries", "rw_base_score", "rw_debug_level_hist",
-    "rw_debug_expf",
+    "rw_predict_f32_device", "rw_predict_f32_noalloc", "rw_compute_boundaries", "rw_base_score",
+    "rw_debug_level_hist", "rw_debug_expf", "rw_debug_binary_version", "rw_debug_level_step",
 ]
 
 

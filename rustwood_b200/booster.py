@@ -20,7 +20,8 @@ from .config import LOGISTIC, Config
 
 
 class Context:
-    """One GPU (and optionally one NCCL rank). rw_ctx_create_rank."""
+    """One GPU (and optionally one NCCL rank of a multi-process job): rw_ctx_create_rank.
+    Context.multi(gpus) drives several GPUs from this process: rw_ctx_create."""
 
     def __init__(self, gpu: int = 0, rank: int = 0, world: int = 1, nccl_id: bytes | None = None):
         h = C.c_void_p()
@@ -28,6 +29,19 @@ class Context:
         N.check(N.lib.rw_ctx_create_rank(gpu, rank, world, idb, C.byref(h)))
         self.h = h
         self.gpu, self.rank, self.world = gpu, rank, world
+
+    @classmethod
+    def multi(cls, gpus) -> "Context":
+        """One context over several GPUs of this host (one rank per GPU inside the
+        library): fits shard rows and exchange histograms, scoring shards rows."""
+        gpus = [int(g) for g in gpus]
+        ids = (C.c_int * len(gpus))(*gpus)
+        h = C.c_void_p()
+        N.check(N.lib.rw_ctx_create(ids, len(gpus), C.byref(h)))
+        self = cls.__new__(cls)
+        self.h = h
+        self.gpu, self.rank, self.world = gpus[0], 0, len(gpus)
+        return self
 
     def close(self):
         if self.h:
@@ -177,7 +191,8 @@ class Booster:
     def ctx(self) -> Context:
         """The GPU context, created on first use (model I/O needs none)."""
         if self._ctx is None:
-            self._ctx = Context(self.cfg.gpu)
+            self._ctx = (Context.multi(self.cfg.gpus) if len(self.cfg.gpus) > 1
+                         else Context(self.cfg.gpus[0] if self.cfg.gpus else self.cfg.gpu))
         return self._ctx
 
     # -- training ----------------------------------------------------------------

@@ -42,11 +42,9 @@ def needs_build() -> bool:
     return any(os.path.getmtime(p) > t for p in deps if os.path.exists(p))
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    if not force and not needs_build():
-        return LIB
+def nvcc_command() -> list[str]:
     inc, lib = nccl_paths()
-    cmd = [
+    return [
         nvcc(),
         "-gencode", "arch=compute_100a,code=sm_100a",
         "-lineinfo", "-O3", "-std=c++17",
@@ -58,6 +56,12 @@ def build(force: bool = False, verbose: bool = False) -> str:
         f"-I{inc}", f"-L{lib}", "-l:libnccl.so.2",
         "-Xlinker", f"-rpath,{lib}",
     ]
+
+
+def build(force: bool = False, verbose: bool = False) -> str:
+    if not force and not needs_build():
+        return LIB
+    cmd = nvcc_command()
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd), flush=True)

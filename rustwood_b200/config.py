@@ -44,6 +44,9 @@ class Config:
     objective: str = LOGISTIC
     bin_sample: int = 200_000
     gpu: int = 0
+    # Extension (rustwood trains on one GPU): several GPUs of this host for one Booster,
+    # one rank per GPU inside the library (rw_ctx_create with n_gpus > 1).
+    gpus: list[int] = field(default_factory=list)
     device: str = GPU
     replicas: int = 64
     profile_out: str = ""
@@ -94,6 +97,7 @@ class Config:
                                                  [int(s) for s in v.split(",") if s]),
                 "--bin-sample": lambda: setattr(cfg, "bin_sample", int(v)),
                 "--gpu": lambda: setattr(cfg, "gpu", int(v)),
+                "--gpus": lambda: setattr(cfg, "gpus", [int(s) for s in v.split(",") if s]),
                 "--device": lambda: setattr(cfg, "device", _device(v)),
                 "--replicas": lambda: setattr(cfg, "replicas", int(v)),
                 "--profile-out": lambda: setattr(cfg, "profile_out", v),

@@ -36,7 +36,9 @@ size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
 // Device address of this device's copy of g_stage. The host-side name g_stage is only
 // a stand-in for the symbol, so the address is looked up once per device (with that
-// device current) and cached; the lookup runs on the first call on each device.
+// device current) and cached; the lookup runs on the first call on each device. The
+// cache lives as long as the process: a caller that resets a device (cudaDeviceReset)
+// and keeps using it must reload the library first.
 int stage_address(rw_ctx* ctx, unsigned char** out) {
   if (ctx->device < 0 || ctx->device >= kMaxDevices)
     return fail(ctx, RW_ERR_ARG, "device index beyond the staging table");
@@ -60,12 +62,19 @@ extern "C" int rw_predict_f32_noalloc(rw_ctx* ctx, const rw_model* m, const floa
   if (!ctx) return fail(nullptr, RW_ERR_ARG, "ctx is NULL");
   if (!m) return fail(ctx, RW_ERR_ARG, "model is NULL");
   if (m->depth < 1 || m->depth > 12) return fail(ctx, RW_ERR_ARG, "depth must be in 1..=12");
-  if (nf != m->n_features || nf == 0)
-    return fail(ctx, RW_ERR_ARG, "nf differs from the model's n_features");
+  if (nf != m->n_features) return fail(ctx, RW_ERR_ARG, "nf differs from the model's n_features");
   if (m->n_trees > 0 && (!m->feat || !m->thr || !m->leafval))
     return fail(ctx, RW_ERR_ARG, "NULL model array");
   if (n == 0) return RW_OK;
   if (!x || !out) return fail(ctx, RW_ERR_ARG, "NULL buffer");
+  if (!ctx->members.empty()) {
+    // a multi-GPU context: contiguous row shards, each GPU through its own staging array
+    const uint64_t W = ctx->members.size();
+    return for_each_rank(ctx, [&](int i) {
+      const uint64_t lo = n * (uint64_t)i / W, hi = n * (uint64_t)(i + 1) / W;
+      return rw_predict_f32_noalloc(ctx->members[i], m, x + lo * nf, hi - lo, nf, out + lo);
+    });
+  }
   const size_t K = (size_t)m->n_trees * m->depth, L = (size_t)m->n_trees << m->depth;
   for (size_t k = 0; k < K; k++)
     if (m->feat[k] >= nf) return fail(ctx, RW_ERR_ARG, "feature index out of range");

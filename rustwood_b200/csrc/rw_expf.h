@@ -144,4 +144,52 @@ RW_HD int32_t rw_quantize(float x, float scale) {
 #endif
 }
 
+/* Wide fixed point for the leaf sums.
+ *
+ * src/cpu.rs:286-318 sums the sampled rows' unquantised f32 g and h per leaf in f64.
+ * Here each row's g and h are scaled by a per-round power of two 2^w chosen from the
+ * same maxima M as the histogram scale and from the global row count n:
+ *     w = (62 - bitlen(n)) - E,  where 2^(E-1) <= M < 2^E,
+ * so every |round(x * 2^w)| <= 2^(62 - bitlen(n)) and the int64 sum over n rows stays
+ * within 2^62: the per-leaf sums are exact integers, identical in any summation order
+ * and at any GPU count. The rounding error per value is at most M * 2^-(63 - bitlen(n))
+ * (2^-43 of M at one million rows); values down to M * 2^-(39 - bitlen(n)) convert
+ * exactly. The sum goes back to double as (double)S * 2^-w (one rounding, like the
+ * reference's f64 accumulator). */
+RW_HD int rw_bitlen64(uint64_t v) {
+  int b = 0;
+  while (v) {
+    b++;
+    v >>= 1;
+  }
+  return b;
+}
+
+RW_HD int rw_wscale_exp(uint32_t max_bits, uint64_t n_rows) {
+  /* max_bits: IEEE bit pattern of a non-negative finite float M. */
+  if ((max_bits & 0x7fffffffu) == 0u) return 0;
+  int biased = (int)((max_bits >> 23) & 0xffu);
+  if (biased == 0xff) return 0; /* not finite: no meaningful scale */
+  int E = (biased == 0 ? 1 : biased) - 126;
+  int nb = rw_bitlen64(n_rows);
+  if (nb < 1) nb = 1;
+  return (62 - nb) - E; /* within [-98, 209]: rw_pow2i covers it */
+}
+
+RW_HD int64_t rw_wquantize(float x, int w) {
+  /* round-half-even of x * 2^w; the product is exact in double. */
+  if (!(x - x == 0.0f)) return 0; /* NaN or infinity */
+  double v = RW_DMUL((double)x, rw_pow2i(w));
+#if defined(__CUDA_ARCH__)
+  return (int64_t)__double2ll_rn(v);
+#else
+  return (int64_t)llrint(v);
+#endif
+}
+
+RW_HD double rw_wvalue(int64_t s, int w) {
+  /* (double)s * 2^-w: one round-to-nearest conversion, then an exact scaling. */
+  return RW_DMUL((double)s, rw_pow2i(-w));
+}
+
 #endif /* RW_EXPF_H */

@@ -5,7 +5,11 @@
 #include <nccl.h>
 #include <stdint.h>
 
+#include <condition_variable>
+#include <functional>
 #include <map>
+#include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -19,12 +23,29 @@ constexpr int kPeerMaxCtas = 148;  // CTAs of one all-reduce (each has its own s
 // signal words: small[kMaxPeers], then arrive and depart [kPeerMaxCtas][kMaxPeers] (u64)
 constexpr size_t kPeerHdr = 64 * 1024;
 static_assert((1 + 2 * (size_t)kPeerMaxCtas) * kMaxPeers * 8 <= kPeerHdr, "signal words fit");
-constexpr int kPeerSmallWords = 256;
+// one-shot exchange slots: the round maxima, GOSS digit counts and the per-tree leaf
+// sums ([2][2^depth] int64, up to 8192 words at depth 12)
+constexpr int kPeerSmallWords = 8192;
 constexpr size_t kPeerDataOff = kPeerHdr + 2 * (size_t)kMaxPeers * kPeerSmallWords * 8;
 struct PeerSet {
   char* base[kMaxPeers];  // each rank's region as mapped in this process (own at [rank])
   int world, rank;
   uint64_t timeout_ns;    // bound of every wait on a peer
+};
+
+// The ranks of one multi-GPU context created in-process (rw_ctx_create with n_gpus > 1):
+// a host rendezvous with a bounded wait, and each rank's symmetric region as a plain
+// device pointer (peer access is enabled between the ranks' devices, no IPC).
+struct RankGroup {
+  int n = 0;
+  std::mutex mu;
+  std::condition_variable cv;
+  int arrived = 0;
+  uint64_t gen = 0;
+  int acc = 0, result = 0;     // min over the ranks of the values they bring
+  bool broken = false;         // a rank gave up waiting (or failed): every later meeting fails
+  bool peer_ok = false;        // every pair of devices has peer access
+  std::vector<char*> sym;      // each rank's region, published at the meeting
 };
 
 struct rw_ctx {
@@ -46,6 +67,10 @@ struct rw_ctx {
   uint64_t peer_epoch = 0;   // exchanges issued on the region (identical on every rank)
   int peer_mode = -1;        // -1 undecided, 0 NCCL, 1 peer memory
   bool peer_failed = false;  // a bounded wait expired: the region's epochs are unusable
+  // in-process ranks: the shared group (each rank), or the ranks this context drives
+  // (the context rw_ctx_create returned for several GPUs; it owns no stream itself)
+  std::shared_ptr<RankGroup> group;
+  std::vector<rw_ctx*> members;
 };
 
 // Bins are stored twice in HBM:
@@ -73,6 +98,10 @@ struct rw_dataset {
   std::vector<float> cuts;
   // Working buffers of the boosting loop, kept across fits (named, grown on demand).
   std::map<std::string, std::pair<void*, size_t>> ws;
+  // A dataset of a multi-GPU context: one contiguous row shard per rank (shard i on
+  // ctx->members[i]); the fields above describe the whole dataset.
+  std::vector<rw_dataset*> shards;
+  std::vector<uint64_t> shard_lo;
 };
 
 struct rw_dmodel {
@@ -85,6 +114,10 @@ struct rw_dmodel {
   float* d_leafval = nullptr;
   int has_bins = 0;
 };
+
+// Runs fn(i) for every rank of a multi-GPU context (ctx->members), one host thread per
+// rank, and returns the first failure (its message on the front context).
+int for_each_rank(rw_ctx* front, const std::function<int(int)>& fn);
 
 // ---- kernel launchers (train_kernels.cu) ------------------------------------------
 
@@ -145,13 +178,13 @@ struct SplitLaunch {
   const int32_t* monotone;  // device [nf] or null
   long long* mono;      // with monotone: [nf][nb-1][4] exact left/right sums, zero on entry
   double* term;         // [nf][n_nodes][nb-1] per-node gain terms
-  long long* prefix;    // last level: [nf][n_nodes][nb][2] exact per-node bin prefixes (g, h)
+  long long* prefix;    // non-last levels with subtraction: [nf][n_nodes][nb][2] exact
+                        // per-node bin prefixes (g, h), for the built-child choice; or null
   float colsample;
   uint32_t tree_seed;
   const float* cuts;
   SplitRec* rec;        // [nf] out
   int last_level;
-  float* leafc;         // last level: [nf][2 * n_nodes] leaf values per candidate feature
   uint8_t* choice;      // non-last levels, with subtraction: [nf][n_nodes] out, 1 = build
                         // the right (odd) child of the node (the side with less hessian)
   // per-node row counts of this level from the previous level's lists (level > 0):
@@ -177,20 +210,43 @@ cudaError_t launch_bin(const float* x_rowmajor, uint64_t n, uint32_t nf, const f
 // rowbins u8 -> 4-bit pairs (separate buffers).
 cudaError_t launch_pack4(const uint8_t* d_u8, uint64_t n_pad, uint32_t nf, uint8_t* d_packed,
                          cudaStream_t s, int* nl);
+// A tree's leaf values from its per-leaf exact sums of the unquantised g and h in the
+// wide fixed point (rw_wquantize, [2][n_leaves] int64, all ranks' rows) and that round's
+// maxima: leafval[l] = (float)(-lr * G / (H + lambda)) (src/cpu.rs:316-317).
+struct LeafValues {
+  const long long* leafsum;
+  const uint32_t* maxbits;
+  uint32_t n_leaves;
+  uint64_t n_rows;  // global row count (the wide scale's row bound)
+  double lr, lambda;
+  float* leafval;   // out: the tree's slot of the model's leaf values
+};
+cudaError_t launch_leafval(const LeafValues& a, cudaStream_t s, int* nl);
+// The previous tree's pred update, done by the next round's gradient kernel:
+// pred += leafval[node & 0x7fff] for every row (src/cpu.rs:319-320).
+struct PrevTree {
+  const float* leafval;  // null: no previous tree
+  const uint16_t* node;
+};
+// Gradients of one round, after the previous tree's pred update (prev.leafval != null).
 // Also zeroes *zero_word (the level-0 row count k_quant accumulates), when non-null.
-cudaError_t launch_grad(const float* pred, const float* y, float* g, float* h, uint64_t n,
+cudaError_t launch_grad(float* pred, const float* y, float* g, float* h, uint64_t n,
                         uint64_t n_pad, int logistic, uint64_t stride, uint64_t phase,
                         uint64_t row_offset, int compute_max, uint32_t* maxbits,
-                        uint32_t* zero_word, cudaStream_t s, int* nl);
+                        uint32_t* zero_word, const PrevTree& prev, cudaStream_t s, int* nl);
 // Per round: fixed-point q = (qg, qh), the excluded flag (bit 15 of node) and node reset;
-// also zeroes the level-0 built histogram (hb0_words int64).
+// also zeroes the level-0 built histogram (hb0_words int64) and the round's leaf sums
+// (leafsum_words int64).
 cudaError_t launch_quant(const float* g, const float* h, const uint32_t* maxbits, uint64_t n_pad,
                          int2* q, uint16_t* node, long long* hb0, uint64_t hb0_words,
-                         uint32_t* ncount0, cudaStream_t s, int* nl);
+                         long long* leafsum, uint32_t leafsum_words, uint32_t* ncount0,
+                         cudaStream_t s, int* nl);
 // The level's split (argmax over the per-feature records) and model slot, then
 // leaf = 2*leaf + (bin > t) keeping the excluded flag; at non-final levels it writes the
 // next level's row list (`lists`) and zeroes the next level's built histogram, at the
-// final level it writes the tree's leaf values and updates pred.
+// final level it adds every row's unquantised g and h (wide fixed point) into its leaf's
+// sums (src/cpu.rs:286-318); launch_leafval turns them into leaf values and the next
+// round's gradient kernel adds them to pred.
 struct ApplyLaunch {
   const uint8_t* colbins;
   uint64_t n_pad;
@@ -200,17 +256,18 @@ struct ApplyLaunch {
   uint32_t n_children;
   LevelLists lists;     // non-final levels: the next level's row list
   int final_level;
-  const float* leafc;  // final level: [nf][n_leaves]
   uint32_t n_leaves;
-  float* pred;
+  const float* g;       // final level: per-row unquantised g, h
+  const float* h;
+  const uint32_t* maxbits;  // the round's maxima (the wide scales)
+  uint64_t n_rows;      // global row count
+  long long* leafsum;   // final level: [2][n_leaves] int64 out (zeroed by k_quant)
   uint32_t* feat;
   float* thr;
   uint16_t* thr_bin;
   float* fi_gain;
   float* fi_count;
   uint32_t slot;
-  float* leafval;
-  uint32_t leaf_base;
   uint32_t* split_out;  // nullable: (feature, bin) of the chosen split
   long long* hb_next;   // built-histogram buffer of the next level, zeroed here (nullable)
   uint64_t hb_next_words;  // even
@@ -262,3 +319,6 @@ cudaError_t launch_predict_u8(const uint8_t* bins, uint64_t n, uint64_t ld, cons
 // ---- test hooks ------------------------------------------------------------------
 cudaError_t launch_debug_expf(const float* x, uint64_t n, float* out_rw, float* out_cuda,
                               cudaStream_t s);
+// The SASS architecture the loaded kernels run as (cudaFuncAttributes::binaryVersion,
+// major * 10 + minor), on the current device.
+cudaError_t kernel_binary_version(int* out);

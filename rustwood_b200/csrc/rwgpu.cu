@@ -13,6 +13,7 @@
 #include <chrono>
 #include <cmath>
 #include <cstdio>
+#include <functional>
 #include <string>
 #include <thread>
 #include <vector>
@@ -173,13 +174,149 @@ int wait_stream(rw_ctx* ctx) {
 void sym_close(rw_ctx* ctx) {
   for (int r = 0; r < kMaxPeers; r++)
     if (ctx->sym_peer[r]) {
-      cudaIpcCloseMemHandle(ctx->sym_peer[r]);
+      // in-process ranks see each other's regions as plain device pointers (no handle)
+      if (!ctx->group) cudaIpcCloseMemHandle(ctx->sym_peer[r]);
       ctx->sym_peer[r] = nullptr;
     }
   if (ctx->sym) cudaFree(ctx->sym);
   ctx->sym = nullptr;
   ctx->sym_bytes = 0;
 }
+
+// ---- in-process ranks (rw_ctx_create with several GPUs) --------------------------------
+
+// A meeting of the group's ranks (host threads): every rank brings `val` and gets the
+// minimum over the ranks, or -1 when the meeting broke (a rank failed, or the wait
+// passed the context timeout); a broken group fails every later meeting.
+int group_meet(rw_ctx* ctx, int val) {
+  RankGroup& g = *ctx->group;
+  std::unique_lock<std::mutex> lk(g.mu);
+  if (g.broken) return -1;
+  const uint64_t my = g.gen;
+  g.acc = g.arrived == 0 ? val : std::min(g.acc, val);
+  if (++g.arrived == g.n) {
+    g.result = g.acc;
+    g.arrived = 0;
+    g.gen++;
+    g.cv.notify_all();
+    return g.result;
+  }
+  auto done = [&] { return g.gen != my || g.broken; };
+  if (ctx->timeout_ms > 0) {
+    if (!g.cv.wait_for(lk, std::chrono::milliseconds(ctx->timeout_ms), done)) {
+      g.broken = true;
+      g.cv.notify_all();
+      return -1;
+    }
+  } else {
+    g.cv.wait(lk, done);
+  }
+  return g.gen != my ? g.result : -1;
+}
+
+void group_break(rw_ctx* ctx) {
+  if (!ctx || !ctx->group) return;
+  std::lock_guard<std::mutex> lk(ctx->group->mu);
+  ctx->group->broken = true;
+  ctx->group->cv.notify_all();
+}
+
+// sym_ensure for in-process ranks: the same protocol as below, with the regions
+// published as device pointers at a host meeting (peer access is enabled between every
+// pair of the group's devices when the context is created).
+int sym_ensure_group(rw_ctx* ctx, size_t need) {
+  RankGroup& g = *ctx->group;
+  if (!g.peer_ok) {  // the same answer on every rank
+    ctx->peer_mode = 0;
+    return RW_OK;
+  }
+  if (ctx->peer_mode == 1 && ctx->sym_bytes >= need) return RW_OK;
+  int rc = wait_stream(ctx);
+  if (rc) return rc;
+  // nobody still reads or writes the old regions
+  if (group_meet(ctx, 1) < 0)
+    return fail(ctx, RW_ERR_TIMEOUT, "a rank of this context did not reach the exchange set-up");
+  for (int r = 0; r < kMaxPeers; r++) ctx->sym_peer[r] = nullptr;
+  if (ctx->sym) cudaFree(ctx->sym);
+  ctx->sym = nullptr;
+  ctx->sym_bytes = 0;
+  const size_t bytes = round_up(need + need / 4, 2u << 20);
+  int ok = 1;
+  if (cudaMalloc(reinterpret_cast<void**>(&ctx->sym), bytes) != cudaSuccess ||
+      cudaMemsetAsync(ctx->sym, 0, bytes, ctx->stream) != cudaSuccess ||
+      cudaStreamSynchronize(ctx->stream) != cudaSuccess) {
+    cudaGetLastError();
+    if (ctx->sym) cudaFree(ctx->sym);
+    ctx->sym = nullptr;
+    ok = 0;
+  }
+  {
+    std::lock_guard<std::mutex> lk(g.mu);
+    g.sym[ctx->rank] = ctx->sym;
+  }
+  ok = group_meet(ctx, ok);
+  if (ok < 0)
+    return fail(ctx, RW_ERR_TIMEOUT, "a rank of this context did not reach the exchange set-up");
+  if (!ok) {  // some rank has no region: every rank uses NCCL from now on
+    if (ctx->sym) cudaFree(ctx->sym);
+    ctx->sym = nullptr;
+    ctx->peer_mode = 0;
+    return RW_OK;
+  }
+  {
+    std::lock_guard<std::mutex> lk(g.mu);
+    for (int r = 0; r < ctx->world; r++)
+      if (r != ctx->rank) ctx->sym_peer[r] = g.sym[r];
+  }
+  // every rank has read every pointer before any rank moves on (the next set-up may
+  // republish them)
+  if (group_meet(ctx, 1) < 0)
+    return fail(ctx, RW_ERR_TIMEOUT, "a rank of this context did not reach the exchange set-up");
+  ctx->sym_bytes = bytes;
+  ctx->peer_epoch = 0;
+  ctx->peer_mode = 1;
+  return RW_OK;
+}
+
+// Runs fn(i) for every rank of a multi-GPU context, one host thread per rank, and
+// reports the first failure that is not a timeout (a timeout on one rank is usually the
+// consequence of another rank's failure). With break_on_fail, a failed rank breaks the
+// group (its peers stop waiting for it at host meetings).
+int run_members(rw_ctx* front, const std::function<int(int)>& fn, bool break_on_fail) {
+  const int n = (int)front->members.size();
+  std::vector<int> rc(n, RW_OK);
+  std::vector<std::thread> th;
+  bool spawn_failed = false;
+  try {
+    for (int i = 0; i < n; i++)
+      th.emplace_back([&, i] {
+        rc[i] = fn(i);
+        if (rc[i] && break_on_fail) group_break(front->members[i]);
+      });
+  } catch (...) {
+    spawn_failed = true;
+    if (!front->members.empty()) group_break(front->members[0]);
+  }
+  for (auto& t : th) t.join();
+  if (spawn_failed) return fail(front, RW_ERR_OOM, "could not start a thread per GPU");
+  int first = -1;
+  for (int i = 0; i < n; i++)
+    if (rc[i] && (first < 0 || (rc[first] == RW_ERR_TIMEOUT && rc[i] != RW_ERR_TIMEOUT)))
+      first = i;
+  if (first < 0) return RW_OK;
+  return fail(front, rc[first],
+              "rank " + std::to_string(first) + " (GPU " +
+                  std::to_string(front->members[first]->device) +
+                  "): " + front->members[first]->last_error);
+}
+
+}  // namespace
+
+int for_each_rank(rw_ctx* front, const std::function<int(int)>& fn) {
+  return run_members(front, fn, false);
+}
+
+namespace {
 
 // All ranks call this at the same point with the same size (a collective): makes every
 // rank's region at least `need` bytes, zeroed, and maps every peer's region. Decides
@@ -200,6 +337,7 @@ int sym_ensure(rw_ctx* ctx, size_t need) {
       return RW_OK;
     }
   }
+  if (ctx->group) return sym_ensure_group(ctx, need);
   if (ctx->peer_mode == 1 && ctx->sym_bytes >= need) return RW_OK;
   int rc = wait_stream(ctx);
   if (rc) return rc;
@@ -330,13 +468,84 @@ int check_params(rw_ctx* ctx, const rw_train_params* p, uint32_t n_bins) {
 // =================================================================================
 // contexts
 
+static void destroy_members(std::vector<rw_ctx*>& m);
+
 extern "C" int rw_ctx_create(const int* gpu_ids, int n_gpus, rw_ctx** out) {
   if (!out) return fail(nullptr, RW_ERR_ARG, "out is NULL");
   *out = nullptr;
-  if (n_gpus != 1)
-    return fail(nullptr, RW_ERR_UNSUPPORTED,
-                "rw_ctx_create takes one GPU; use rw_ctx_create_rank per process");
-  return rw_ctx_create_rank(gpu_ids ? gpu_ids[0] : 0, 0, 1, nullptr, out);
+  if (n_gpus < 1 || n_gpus > kMaxPeers)
+    return fail(nullptr, RW_ERR_ARG, "n_gpus must be in 1..=8");
+  if (n_gpus == 1) return rw_ctx_create_rank(gpu_ids ? gpu_ids[0] : 0, 0, 1, nullptr, out);
+  if (!gpu_ids) return fail(nullptr, RW_ERR_ARG, "gpu_ids is NULL");
+  int ndev = 0;
+  cudaError_t e = cudaGetDeviceCount(&ndev);
+  if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaGetDeviceCount");
+  for (int i = 0; i < n_gpus; i++) {
+    if (gpu_ids[i] < 0 || gpu_ids[i] >= ndev) return fail(nullptr, RW_ERR_ARG, "gpu id out of range");
+    // two ranks on one GPU would wait on each other inside concurrent kernels
+    for (int j = 0; j < i; j++)
+      if (gpu_ids[j] == gpu_ids[i]) return fail(nullptr, RW_ERR_ARG, "gpu_ids repeat a GPU");
+  }
+  // One rank per GPU, in this process: NCCL communicators initialised together, one
+  // thread per rank.
+  ncclUniqueId id;
+  ncclResult_t r = ncclGetUniqueId(&id);
+  if (r != ncclSuccess)
+    return fail(nullptr, RW_ERR_NCCL, std::string("ncclGetUniqueId: ") + ncclGetErrorString(r));
+  std::vector<rw_ctx*> m(n_gpus, nullptr);
+  std::vector<int> rc(n_gpus, RW_OK);
+  std::vector<std::string> err(n_gpus);
+  {
+    std::vector<std::thread> th;
+    try {
+      for (int i = 0; i < n_gpus; i++)
+        th.emplace_back([&, i] {
+          rc[i] = rw_ctx_create_rank(gpu_ids[i], i, n_gpus, &id, &m[i]);
+          if (rc[i]) err[i] = g_tls_error;
+        });
+    } catch (...) {
+      for (auto& t : th) t.join();
+      destroy_members(m);
+      return fail(nullptr, RW_ERR_OOM, "could not start a thread per GPU");
+    }
+    for (auto& t : th) t.join();
+  }
+  for (int i = 0; i < n_gpus; i++)
+    if (rc[i]) {
+      destroy_members(m);
+      return fail(nullptr, rc[i], "GPU " + std::to_string(gpu_ids[i]) + ": " + err[i]);
+    }
+  auto grp = std::make_shared<RankGroup>();
+  grp->n = n_gpus;
+  grp->sym.assign(n_gpus, nullptr);
+  // peer access between every pair of the group's devices (kept for the process)
+  bool peer_ok = true;
+  for (int i = 0; i < n_gpus && peer_ok; i++) {
+    cudaSetDevice(gpu_ids[i]);
+    for (int j = 0; j < n_gpus && peer_ok; j++) {
+      if (i == j) continue;
+      int can = 0;
+      if (cudaDeviceCanAccessPeer(&can, gpu_ids[i], gpu_ids[j]) != cudaSuccess || !can) {
+        peer_ok = false;
+        break;
+      }
+      cudaError_t pe = cudaDeviceEnablePeerAccess(gpu_ids[j], 0);
+      if (pe == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+      else if (pe != cudaSuccess) {
+        cudaGetLastError();
+        peer_ok = false;
+      }
+    }
+  }
+  grp->peer_ok = peer_ok;
+  auto* front = new rw_ctx();
+  front->device = gpu_ids[0];
+  front->rank = 0;
+  front->world = n_gpus;
+  front->members = m;
+  for (auto* c : m) c->group = grp;
+  *out = front;
+  return RW_OK;
 }
 
 extern "C" int rw_nccl_unique_id(void* out128) {
@@ -422,11 +631,34 @@ extern "C" int rw_ctx_create_rank(int gpu_id, int rank, int world, const void* n
   return RW_OK;
 }
 
+// Destroys in-process ranks, one thread each (communicator teardown may involve every
+// rank of the communicator).
+static void destroy_members(std::vector<rw_ctx*>& m) {
+  std::vector<std::thread> th;
+  for (auto*& c : m)
+    if (c) {
+      try {
+        th.emplace_back([c] { rw_ctx_destroy(c); });
+      } catch (...) {
+        rw_ctx_destroy(c);
+      }
+      c = nullptr;
+    }
+  for (auto& t : th) t.join();
+}
+
 extern "C" void rw_ctx_destroy(rw_ctx* ctx) {
   if (!ctx) return;
+  if (!ctx->members.empty()) {
+    destroy_members(ctx->members);
+    delete ctx;
+    return;
+  }
   cudaSetDevice(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
-  if (ctx->sym && ctx->comm && !ctx->peer_failed) {
+  // In-process ranks have no kernel in flight here (every call waits for all of its
+  // ranks' streams before it returns), so they skip the freeing barrier.
+  if (ctx->sym && ctx->comm && !ctx->peer_failed && !ctx->group) {
     // no rank frees its region while another may still store into it (bounded wait)
     int* one = nullptr;
     if (cudaMalloc(reinterpret_cast<void**>(&one), 4) == cudaSuccess) {
@@ -447,11 +679,15 @@ extern "C" const char* rw_last_error(const rw_ctx* ctx) {
   return ctx ? ctx->last_error.c_str() : g_tls_error.c_str();
 }
 
-extern "C" void* rw_ctx_stream(const rw_ctx* ctx) { return ctx ? (void*)ctx->stream : nullptr; }
+extern "C" void* rw_ctx_stream(const rw_ctx* ctx) {
+  if (ctx && !ctx->members.empty()) return (void*)ctx->members[0]->stream;
+  return ctx ? (void*)ctx->stream : nullptr;
+}
 
 extern "C" int rw_ctx_set_timeout(rw_ctx* ctx, int64_t ms) {
   if (!ctx || ms < 0) return fail(ctx, RW_ERR_ARG, "bad timeout");
   ctx->timeout_ms = ms;
+  for (auto* c : ctx->members) c->timeout_ms = ms;
   return RW_OK;
 }
 
@@ -531,12 +767,79 @@ static int dataset_args_ok(rw_ctx* ctx, const void* x, const void* y, uint64_t n
   return RW_OK;
 }
 
+// A dataset of a multi-GPU context: the rows split into contiguous shards, one per rank,
+// each uploaded and binned by its rank's thread on its own GPU (row ids stay global, so
+// hashes and the subsample stride see the same rows as on one GPU).
+static int group_dataset_create(rw_ctx* front, const float* x, const float* y, bool on_device,
+                                uint64_t n, uint32_t nf, const float* cuts, uint32_t n_bins,
+                                int32_t pack4, uint64_t n_global, uint64_t row_offset,
+                                rw_dataset** out) {
+  const int W = (int)front->members.size();
+  if (n_global != n || row_offset != 0)
+    return fail(front, RW_ERR_ARG,
+                "a multi-GPU context takes the whole dataset (n_global = n, row_offset = 0)");
+  if (n < (uint64_t)W) return fail(front, RW_ERR_ARG, "fewer rows than GPUs");
+  int src_dev = -1;
+  if (on_device) {
+    cudaPointerAttributes ax, ay;
+    if (cudaPointerGetAttributes(&ax, x) != cudaSuccess ||
+        cudaPointerGetAttributes(&ay, y) != cudaSuccess || ax.type != cudaMemoryTypeDevice ||
+        ay.type != cudaMemoryTypeDevice || ax.device != ay.device) {
+      cudaGetLastError();
+      return fail(front, RW_ERR_ARG, "x and y must be device memory of one GPU");
+    }
+    src_dev = ax.device;
+  }
+  auto* gd = new rw_dataset();
+  gd->ctx = front;
+  gd->n = gd->n_pad = gd->n_global = n;
+  gd->nf = nf;
+  gd->n_bins = n_bins;
+  gd->packed = (pack4 && n_bins <= 16) ? 1 : 0;
+  gd->ftiles = (nf + kHistFeat - 1) / kHistFeat;
+  gd->cuts.assign(cuts, cuts + (size_t)nf * (n_bins - 1));
+  gd->shards.assign(W, nullptr);
+  gd->shard_lo.resize(W + 1);
+  for (int i = 0; i <= W; i++) gd->shard_lo[i] = n * (uint64_t)i / (uint64_t)W;
+  int rc = run_members(
+      front,
+      [&](int i) -> int {
+        rw_ctx* c = front->members[i];
+        const uint64_t lo = gd->shard_lo[i], rows = gd->shard_lo[i + 1] - lo;
+        if (!on_device)
+          return rw_dataset_create(c, x + lo * nf, y + lo, rows, nf, cuts, n_bins, pack4, n, lo,
+                                   &gd->shards[i]);
+        // this rank's slice comes to its own GPU first (peer copy), then it is binned there
+        RW_CU(c, cudaSetDevice(c->device));
+        DBuf<float> lx, ly;
+        RW_CU(c, lx.alloc(c, (size_t)rows * nf));
+        RW_CU(c, ly.alloc(c, (size_t)rows));
+        RW_CU(c, cudaMemcpyPeerAsync(lx.p, c->device, x + lo * nf, src_dev,
+                                     (size_t)rows * nf * sizeof(float), c->stream));
+        RW_CU(c, cudaMemcpyPeerAsync(ly.p, c->device, y + lo, src_dev, (size_t)rows * sizeof(float),
+                                     c->stream));
+        return rw_dataset_create_device(c, lx.p, ly.p, rows, nf, cuts, n_bins, pack4, n, lo,
+                                        &gd->shards[i]);
+      },
+      false);
+  if (rc) {
+    for (auto* sd : gd->shards) rw_dataset_destroy(sd);
+    delete gd;
+    return rc;
+  }
+  *out = gd;
+  return RW_OK;
+}
+
 extern "C" int rw_dataset_create(rw_ctx* ctx, const float* x, const float* y, uint64_t n,
                                  uint32_t nf, const float* cuts, uint32_t n_bins, int32_t pack4,
                                  uint64_t n_global, uint64_t row_offset, rw_dataset** out) {
   int rc = dataset_args_ok(ctx, x, y, n, nf, cuts, n_bins, n_global, row_offset, out);
   if (rc) return rc;
   *out = nullptr;
+  if (!ctx->members.empty())
+    return group_dataset_create(ctx, x, y, false, n, nf, cuts, n_bins, pack4, n_global,
+                                row_offset, out);
   RW_CU(ctx, cudaSetDevice(ctx->device));
   DBuf<float> dx;
   RW_CU(ctx, dx.alloc(ctx, (size_t)n * nf));
@@ -553,6 +856,9 @@ extern "C" int rw_dataset_create_device(rw_ctx* ctx, const float* d_x, const flo
   int rc = dataset_args_ok(ctx, d_x, d_y, n, nf, cuts, n_bins, n_global, row_offset, out);
   if (rc) return rc;
   *out = nullptr;
+  if (!ctx->members.empty())
+    return group_dataset_create(ctx, d_x, d_y, true, n, nf, cuts, n_bins, pack4, n_global,
+                                row_offset, out);
   RW_CU(ctx, cudaSetDevice(ctx->device));
   return dataset_build(ctx, d_x, d_y, true, n, nf, cuts, n_bins, pack4, n_global, row_offset,
                        out);
@@ -560,6 +866,11 @@ extern "C" int rw_dataset_create_device(rw_ctx* ctx, const float* d_x, const flo
 
 extern "C" void rw_dataset_destroy(rw_dataset* ds) {
   if (!ds) return;
+  if (!ds->shards.empty()) {
+    for (auto* sd : ds->shards) rw_dataset_destroy(sd);
+    delete ds;
+    return;
+  }
   cudaSetDevice(ds->ctx->device);
   rw_ctx* ctx = ds->ctx;
   pool_free(ctx, ds->d_colbins);
@@ -572,6 +883,18 @@ extern "C" void rw_dataset_destroy(rw_dataset* ds) {
 
 extern "C" int rw_dataset_bins(const rw_dataset* ds, uint8_t* out) {
   if (!ds || !out) return fail(nullptr, RW_ERR_ARG, "NULL argument");
+  if (!ds->shards.empty()) {
+    // shard i holds columns [lo_i, lo_{i+1}) of every feature row of the [nf][n] matrix
+    for (size_t i = 0; i < ds->shards.size(); i++) {
+      const rw_dataset* sd = ds->shards[i];
+      rw_ctx* c = sd->ctx;
+      RW_CU(c, cudaSetDevice(c->device));
+      RW_CU(c, cudaMemcpy2DAsync(out + ds->shard_lo[i], ds->n, sd->d_colbins, sd->n_pad, sd->n,
+                                 sd->nf, cudaMemcpyDeviceToHost, c->stream));
+      RW_CU(c, cudaStreamSynchronize(c->stream));
+    }
+    return RW_OK;
+  }
   rw_ctx* ctx = ds->ctx;
   RW_CU(ctx, cudaSetDevice(ctx->device));
   RW_CU(ctx, cudaMemcpy2DAsync(out, ds->n, ds->d_colbins, ds->n_pad, ds->n, ds->nf,
@@ -583,10 +906,17 @@ extern "C" int rw_dataset_bins(const rw_dataset* ds, uint8_t* out) {
 // =================================================================================
 // training loop
 
+static int group_fit(rw_dataset* gd, const rw_train_params* p, float base_score, uint32_t* feat,
+                     float* thr, uint16_t* thr_bin, float* leafval, float* leafvar,
+                     float* fi_gain, float* fi_count, rw_profile* prof);
+
 extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float base_score,
                               uint32_t* feat, float* thr, uint16_t* thr_bin, float* leafval,
                               float* leafvar, float* fi_gain, float* fi_count, rw_profile* prof) {
   if (!ds) return fail(nullptr, RW_ERR_ARG, "dataset is NULL");
+  if (!ds->shards.empty())
+    return group_fit(ds, p, base_score, feat, thr, thr_bin, leafval, leafvar, fi_gain, fi_count,
+                     prof);
   rw_ctx* ctx = ds->ctx;
   int rc = check_params(ctx, p, ds->n_bins);
   if (rc) return rc;
@@ -625,7 +955,7 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
   WsBuf<long long> hb0, hb1, hf0, hf1;
   WsBuf<uint32_t> d_feat, maxbits;
   WsBuf<SplitRec> rec;
-  WsBuf<float> leafc;
+  WsBuf<long long> leafsum;  // [2][NL] per-leaf wide-fixed-point sums of g and h
   WsBuf<double> term;
   WsBuf<long long> mono_sums;
   WsBuf<int32_t> d_mono;
@@ -686,7 +1016,7 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
   RW_CU(ctx, kerr.get(ds, "kernel_err", 1));
   RW_CU(ctx, cudaMemsetAsync(kerr.p, 0, sizeof(int), s));
   RW_CU(ctx, rec.get(ds, "split_rec", nf));
-  RW_CU(ctx, leafc.get(ds, "leaf_cand", (size_t)nf * NL));
+  RW_CU(ctx, leafsum.get(ds, "leaf_sums", 2 * (size_t)NL));
   RW_CU(ctx, term.get(ds, "gain_terms", (size_t)nf * (NL / 2) * (nb - 1)));
   WsBuf<long long> prefix;
   RW_CU(ctx, prefix.get(ds, "leaf_prefix", (size_t)nf * (NL / 2) * nb * 2));
@@ -749,9 +1079,15 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
 
   for (uint32_t t = 0; t < T; t++) {
     uint32_t* mb = maxbits.p + 2 * (size_t)t;
+    // the previous tree's pred update runs in this round's gradient kernel
+    PrevTree prev = {};
+    if (t > 0) {
+      prev.leafval = d_leafval.p + (size_t)(t - 1) * NL;
+      prev.node = node.p;
+    }
     if (goss) {
       RW_CU(ctx, launch_grad(pred.p, ds->d_y, g.p, h.p, n, n_pad, logistic, 1, 0, ds->row_offset,
-                             0, mb, ncount[0], s, &nl));
+                             0, mb, ncount[0], prev, s, &nl));
       RW_CU(ctx, launch_goss_init(gst, goss_k, s, &nl));
       for (int pass = 0; pass < 4; pass++) {
         RW_CU(ctx, launch_goss_digit_hist(g.p, n, gst, pass, s, &nl));
@@ -766,13 +1102,14 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
     } else {
       RW_CU(ctx, launch_grad(pred.p, ds->d_y, g.p, h.p, n, n_pad, logistic, stride,
                              stride > 1 ? (uint64_t)t % stride : 0, ds->row_offset, 1, mb,
-                             ncount[0], s, &nl));
+                             ncount[0], prev, s, &nl));
     }
     if (peer)
       RW_CU(ctx, launch_peer_small(ps, mb, 2, 1, ++ctx->peer_epoch, kerr.p, s, &nl));
     else if (ctx->comm)
       RW_NC(ctx, ncclAllReduce(mb, mb, 2, ncclUint32, ncclMax, ctx->comm, s));
-    RW_CU(ctx, launch_quant(g.p, h.p, mb, n_pad, q.p, node.p, hbp[0], cell, ncount[0], s, &nl));
+    RW_CU(ctx, launch_quant(g.p, h.p, mb, n_pad, q.p, node.p, hbp[0], cell, leafsum.p, 2 * NL,
+                            ncount[0], s, &nl));
     pt.mark(RW_CAT_GRADIENTS);
 
     const uint32_t tree_seed = t * 2654435761u + 0x455A4B41u;  // src/booster.rs:351
@@ -838,13 +1175,13 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
       sl.monotone = any_mono ? d_mono.p : nullptr;
       sl.mono = any_mono ? mono_sums.p : nullptr;
       sl.term = term.p;
-      sl.prefix = prefix.p;
+      // prefixes only feed the next level's built-child choice
+      sl.prefix = subtract && d + 1 < D ? prefix.p : nullptr;
       sl.colsample = p->colsample;
       sl.tree_seed = tree_seed;
       sl.cuts = ds->d_cuts;
       sl.rec = rec.p;
       sl.last_level = d == D - 1;
-      sl.leafc = leafc.p;
       RW_CU(ctx, launch_split(sl, s, &nl));
       pt.mark(RW_CAT_SPLIT);
       const uint32_t n_children = 2u << d;
@@ -863,23 +1200,43 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
       al.lists.built_odd = rl_built.p;
       al.lists.subtract = subtract ? 1 : 0;
       al.final_level = d == D - 1;
-      al.leafc = leafc.p;
       al.n_leaves = NL;
-      al.pred = pred.p;
+      al.g = g.p;
+      al.h = h.p;
+      al.maxbits = mb;
+      al.n_rows = ds->n_global;
+      al.leafsum = leafsum.p;
       al.feat = d_feat.p;
       al.thr = d_thr.p;
       al.thr_bin = d_thr_bin.p;
       al.fi_gain = d_fi_gain.p;
       al.fi_count = d_fi_count.p;
       al.slot = t * D + d;
-      al.leafval = d_leafval.p;
-      al.leaf_base = t * NL;
       al.split_out = nullptr;
       al.hb_next = groups_next ? hb_next : nullptr;
       al.hb_next_words = (uint64_t)groups_next * cell;
       RW_CU(ctx, launch_apply(al, s, &nl));
       pt.mark(d == D - 1 ? RW_CAT_UPDATE_PRED : RW_CAT_APPLY);
     }
+    // every rank's leaf sums (exact integers: any order gives the same totals)
+    if (peer) {
+      RW_CU(ctx, launch_peer_small(ps, leafsum.p, 2 * NL, 0, ++ctx->peer_epoch, kerr.p, s, &nl));
+      pt.mark(RW_CAT_ALLREDUCE);
+    } else if (ctx->comm) {
+      RW_NC(ctx, ncclAllReduce(leafsum.p, leafsum.p, 2 * (size_t)NL, ncclInt64, ncclSum, ctx->comm,
+                               s));
+      pt.mark(RW_CAT_ALLREDUCE);
+    }
+    LeafValues lv;
+    lv.leafsum = leafsum.p;
+    lv.maxbits = mb;
+    lv.n_leaves = NL;
+    lv.n_rows = ds->n_global;
+    lv.lr = (double)p->learning_rate;
+    lv.lambda = (double)p->lambda;
+    lv.leafval = d_leafval.p + (size_t)t * NL;
+    RW_CU(ctx, launch_leafval(lv, s, &nl));
+    pt.mark(RW_CAT_UPDATE_PRED);
   }
   RW_CU(ctx, cudaEventRecord(ev1, s));
   rc = wait_stream(ctx);
@@ -928,6 +1285,75 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
   return RW_OK;
 }
 
+// The tree loop on every rank of a multi-GPU context at once (one host thread per GPU):
+// each rank fits its shard and exchanges the per-level histograms with the others, so
+// every rank ends with the same model, which rank 0 writes to the caller's buffers.
+static int group_fit(rw_dataset* gd, const rw_train_params* p, float base_score, uint32_t* feat,
+                     float* thr, uint16_t* thr_bin, float* leafval, float* leafvar,
+                     float* fi_gain, float* fi_count, rw_profile* prof) {
+  rw_ctx* front = gd->ctx;
+  int rc = check_params(front, p, gd->n_bins);
+  if (rc) return rc;
+  if (leafvar) return fail(front, RW_ERR_UNSUPPORTED, "leafvar output is not supported");
+  if (p->n_trees > 0 && (!feat || !thr || !leafval))
+    return fail(front, RW_ERR_ARG, "NULL model output");
+  if (!fi_gain || !fi_count) return fail(front, RW_ERR_ARG, "NULL feature-importance output");
+  const int W = (int)gd->shards.size();
+  const size_t K = (size_t)p->n_trees * p->depth, L = (size_t)p->n_trees << p->depth;
+  const size_t nf = gd->nf;
+  struct Out {
+    std::vector<uint32_t> feat;
+    std::vector<float> thr, leafval, fig, fic;
+    std::vector<uint16_t> tb;
+    rw_profile prof;
+  };
+  std::vector<Out> o(W);
+  for (auto& q : o) {
+    q.feat.resize(std::max<size_t>(K, 1));
+    q.thr.resize(std::max<size_t>(K, 1));
+    q.tb.resize(std::max<size_t>(K, 1));
+    q.leafval.resize(std::max<size_t>(L, 1));
+    q.fig.resize(nf);
+    q.fic.resize(nf);
+    memset(&q.prof, 0, sizeof q.prof);
+    q.prof.enable = prof ? prof->enable : 0;
+  }
+  rc = run_members(
+      front,
+      [&](int i) {
+        Out& q = o[i];
+        return rw_fit_dataset(gd->shards[i], p, base_score, q.feat.data(), q.thr.data(),
+                              q.tb.data(), q.leafval.data(), nullptr, q.fig.data(), q.fic.data(),
+                              &q.prof);
+      },
+      true);
+  if (rc) return rc;
+  // every split decision reads all-rank sums, so every rank holds the same model
+  for (int i = 1; i < W; i++)
+    if (memcmp(o[i].feat.data(), o[0].feat.data(), K * 4) ||
+        memcmp(o[i].thr.data(), o[0].thr.data(), K * 4) ||
+        memcmp(o[i].tb.data(), o[0].tb.data(), K * 2) ||
+        memcmp(o[i].leafval.data(), o[0].leafval.data(), L * 4) ||
+        memcmp(o[i].fig.data(), o[0].fig.data(), nf * 4) ||
+        memcmp(o[i].fic.data(), o[0].fic.data(), nf * 4))
+      return fail(front, RW_ERR_CUDA, "ranks produced different models");
+  if (K) {
+    memcpy(feat, o[0].feat.data(), K * 4);
+    memcpy(thr, o[0].thr.data(), K * 4);
+    if (thr_bin) memcpy(thr_bin, o[0].tb.data(), K * 2);
+    memcpy(leafval, o[0].leafval.data(), L * 4);
+  }
+  memcpy(fi_gain, o[0].fig.data(), nf * 4);
+  memcpy(fi_count, o[0].fic.data(), nf * 4);
+  if (prof) {
+    const int32_t en = prof->enable;
+    *prof = o[0].prof;
+    prof->enable = en;
+    for (int i = 1; i < W; i++) prof->total_ms = std::max(prof->total_ms, o[i].prof.total_ms);
+  }
+  return RW_OK;
+}
+
 extern "C" int rw_fit(rw_ctx* ctx, const rw_train_params* p, const float* x, const float* y,
                       uint64_t n, uint32_t nf, const float* cuts, float base_score,
                       uint32_t* feat, float* thr, uint16_t* thr_bin, float* leafval,
@@ -960,7 +1386,14 @@ static int model_check(rw_ctx* ctx, const rw_model* m, bool need_bins) {
   return RW_OK;
 }
 
+// Entry points that take device pointers or a device-resident model run on the first
+// GPU of a multi-GPU context.
+static rw_ctx* first_rank(rw_ctx* ctx) {
+  return ctx && !ctx->members.empty() ? ctx->members[0] : ctx;
+}
+
 extern "C" int rw_model_upload(rw_ctx* ctx, const rw_model* m, rw_dmodel** out) {
+  ctx = first_rank(ctx);
   if (!out) return fail(ctx, RW_ERR_ARG, "out is NULL");
   *out = nullptr;
   int rc = model_check(ctx, m, false);
@@ -1009,7 +1442,9 @@ extern "C" void rw_model_free(rw_dmodel* dm) {
 
 static int predict_device_common(rw_ctx* ctx, const rw_dmodel* dm, float* d_out, uint64_t n,
                                  float* kernel_ms, bool u8, const void* in, uint64_t ld) {
+  ctx = first_rank(ctx);
   if (!ctx || !dm || (n > 0 && (!in || !d_out))) return fail(ctx, RW_ERR_ARG, "NULL argument");
+  if (dm->ctx != ctx) return fail(ctx, RW_ERR_ARG, "the model was uploaded on another context");
   if (u8 && !dm->has_bins) return fail(ctx, RW_ERR_ARG, "model uploaded without thr_bin");
   if (u8 && ld < n) return fail(ctx, RW_ERR_ARG, "ld < n");
   RW_CU(ctx, cudaSetDevice(ctx->device));
@@ -1049,6 +1484,9 @@ extern "C" int rw_predict_f32_device(rw_ctx* ctx, const rw_dmodel* dm, const flo
   return predict_device_common(ctx, dm, d_out, n, kernel_ms, false, d_x, 0);
 }
 
+// Row ranges of a multi-GPU context's ranks for n rows (contiguous, in rank order).
+static uint64_t rank_lo(uint64_t n, int i, int W) { return n * (uint64_t)i / (uint64_t)W; }
+
 extern "C" int rw_predict_f32(rw_ctx* ctx, const rw_model* m, const float* x, uint64_t n,
                               uint32_t nf, float* out) {
   int rc = model_check(ctx, m, false);
@@ -1056,6 +1494,16 @@ extern "C" int rw_predict_f32(rw_ctx* ctx, const rw_model* m, const float* x, ui
   if (nf != m->n_features) return fail(ctx, RW_ERR_ARG, "nf differs from the model's n_features");
   if (n == 0) return RW_OK;
   if (!x || !out) return fail(ctx, RW_ERR_ARG, "NULL buffer");
+  if (!ctx->members.empty()) {  // row shards, one per GPU, no communication
+    const int W = (int)ctx->members.size();
+    return run_members(
+        ctx,
+        [&](int i) {
+          const uint64_t lo = rank_lo(n, i, W), rows = rank_lo(n, i + 1, W) - lo;
+          return rw_predict_f32(ctx->members[i], m, x + lo * nf, rows, nf, out + lo);
+        },
+        false);
+  }
   rw_dmodel* dm = nullptr;
   rc = rw_model_upload(ctx, m, &dm);
   if (rc) return rc;
@@ -1078,15 +1526,12 @@ extern "C" int rw_predict_f32(rw_ctx* ctx, const rw_model* m, const float* x, ui
   return rc;
 }
 
-extern "C" int rw_predict_u8(rw_ctx* ctx, const rw_model* m, const uint8_t* bins, uint64_t n,
-                             uint32_t nf, float* out) {
-  int rc = model_check(ctx, m, true);
-  if (rc) return rc;
-  if (nf != m->n_features) return fail(ctx, RW_ERR_ARG, "nf differs from the model's n_features");
+// n rows of feature-major u8 bins whose feature rows are `pitch` bytes apart.
+static int predict_u8_host(rw_ctx* ctx, const rw_model* m, const uint8_t* bins, uint64_t n,
+                           uint64_t pitch, uint32_t nf, float* out) {
   if (n == 0) return RW_OK;
-  if (!bins || !out) return fail(ctx, RW_ERR_ARG, "NULL buffer");
   rw_dmodel* dm = nullptr;
-  rc = rw_model_upload(ctx, m, &dm);
+  int rc = rw_model_upload(ctx, m, &dm);
   if (rc) return rc;
   const uint64_t ld = round_up(n, 16);
   DBuf<uint8_t> db;
@@ -1095,7 +1540,7 @@ extern "C" int rw_predict_u8(rw_ctx* ctx, const rw_model* m, const uint8_t* bins
   if (e == cudaSuccess) e = dout.alloc(n);
   if (e == cudaSuccess) e = cudaMemsetAsync(db.p, 0, (size_t)nf * ld, ctx->stream);
   if (e == cudaSuccess)
-    e = cudaMemcpy2DAsync(db.p, ld, bins, n, n, nf, cudaMemcpyHostToDevice, ctx->stream);
+    e = cudaMemcpy2DAsync(db.p, ld, bins, pitch, n, nf, cudaMemcpyHostToDevice, ctx->stream);
   if (e != cudaSuccess) {
     rw_model_free(dm);
     return cuda_fail(ctx, e, "predict upload");
@@ -1108,6 +1553,26 @@ extern "C" int rw_predict_u8(rw_ctx* ctx, const rw_model* m, const uint8_t* bins
   }
   rw_model_free(dm);
   return rc;
+}
+
+extern "C" int rw_predict_u8(rw_ctx* ctx, const rw_model* m, const uint8_t* bins, uint64_t n,
+                             uint32_t nf, float* out) {
+  int rc = model_check(ctx, m, true);
+  if (rc) return rc;
+  if (nf != m->n_features) return fail(ctx, RW_ERR_ARG, "nf differs from the model's n_features");
+  if (n == 0) return RW_OK;
+  if (!bins || !out) return fail(ctx, RW_ERR_ARG, "NULL buffer");
+  if (!ctx->members.empty()) {  // row shards, one per GPU, no communication
+    const int W = (int)ctx->members.size();
+    return run_members(
+        ctx,
+        [&](int i) {
+          const uint64_t lo = rank_lo(n, i, W), rows = rank_lo(n, i + 1, W) - lo;
+          return predict_u8_host(ctx->members[i], m, bins + lo, rows, n, nf, out + lo);
+        },
+        false);
+  }
+  return predict_u8_host(ctx, m, bins, n, n, nf, out);
 }
 
 // =================================================================================
@@ -1169,6 +1634,8 @@ extern "C" int rw_debug_level_hist(rw_dataset* ds, const int32_t* node, const fl
                                    const float* h, int32_t e_g, int32_t e_h, uint32_t groups,
                                    int32_t odd_only, int64_t* out) {
   if (!ds || !node || !g || !h || !out || groups == 0) return fail(nullptr, RW_ERR_ARG, "NULL argument");
+  if (!ds->shards.empty())
+    return fail(ds->ctx, RW_ERR_UNSUPPORTED, "a multi-GPU dataset has no single histogram hook");
   rw_ctx* ctx = ds->ctx;
   RW_CU(ctx, cudaSetDevice(ctx->device));
   const uint64_t n = ds->n, n_pad = ds->n_pad;
@@ -1251,8 +1718,163 @@ extern "C" int rw_debug_level_hist(rw_dataset* ds, const int32_t* node, const fl
   return RW_OK;
 }
 
+extern "C" int rw_debug_level_step(rw_dataset* ds, const rw_train_params* p,
+                                   const int32_t* node, const float* g, const float* h,
+                                   uint32_t n_nodes, uint32_t tree, double* gain_out,
+                                   uint32_t* bin_out, uint32_t* chosen) {
+  if (!ds || !node || !g || !h || !gain_out || !bin_out || !chosen)
+    return fail(nullptr, RW_ERR_ARG, "NULL argument");
+  if (!ds->shards.empty())
+    return fail(ds->ctx, RW_ERR_UNSUPPORTED, "a multi-GPU dataset has no single level hook");
+  rw_ctx* ctx = ds->ctx;
+  int rc = check_params(ctx, p, ds->n_bins);
+  if (rc) return rc;
+  if (n_nodes == 0 || (n_nodes & (n_nodes - 1)) || n_nodes > 2048)
+    return fail(ctx, RW_ERR_ARG, "n_nodes must be a power of two up to 2048");
+  RW_CU(ctx, cudaSetDevice(ctx->device));
+  const uint64_t n = ds->n, n_pad = ds->n_pad;
+  const uint32_t nf = ds->nf, nb = ds->n_bins;
+  // the round's maxima over the level's rows and their fixed-point scales (k_grad, k_quant)
+  uint32_t mbits[2] = {0u, 0u};
+  for (uint64_t i = 0; i < n; i++) {
+    if (node[i] < 0) continue;
+    if ((uint32_t)node[i] >= n_nodes) return fail(ctx, RW_ERR_ARG, "node beyond n_nodes");
+    uint32_t bg, bh;
+    const float ag = std::fabs(g[i]);
+    memcpy(&bg, &ag, 4);
+    memcpy(&bh, &h[i], 4);
+    mbits[0] = std::max(mbits[0], bg & 0x7fffffffu);
+    mbits[1] = std::max(mbits[1], bh & 0x7fffffffu);
+  }
+  const float sg = rw_pow2f(rw_qscale_exp(mbits[0])), sh = rw_pow2f(rw_qscale_exp(mbits[1]));
+  // the level's row list, grouped by node (a counting sort), entries (row, q(g), q(h), 0)
+  std::vector<int2> qv(n_pad, make_int2(0, 0));
+  std::vector<uint32_t> seg(n_nodes + 1, 0);
+  for (uint64_t i = 0; i < n; i++) {
+    if (node[i] < 0) continue;
+    const int32_t a = rw_quantize(g[i], sg), b = rw_quantize(h[i], sh);
+    if ((a | b) == 0) continue;
+    qv[i] = make_int2(a, b);
+    seg[node[i] + 1]++;
+  }
+  for (uint32_t k = 0; k < n_nodes; k++) seg[k + 1] += seg[k];
+  std::vector<int4> rows(std::max<uint32_t>(seg[n_nodes], 1), make_int4(0, 0, 0, 0));
+  {
+    std::vector<uint32_t> cur(seg.begin(), seg.end() - 1);
+    for (uint64_t i = 0; i < n; i++)
+      if (node[i] >= 0 && (qv[i].x | qv[i].y) != 0)
+        rows[cur[node[i]]++] = make_int4((int)i, qv[i].x, qv[i].y, 0);
+  }
+  std::vector<uint32_t> len(n_nodes);
+  for (uint32_t k = 0; k < n_nodes; k++) len[k] = seg[k + 1] - seg[k];
+  const size_t cell = (size_t)ds->ftiles * nb * 2 * kHistFeat;
+  std::vector<int32_t> mono(nf, 0);
+  bool any_mono = false;
+  for (uint32_t i = 0; i < std::min<uint32_t>(nf, p->monotone ? p->n_monotone : 0); i++) {
+    mono[i] = p->monotone[i];
+    any_mono |= mono[i] != 0;
+  }
+  DBuf<int2> dq;
+  DBuf<int4> drows;
+  DBuf<uint32_t> dlen, dmb;
+  DBuf<long long> dhb, dhf, dmono_sums;
+  DBuf<double> dterm;
+  DBuf<SplitRec> drec;
+  DBuf<int32_t> dmono;
+  RW_CU(ctx, dq.alloc(n_pad));
+  RW_CU(ctx, drows.alloc(rows.size()));
+  RW_CU(ctx, dlen.alloc(n_nodes));
+  RW_CU(ctx, dmb.alloc(2));
+  RW_CU(ctx, dhb.alloc((size_t)n_nodes * cell));
+  RW_CU(ctx, dhf.alloc((size_t)n_nodes * cell));
+  RW_CU(ctx, dterm.alloc((size_t)nf * n_nodes * (nb - 1)));
+  RW_CU(ctx, drec.alloc(nf));
+  RW_CU(ctx, cudaMemcpy(dq.p, qv.data(), n_pad * sizeof(int2), cudaMemcpyHostToDevice));
+  RW_CU(ctx, cudaMemcpy(drows.p, rows.data(), rows.size() * sizeof(int4), cudaMemcpyHostToDevice));
+  RW_CU(ctx, cudaMemcpy(dlen.p, len.data(), n_nodes * 4, cudaMemcpyHostToDevice));
+  RW_CU(ctx, cudaMemcpy(dmb.p, mbits, 8, cudaMemcpyHostToDevice));
+  RW_CU(ctx, cudaMemset(dhb.p, 0, (size_t)n_nodes * cell * 8));
+  if (any_mono) {
+    RW_CU(ctx, dmono.alloc(nf));
+    RW_CU(ctx, dmono_sums.alloc((size_t)nf * (nb - 1) * 4));
+    RW_CU(ctx, cudaMemcpy(dmono.p, mono.data(), nf * 4, cudaMemcpyHostToDevice));
+    RW_CU(ctx, cudaMemset(dmono_sums.p, 0, (size_t)nf * (nb - 1) * 4 * 8));
+  }
+  HistLaunch hl;
+  hl.rowbins = ds->d_rowbins;
+  hl.n_pad = n_pad;
+  hl.packed = ds->packed;
+  hl.err = nullptr;
+  hl.q = dq.p;
+  hl.entries = drows.p;
+  hl.pcount = dlen.p;
+  hl.glen = dlen.p;
+  hl.parents = n_nodes;
+  hl.pairs = 1;
+  hl.n_ident = 0;
+  hl.groups = n_nodes;
+  hl.nf = nf;
+  hl.nb = nb;
+  hl.out = dhb.p;
+  int nl = 0;
+  RW_CU(ctx, launch_hist(hl, ctx->stream, &nl));
+  SplitLaunch sl = {};
+  sl.hb = dhb.p;
+  sl.hp = nullptr;
+  sl.hf = dhf.p;
+  sl.n_nodes = n_nodes;
+  sl.nf = nf;
+  sl.nb = nb;
+  sl.mode = 0;
+  sl.maxbits = dmb.p;
+  sl.lambda = (double)p->lambda;
+  sl.min_child = (double)p->min_child_h;
+  sl.lr = (double)p->learning_rate;
+  sl.monotone = any_mono ? dmono.p : nullptr;
+  sl.mono = any_mono ? dmono_sums.p : nullptr;
+  sl.term = dterm.p;
+  sl.prefix = nullptr;
+  sl.colsample = p->colsample;
+  sl.tree_seed = tree * 2654435761u + 0x455A4B41u;  // src/booster.rs:351
+  sl.cuts = ds->d_cuts;
+  sl.rec = drec.p;
+  sl.last_level = 1;
+  RW_CU(ctx, launch_split(sl, ctx->stream, &nl));
+  RW_CU(ctx, cudaStreamSynchronize(ctx->stream));
+  ctx->launches += nl;
+  std::vector<SplitRec> rec(nf);
+  RW_CU(ctx, cudaMemcpy(rec.data(), drec.p, nf * sizeof(SplitRec), cudaMemcpyDeviceToHost));
+  // the cross-feature choice k_apply makes: highest gain, ties to the lowest feature,
+  // feature 0 bin 0 when no split is feasible
+  double best = -INFINITY;
+  uint32_t bf = 0xffffffffu;
+  for (uint32_t f = 0; f < nf; f++) {
+    gain_out[f] = rec[f].gain;
+    bin_out[f] = rec[f].bin;
+    if (rec[f].gain > best) {
+      best = rec[f].gain;
+      bf = f;
+    }
+  }
+  if (bf == 0xffffffffu) bf = 0;
+  chosen[0] = bf;
+  chosen[1] = best == -INFINITY ? 0u : rec[bf].bin;
+  return RW_OK;
+}
+
+extern "C" int rw_debug_binary_version(rw_ctx* ctx, int32_t* out) {
+  ctx = first_rank(ctx);
+  if (!ctx || !out) return fail(ctx, RW_ERR_ARG, "NULL argument");
+  RW_CU(ctx, cudaSetDevice(ctx->device));
+  int v = 0;
+  RW_CU(ctx, kernel_binary_version(&v));
+  *out = v;
+  return RW_OK;
+}
+
 extern "C" int rw_debug_expf(rw_ctx* ctx, const float* x, uint64_t n, float* out_rw,
                              float* out_cuda) {
+  ctx = first_rank(ctx);
   if (!ctx || !x || !out_rw || !out_cuda) return fail(ctx, RW_ERR_ARG, "NULL argument");
   RW_CU(ctx, cudaSetDevice(ctx->device));
   DBuf<float> dx, dr, dc;

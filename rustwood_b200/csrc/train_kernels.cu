@@ -25,6 +25,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <map>
 #include <mutex>
 #include <utility>
@@ -653,34 +654,17 @@ __global__ void __launch_bounds__(kBestThreads) k_best(SplitLaunch a) {
   }
   __syncthreads();
   const uint32_t bs = s_b;
-  if (!a.last_level) {
-    // Which child of each node the next level builds if this feature wins: the side with
-    // less hessian (ties: the right, odd child); its sibling is derived by subtraction.
-    // Any choice gives the same exact histograms; this one reads allreduced sums, so
-    // every rank makes the same choice.
-    if (a.choice && a.prefix)
-      for (uint32_t nd = threadIdx.x; nd < a.n_nodes; nd += kBestThreads) {
-        const longlong2* pr =
-            reinterpret_cast<const longlong2*>(a.prefix) + ((size_t)f * a.n_nodes + nd) * nb;
-        const long long hl = __ldcg(pr + bs).y, ht = __ldcg(pr + nb - 1).y;
-        a.choice[(size_t)f * a.n_nodes + nd] = (ht - hl) <= hl ? 1 : 0;
-      }
-    return;
-  }
-  // Last level: the leaf values this feature's best split would give (src/cpu.rs:286-318
-  // from the exact per-node prefix sums k_gain kept), one thread per node; k_apply keeps
-  // the winning feature's.
-  for (uint32_t nd = threadIdx.x; nd < a.n_nodes; nd += kBestThreads) {
-    const longlong2* pr = reinterpret_cast<const longlong2*>(a.prefix) + ((size_t)f * a.n_nodes + nd) * nb;
-    const longlong2 l = __ldcg(pr + bs), tt = __ldcg(pr + nb - 1);
-    const long long lg = l.x, lh = l.y, tg = tt.x, th = tt.y;
-    const long long rg = tg - lg, rh = th - lh;
-    const double lgd = (double)lg * inv_g, lhd = (double)lh * inv_h;
-    const double rgd = (double)rg * inv_g, rhd = (double)rh * inv_h;
-    float* out = a.leafc + (size_t)f * (2 * a.n_nodes);
-    out[2 * nd] = (float)(-a.lr * lgd / (lhd + lambda));
-    out[2 * nd + 1] = (float)(-a.lr * rgd / (rhd + lambda));
-  }
+  // Which child of each node the next level builds if this feature wins: the side with
+  // less hessian (ties: the right, odd child); its sibling is derived by subtraction.
+  // Any choice gives the same exact histograms; this one reads allreduced sums, so
+  // every rank makes the same choice.
+  if (!a.last_level && a.choice && a.prefix)
+    for (uint32_t nd = threadIdx.x; nd < a.n_nodes; nd += kBestThreads) {
+      const longlong2* pr =
+          reinterpret_cast<const longlong2*>(a.prefix) + ((size_t)f * a.n_nodes + nd) * nb;
+      const long long hl = __ldcg(pr + bs).y, ht = __ldcg(pr + nb - 1).y;
+      a.choice[(size_t)f * a.n_nodes + nd] = (ht - hl) <= hl ? 1 : 0;
+    }
 }
 
 // --------------------------------------------------------------------------------
@@ -792,35 +776,73 @@ __device__ void block_max2_atomic(uint32_t mg, uint32_t mh, uint32_t* maxbits) {
   }
 }
 
+// A tree's leaf values from its exact wide-fixed-point sums (src/cpu.rs:316-317:
+// (-lr * G / (H + lambda)) as f32), one thread per leaf.
+__global__ void k_leafval(LeafValues a) {
+  pdl_enter();
+  const int wg = rw_wscale_exp(__ldcg(a.maxbits), a.n_rows);
+  const int wh = rw_wscale_exp(__ldcg(a.maxbits + 1), a.n_rows);
+  for (uint32_t l = blockIdx.x * blockDim.x + threadIdx.x; l < a.n_leaves;
+       l += gridDim.x * blockDim.x) {
+    const double G = rw_wvalue(__ldcg(a.leafsum + l), wg);
+    const double H = rw_wvalue(__ldcg(a.leafsum + a.n_leaves + l), wh);
+    a.leafval[l] = (float)(-a.lr * G / (H + a.lambda));
+  }
+}
+
 // Gradients (src/cpu.rs:181-193), stride row sampling (src/cpu.rs:172-176, 202-204)
-// and the round's maxima over the sampled rows. Unsampled and padded rows
-// (n <= i < n_pad) get g = h = 0, which removes them from every histogram and leaf sum.
-__global__ void k_grad(const float* __restrict__ pred, const float* __restrict__ y,
+// and the round's maxima over the sampled rows, 4 rows per thread. Unsampled and padded
+// rows (n <= i < n_pad) get g = h = 0, which removes them from every histogram and leaf
+// sum. With a previous tree, every row first takes its leaf value:
+// pred += leafval[leaf] (src/cpu.rs:319-320), in f32 as the reference adds it.
+__global__ void k_grad(float* __restrict__ pred, const float* __restrict__ y,
                        float* __restrict__ g, float* __restrict__ h, uint64_t n, uint64_t n_pad,
                        int logistic, uint64_t stride, uint64_t phase, uint64_t row_offset,
-                       int compute_max, uint32_t* maxbits, uint32_t* zero_word) {
+                       int compute_max, uint32_t* maxbits, uint32_t* zero_word, PrevTree pt) {
   pdl_enter();
   if (zero_word && blockIdx.x == 0 && threadIdx.x == 0) *zero_word = 0u;
   uint32_t mg = 0, mh = 0;
-  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_pad;
-       i += (uint64_t)gridDim.x * blockDim.x) {
-    float gv = 0.0f, hv = 0.0f;
-    if (i < n) {
-      if (logistic) rw_logistic_grad(pred[i], y[i], &gv, &hv);
-      else {
-        gv = pred[i] - y[i];
-        hv = 1.0f;
+  const uint64_t n4 = n_pad / 4;
+  for (uint64_t qi = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; qi < n4;
+       qi += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t r = qi * 4;
+    float4 p4 = make_float4(0.f, 0.f, 0.f, 0.f), y4 = p4;
+    if (r < n) {
+      p4 = *reinterpret_cast<const float4*>(pred + r);
+      y4 = __ldg(reinterpret_cast<const float4*>(y + r));
+      if (pt.leafval) {
+        const uint2 nd = *reinterpret_cast<const uint2*>(pt.node + r);
+        p4.x = p4.x + __ldg(pt.leafval + (nd.x & 0x7fffu));
+        p4.y = p4.y + __ldg(pt.leafval + ((nd.x >> 16) & 0x7fffu));
+        p4.z = p4.z + __ldg(pt.leafval + (nd.y & 0x7fffu));
+        p4.w = p4.w + __ldg(pt.leafval + ((nd.y >> 16) & 0x7fffu));
+        *reinterpret_cast<float4*>(pred + r) = p4;  // rows past n are never read
       }
     }
-    const bool sampled = i < n && (stride <= 1 || ((row_offset + i) % stride) == phase);
-    if (!sampled) {
-      gv = 0.0f;
-      hv = 0.0f;
+    const float pv[4] = {p4.x, p4.y, p4.z, p4.w}, yv[4] = {y4.x, y4.y, y4.z, y4.w};
+    float gv[4], hv[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const uint64_t i = r + k;
+      gv[k] = 0.0f;
+      hv[k] = 0.0f;
+      if (i < n) {
+        if (logistic) rw_logistic_grad(pv[k], yv[k], &gv[k], &hv[k]);
+        else {
+          gv[k] = pv[k] - yv[k];
+          hv[k] = 1.0f;
+        }
+      }
+      const bool sampled = i < n && (stride <= 1 || ((row_offset + i) % stride) == phase);
+      if (!sampled) {
+        gv[k] = 0.0f;
+        hv[k] = 0.0f;
+      }
+      mg = max(mg, f32_bits_abs(gv[k]));
+      mh = max(mh, f32_bits_abs(hv[k]));
     }
-    g[i] = gv;
-    h[i] = hv;
-    mg = max(mg, f32_bits_abs(gv));
-    mh = max(mh, f32_bits_abs(hv));
+    *reinterpret_cast<float4*>(g + r) = make_float4(gv[0], gv[1], gv[2], gv[3]);
+    *reinterpret_cast<float4*>(h + r) = make_float4(hv[0], hv[1], hv[2], hv[3]);
   }
   if (compute_max) block_max2_atomic(mg, mh, maxbits);
 }
@@ -835,6 +857,7 @@ __global__ void k_quant(const float* __restrict__ g, const float* __restrict__ h
                         const uint32_t* __restrict__ maxbits, uint64_t n_pad,
                         int2* __restrict__ q, uint16_t* __restrict__ node,
                         long long* __restrict__ hb0, uint64_t hb0_words,
+                        long long* __restrict__ leafsum, uint32_t leafsum_words,
                         uint32_t* __restrict__ ncount0) {
   pdl_enter();
   __shared__ uint32_t s_rows;
@@ -846,6 +869,7 @@ __global__ void k_quant(const float* __restrict__ g, const float* __restrict__ h
   const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const uint64_t nthr = (uint64_t)gridDim.x * blockDim.x;
   for (uint64_t w = tid; w < hb0_words; w += nthr) hb0[w] = 0;
+  for (uint64_t w = tid; w < leafsum_words; w += nthr) leafsum[w] = 0;
   for (uint64_t i = tid; i < n_pad; i += nthr) {
     const int32_t a = rw_quantize(g[i], sg), b = rw_quantize(h[i], sh);
     q[i] = make_int2(a, b);
@@ -870,8 +894,11 @@ __global__ void k_quant(const float* __restrict__ g, const float* __restrict__ h
 // without, the left child's rows from the start and the right child's from the end.
 // Each chunk of rows ranks its rows per group in shared memory (warp-aggregated) and
 // reserves space with one global add per nonzero group; the entry carries the row's q.
-// The final level adds the tree's leaf value to pred (src/cpu.rs:319-320).
+// The final level adds every row's unquantised g and h, in the wide fixed point
+// (rw_wquantize), into its leaf's exact int64 sums (src/cpu.rs:286-318): per CTA in
+// shared memory for up to kLeafSmem leaves, then one global add per nonzero sum.
 constexpr int kApplyThreads = 256;
+constexpr uint32_t kLeafSmem = 1024;
 
 // The level's split from the per-feature records (every CTA), and by CTA 0 the model
 // slot and feature importance. Leaves (feature, bin) in s_ft.
@@ -914,22 +941,36 @@ __device__ void choose_split(const ApplyLaunch& a, uint32_t* s_ft, double* red_g
   __syncthreads();
 }
 
-__global__ void __launch_bounds__(kApplyThreads) k_apply(ApplyLaunch a) {
+// FINAL: the last level of a tree (leaf sums, no list); a separate instantiation keeps
+// the listing levels' register count (and so their occupancy) free of the leaf sums.
+template <bool FINAL>
+__global__ void __launch_bounds__(kApplyThreads, 8) k_apply(ApplyLaunch a) {
   pdl_enter();
-  extern __shared__ uint32_t lsm[];
+  extern __shared__ __align__(16) uint32_t lsm[];
   __shared__ double red_g[kApplyThreads / 32];
   __shared__ uint32_t red_i[kApplyThreads / 32];
   __shared__ uint32_t s_ft[2];
   __shared__ uint32_t warp_sums[33];
   const uint32_t lane = threadIdx.x & 31;
   const LevelLists& L = a.lists;
-  const bool listing = !a.final_level && L.entries;
+  const bool listing = !FINAL && L.entries;
   const uint32_t n_nodes = a.n_children / 2;
   const uint32_t G = L.subtract ? n_nodes : a.n_children;  // next-level groups
   uint32_t* s_cap = lsm;                   // [n_nodes + 1] prefix of the node row counts
   uint32_t* s_cnt = s_cap + n_nodes + 1;   // [G] this chunk's rows per group
   uint32_t* s_base = s_cnt + G;            // [G] their reservation in the group's region
   uint8_t* s_choice = reinterpret_cast<uint8_t*>(s_base + G);  // [n_nodes]
+  // final level: the CTA's leaf sums [2][n_leaves] (g, then h) when they fit
+  long long* s_ls = reinterpret_cast<long long*>(lsm);
+  const bool ls_smem = FINAL && a.n_leaves <= kLeafSmem;
+  int wg = 0, wh = 0;
+  if (FINAL) {
+    wg = rw_wscale_exp(__ldcg(a.maxbits), a.n_rows);
+    wh = rw_wscale_exp(__ldcg(a.maxbits + 1), a.n_rows);
+    if (ls_smem)
+      for (uint32_t l = threadIdx.x; l < 2 * a.n_leaves; l += blockDim.x) s_ls[l] = 0;
+  }
+  long long* ls = ls_smem ? s_ls : a.leafsum;
   if (listing)
     for (uint32_t g = threadIdx.x; g < G; g += blockDim.x) s_cnt[g] = 0u;
   if (a.hb_next) {
@@ -955,10 +996,6 @@ __global__ void __launch_bounds__(kApplyThreads) k_apply(ApplyLaunch a) {
       }
     __syncthreads();
   }
-  const float* lv = a.final_level ? a.leafc + (size_t)f * a.n_leaves : nullptr;
-  if (a.final_level && blockIdx.x == 0)
-    for (uint32_t l = threadIdx.x; l < a.n_leaves; l += blockDim.x)
-      a.leafval[a.leaf_base + l] = __ldcg(lv + l);
   const uint8_t* col = a.colbins + (size_t)f * a.n_pad;
   // block-uniform chunks of blockDim.x row quads (the list phases synchronise the CTA)
   for (uint64_t c0 = (uint64_t)blockIdx.x * blockDim.x; c0 < n4;
@@ -982,13 +1019,20 @@ __global__ void __launch_bounds__(kApplyThreads) k_apply(ApplyLaunch a) {
       nd2.x = (nds[0] & 0xffffu) | (nds[1] << 16);
       nd2.y = (nds[2] & 0xffffu) | (nds[3] << 16);
       *reinterpret_cast<uint2*>(a.node + r) = nd2;
-      if (a.final_level) {
-        float4 p4 = *reinterpret_cast<const float4*>(a.pred + r);
-        p4.x += __ldg(lv + (nds[0] & 0x7fffu));
-        p4.y += __ldg(lv + (nds[1] & 0x7fffu));
-        p4.z += __ldg(lv + (nds[2] & 0x7fffu));
-        p4.w += __ldg(lv + (nds[3] & 0x7fffu));
-        *reinterpret_cast<float4*>(a.pred + r) = p4;
+      if (FINAL) {
+        // every sampled row counts, including rows whose 17-bit q are both 0
+        const float4 g4 = __ldcg(reinterpret_cast<const float4*>(a.g + r));
+        const float4 h4 = __ldcg(reinterpret_cast<const float4*>(a.h + r));
+        const float gv[4] = {g4.x, g4.y, g4.z, g4.w}, hv[4] = {h4.x, h4.y, h4.z, h4.w};
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          const uint32_t leaf = nds[q] & 0x7fffu;
+          const long long qg = rw_wquantize(gv[q], wg), qh = rw_wquantize(hv[q], wh);
+          if (qg) atomicAdd(reinterpret_cast<unsigned long long*>(ls + leaf), (unsigned long long)qg);
+          if (qh)
+            atomicAdd(reinterpret_cast<unsigned long long*>(ls + a.n_leaves + leaf),
+                      (unsigned long long)qh);
+        }
       }
     }
     if (!listing) continue;
@@ -1039,6 +1083,13 @@ __global__ void __launch_bounds__(kApplyThreads) k_apply(ApplyLaunch a) {
       }
       const uint32_t row = (uint32_t)(qi * 4 + q);
       if (pos < a.n_pad) L.entries[pos] = make_int4((int)row, qv[q].x, qv[q].y, 0);
+    }
+  }
+  if (ls_smem) {
+    __syncthreads();
+    for (uint32_t l = threadIdx.x; l < 2 * a.n_leaves; l += blockDim.x) {
+      const long long v = s_ls[l];
+      if (v) atomicAdd(reinterpret_cast<unsigned long long*>(a.leafsum + l), (unsigned long long)v);
     }
   }
 }
@@ -1280,14 +1331,24 @@ cudaError_t launch_pack4(const uint8_t* d_u8, uint64_t n_pad, uint32_t nf, uint8
   return cudaGetLastError();
 }
 
-cudaError_t launch_grad(const float* pred, const float* y, float* g, float* h, uint64_t n,
+cudaError_t launch_grad(float* pred, const float* y, float* g, float* h, uint64_t n,
                         uint64_t n_pad, int logistic, uint64_t stride, uint64_t phase,
                         uint64_t row_offset, int compute_max, uint32_t* maxbits,
-                        uint32_t* zero_word, cudaStream_t s, int* nl) {
+                        uint32_t* zero_word, const PrevTree& prev, cudaStream_t s, int* nl) {
+  if ((n_pad & 3) != 0 || (prev.leafval && !prev.node)) return cudaErrorInvalidValue;
   RW_PREFER_SMEM(k_grad);
-  cudaError_t e = launch_pdl(k_grad, dim3(grid_for(n_pad, 256)), dim3(256), 0, s, pred, y, g, h, n,
-                             n_pad, logistic, stride, phase, row_offset, compute_max, maxbits,
-                             zero_word);
+  cudaError_t e = launch_pdl(k_grad, dim3(grid_for(n_pad / 4, 256)), dim3(256), 0, s, pred, y, g,
+                             h, n, n_pad, logistic, stride, phase, row_offset, compute_max,
+                             maxbits, zero_word, prev);
+  if (e != cudaSuccess) return e;
+  if (nl) (*nl)++;
+  return cudaGetLastError();
+}
+
+cudaError_t launch_leafval(const LeafValues& a, cudaStream_t s, int* nl) {
+  if (!a.leafsum || !a.leafval || !a.maxbits || a.n_leaves == 0) return cudaErrorInvalidValue;
+  const unsigned blocks = (a.n_leaves + 255) / 256;
+  cudaError_t e = launch_pdl(k_leafval, dim3(blocks), dim3(256), 0, s, a);
   if (e != cudaSuccess) return e;
   if (nl) (*nl)++;
   return cudaGetLastError();
@@ -1295,10 +1356,11 @@ cudaError_t launch_grad(const float* pred, const float* y, float* g, float* h, u
 
 cudaError_t launch_quant(const float* g, const float* h, const uint32_t* maxbits, uint64_t n_pad,
                          int2* q, uint16_t* node, long long* hb0, uint64_t hb0_words,
-                         uint32_t* ncount0, cudaStream_t s, int* nl) {
+                         long long* leafsum, uint32_t leafsum_words, uint32_t* ncount0,
+                         cudaStream_t s, int* nl) {
   RW_PREFER_SMEM(k_quant);
   cudaError_t e = launch_pdl(k_quant, dim3(grid_for(n_pad, 256)), dim3(256), 0, s, g, h, maxbits,
-                             n_pad, q, node, hb0, hb0_words, ncount0);
+                             n_pad, q, node, hb0, hb0_words, leafsum, leafsum_words, ncount0);
   if (e != cudaSuccess) return e;
   if (nl) (*nl)++;
   return cudaGetLastError();
@@ -1310,13 +1372,25 @@ cudaError_t launch_apply(const ApplyLaunch& a, cudaStream_t s, int* nl) {
   const uint32_t G = a.lists.subtract ? n_nodes : a.n_children;
   const bool listing = !a.final_level && a.lists.entries;
   if (listing && n_nodes > 4 * kApplyThreads) return cudaErrorInvalidValue;
-  const size_t smem = listing ? ((size_t)n_nodes + 1 + 2 * (size_t)G) * 4 + n_nodes : 0;
+  if (a.final_level && (!a.leafsum || !a.g || !a.h || !a.maxbits || a.n_leaves != a.n_children))
+    return cudaErrorInvalidValue;
+  const size_t smem = listing ? ((size_t)n_nodes + 1 + 2 * (size_t)G) * 4 + n_nodes
+                      : (a.final_level && a.n_leaves <= kLeafSmem) ? (size_t)a.n_leaves * 16
+                                                                   : 0;
   if (smem > 48 * 1024 &&
-      set_smem_and_occupancy(reinterpret_cast<const void*>(&k_apply), kApplyThreads, smem) < 1)
+      set_smem_and_occupancy(a.final_level ? reinterpret_cast<const void*>(&k_apply<true>)
+                                           : reinterpret_cast<const void*>(&k_apply<false>),
+                             kApplyThreads, smem) < 1)
     return cudaErrorInvalidConfiguration;
-  RW_PREFER_SMEM(k_apply);
-  cudaError_t e = launch_pdl(k_apply, dim3(grid_for(n4, kApplyThreads)), dim3(kApplyThreads), smem,
-                             s, a);
+  RW_PREFER_SMEM(k_apply<false>);
+  RW_PREFER_SMEM(k_apply<true>);
+  // The final level ends with every CTA adding its leaf sums into the global ones: two
+  // CTAs per SM keep those adds (2 x leaves per CTA onto the same words) few.
+  int grid = grid_for(n4, kApplyThreads);
+  if (a.final_level) grid = std::min(grid, 2 * sm_count());
+  cudaError_t e = a.final_level
+                      ? launch_pdl(k_apply<true>, dim3(grid), dim3(kApplyThreads), smem, s, a)
+                      : launch_pdl(k_apply<false>, dim3(grid), dim3(kApplyThreads), smem, s, a);
   if (e != cudaSuccess) return e;
   if (nl) (*nl)++;
   return cudaGetLastError();
@@ -1362,6 +1436,13 @@ cudaError_t launch_goss_apply(float* g, float* h, uint64_t n, uint64_t row_offse
   if (e != cudaSuccess) return e;
   if (nl) (*nl)++;
   return cudaGetLastError();
+}
+
+cudaError_t kernel_binary_version(int* out) {
+  cudaFuncAttributes fa;
+  cudaError_t e = cudaFuncGetAttributes(&fa, k_fill);
+  if (e == cudaSuccess) *out = fa.binaryVersion;
+  return e;
 }
 
 cudaError_t launch_debug_expf(const float* x, uint64_t n, float* out_rw, float* out_cuda,

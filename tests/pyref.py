@@ -5,7 +5,8 @@ booster.rs:582-601), written with plain Python loops so the C oracle can be chec
 against it bit-for-bit and golden fixtures can be generated from it. Both modes:
   exact=False: cpu.rs as written -- f32 chunked histograms combined by rayon's midpoint
                reduce tree, f64 gains and leaf sums, glibc expf;
-  exact=True:  the fixed-point variant the GPU implements (see rw_expf.h).
+  exact=True:  the fixed-point variant the GPU implements (see rw_expf.h): 17-bit
+               histogram values, leaf sums of the unquantised g/h in a wide fixed point.
 Only for n <= a few hundred rows: every operation is a Python-level scalar op.
 """
 from __future__ import annotations
@@ -74,6 +75,18 @@ def qscale_exp(m: np.float32) -> int:
 def quantize(x: np.float32, e: int) -> int:
     v = F32(x) * F32(2.0 ** e)
     return int(np.rint(v))
+
+
+def wscale_exp(m: np.float32, n_rows: int) -> int:
+    """Wide leaf-sum scale: (62 - bitlen(n)) - E with 2^(E-1) <= m < 2^E."""
+    if m == 0:
+        return 0
+    _, e = math.frexp(float(m))  # m = f * 2^e with 0.5 <= f < 1
+    return (62 - max(int(n_rows).bit_length(), 1)) - e
+
+
+def wquantize(x: np.float32, w: int) -> int:
+    return round(math.ldexp(float(x), w))  # exact product, round-half-even
 
 
 def partition_point(cuts, v) -> int:
@@ -162,6 +175,7 @@ def train(x, y, cuts, base, *, n_trees, depth, n_bins, learning_rate=0.1, lambda
             mg = max([abs(g[r]) for r in samp] + [F32(0)])
             mh = max([h[r] for r in samp] + [F32(0)])
             eg, eh = qscale_exp(mg), qscale_exp(mh)
+            wg, wh = wscale_exp(mg, n), wscale_exp(mh, n)
             qg = {r: quantize(g[r], eg) for r in samp}
             qh = {r: quantize(h[r], eh) for r in samp}
             inv_g, inv_h = 2.0 ** -eg, 2.0 ** -eh
@@ -257,12 +271,13 @@ def train(x, y, cuts, base, *, n_trees, depth, n_bins, learning_rate=0.1, lambda
                 node[r] = node[r] * 2 + (1 if bins[r][bf] > bb else 0)
             prev = hist
         if exact:
+            # exact integer sums of the unquantised g/h in the wide fixed point
             sg, sh = [0] * leaves, [0] * leaves
             for r in samp:
-                sg[node[r]] += qg[r]
-                sh[node[r]] += qh[r]
-            lg = [float(v) * inv_g for v in sg]
-            lc = [float(v) * inv_h for v in sh]
+                sg[node[r]] += wquantize(g[r], wg)
+                sh[node[r]] += wquantize(h[r], wh)
+            lg = [math.ldexp(float(v), -wg) for v in sg]
+            lc = [math.ldexp(float(v), -wh) for v in sh]
         else:
             m = len(samp)
             chunk = -(-m // n_threads)

@@ -13,7 +13,8 @@ torch.distributed backend so the protocol itself can be checked on CPU ranks (gl
   per level  local int64 histogram of the odd children (all nodes at level 0 or without
              subtraction), one all-reduce(sum) of it, even = parent - odd locally, then the
              same split scan on every rank (identical splits, nothing broadcast);
-  leaves     one all-reduce(sum) of the per-leaf integer sums.
+  leaves     one all-reduce(sum) of the per-leaf integer sums (wide fixed point of the
+             unquantised g/h, scaled by the global row count).
 
 Every all-reduce is of integers, so the model is bit-identical to the single-process
 exact trainer at any rank count (src/cpu.rs:123-325 with exact accumulation). Only
@@ -40,6 +41,19 @@ def qscale_exp(max_bits: int) -> int:
 def quantize(x: np.ndarray, e: int) -> np.ndarray:
     """round-half-even(f32(x) * f32(2^e)) as int64 (rw_quantize)."""
     return np.rint(x.astype(F32) * F32(2.0 ** e)).astype(np.int64)
+
+
+def wscale_exp(max_bits: int, n_rows: int) -> int:
+    """Wide leaf-sum exponent (62 - bitlen(n)) - E, 2^(E-1) <= max < 2^E (rw_wscale_exp)."""
+    if max_bits & 0x7FFFFFFF == 0:
+        return 0
+    biased = (max_bits >> 23) & 0xFF
+    return (62 - max(int(n_rows).bit_length(), 1)) - ((1 if biased == 0 else biased) - 126)
+
+
+def wquantize(x: np.ndarray, w: int) -> np.ndarray:
+    """round-half-even(f64(x) * 2^w) as int64 (rw_wquantize); the product is exact."""
+    return np.rint(x.astype(np.float64) * 2.0 ** w).astype(np.int64)
 
 
 def f32_bits(x: np.ndarray) -> np.ndarray:
@@ -154,6 +168,7 @@ def train_shard(bins, y, cuts, base, *, row_offset, n_global, n_trees, depth, n_
         qg = np.where(samp, quantize(g, eg), 0)
         qh = np.where(samp, quantize(h, eh), 0)
         inv_g, inv_h = 2.0 ** -eg, 2.0 ** -eh
+        wg, wh = wscale_exp(int(mx[0]), n_global), wscale_exp(int(mx[1]), n_global)
         node = np.zeros(n, np.int64)
         prev = None
         for level in range(depth):
@@ -201,11 +216,11 @@ def train_shard(bins, y, cuts, base, *, row_offset, n_global, n_trees, depth, n_
             prev = hist
         sg = np.zeros(leaves, np.int64)
         sh = np.zeros(leaves, np.int64)
-        np.add.at(sg, node[samp], qg[samp])
-        np.add.at(sh, node[samp], qh[samp])
+        np.add.at(sg, node[samp], wquantize(g[samp], wg))
+        np.add.at(sh, node[samp], wquantize(h[samp], wh))
         s = ex.sum(np.concatenate([sg, sh]))
-        lg = s[:leaves].astype(np.float64) * inv_g
-        lc = s[leaves:].astype(np.float64) * inv_h
+        lg = s[:leaves].astype(np.float64) * 2.0 ** -wg
+        lc = s[leaves:].astype(np.float64) * 2.0 ** -wh
         lv = (-lr * lg / (lc + lam)).astype(F32)
         leafval[t * leaves:(t + 1) * leaves] = lv
         pred = (pred + lv[node]).astype(F32)

@@ -233,13 +233,16 @@ def test_fit_vs_faithful_cpu_rs(ctx):
 
 
 def test_errors_are_reported(ctx):
-    cfg = rb.Config(n_trees=1, depth=13)
-    with pytest.raises(Exception):
-        rb.train_params(cfg)  # depth 13 accepted by the struct; rejected by the library below
-        x, y, _, _ = synth.c1(1000)
-        cuts = rb.compute_boundaries(x, 256)
-        ds = Dataset(ctx, x, y, cuts, 256)
+    # depth 13 passes the host mirror and the parameter struct; the library rejects it
+    cfg = rb.Config(n_trees=1, depth=13, n_bins=256)
+    rb.train_params(cfg)
+    x, y, _, _ = synth.c1(1000)
+    cuts = rb.compute_boundaries(x, 256)
+    ds = Dataset(ctx, x, y, cuts, 256)
+    with pytest.raises(N.RwError) as ei:
         fit_dataset(ds, cfg, 0.0)
+    assert ei.value.code == -1 and "depth" in str(ei.value)
+    ds.close()
     x, y, _, _ = synth.c1(1000)
     cuts = rb.compute_boundaries(x, 64)
     ds = Dataset(ctx, x, y, cuts, 64)

@@ -56,6 +56,23 @@ def test_noalloc_scores_match_rw_predict_f32_twice_in_a_row():
         want2 = _score(N.lib.rw_predict_f32, ctx, m2, x2)
         got2 = _score(N.lib.rw_predict_f32_noalloc, ctx, m2, x2)
         np.testing.assert_array_equal(got2.view(np.uint32), want2.view(np.uint32))
+        # the defining property: after the first call has loaded everything, further calls
+        # leave the device's free memory unchanged (nothing allocated, nothing freed)
+        free0 = torch.cuda.mem_get_info(0)[0]
+        for _ in range(3):
+            _score(N.lib.rw_predict_f32_noalloc, ctx, m1, x1)
+            _score(N.lib.rw_predict_f32_noalloc, ctx, m2, x2)
+        assert torch.cuda.mem_get_info(0)[0] == free0
+        # a model without trees scores base_score, as rw_predict_f32 does (also with no
+        # features)
+        for nf0 in (5, 0):
+            m0 = N.Model()
+            m0.n_trees, m0.depth, m0.n_features, m0.base_score = 0, 6, nf0, -0.75
+            x0 = np.zeros((1000, nf0), np.float32)
+            want0 = _score(N.lib.rw_predict_f32, ctx, m0, x0)
+            got0 = _score(N.lib.rw_predict_f32_noalloc, ctx, m0, x0)
+            np.testing.assert_array_equal(got0, want0)
+            assert (got0 == np.float32(-0.75)).all()
         # a model beyond the 4 MiB staging limit is rejected with a clear error
         m3, keep3 = _model(300, 12, 8, seed=9)
         with pytest.raises(N.RwError) as ei:
