@@ -124,6 +124,9 @@ const char* rw_last_error(const rw_ctx* ctx);
 void* rw_ctx_stream(const rw_ctx* ctx);
 /* Bound (milliseconds) on each collective wait; 0 = wait forever. Default 60000. */
 int rw_ctx_set_timeout(rw_ctx* ctx, int64_t ms);
+/* 1 when a wait on a peer rank expired on this context (its exchanges can no longer be
+ * trusted: later fits return an error; recreate the context), else 0. */
+int rw_ctx_peer_failed(const rw_ctx* ctx);
 
 /* ---- training ---------------------------------------------------------------- */
 
@@ -226,6 +229,18 @@ int rw_debug_level_hist(rw_dataset* ds, const int32_t* node, const float* g, con
 int rw_debug_level_step(rw_dataset* ds, const rw_train_params* p, const int32_t* node,
                         const float* g, const float* h, uint32_t n_nodes, uint32_t tree,
                         double* gain_out, uint32_t* bin_out, uint32_t* chosen);
+/* Failure detection without a fault: one one-shot peer exchange on this device whose
+ * rank 1 is a local region that nothing runs for, with each wait bounded by timeout_ms
+ * (1..10000). mode 0: rank 1 never signals (the wait expires: error word 2); 1: rank 1's
+ * signal carries its error bit (error word 3); 2: this rank's error word is already 2
+ * (the wait is skipped); 3: rank 1 signalled normally (error word 0). Out: the error
+ * word and the exchange kernel's time. */
+int rw_debug_peer_wait(rw_ctx* ctx, int32_t mode, int64_t timeout_ms, int32_t* err_out,
+                       float* kernel_ms);
+/* A context on gpu_id that is rank 0 of 2 with peer exchanges on, whose rank 1 never
+ * runs (its region is a local buffer), and whose waits expire after timeout_ms: every
+ * fit on it must return RW_ERR_TIMEOUT instead of waiting. */
+int rw_debug_lonely_rank_ctx(int gpu_id, int64_t timeout_ms, rw_ctx** out);
 /* The architecture the library's kernels run as on the context's device
  * (cudaFuncAttributes::binaryVersion: 100 for sm_100a code). */
 int rw_debug_binary_version(rw_ctx* ctx, int32_t* out);

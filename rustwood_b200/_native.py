@@ -94,6 +94,9 @@ def _load() -> C.CDLL:
         "rw_debug_expf": (i32, [vp, vp, u64, vp, vp]),
         "rw_debug_binary_version": (i32, [vp, P(i32)]),
         "rw_debug_level_step": (i32, [vp, P(TrainParams), vp, vp, vp, u32, u32, vp, vp, vp]),
+        "rw_debug_peer_wait": (i32, [vp, i32, C.c_int64, P(i32), P(f32)]),
+        "rw_debug_lonely_rank_ctx": (i32, [C.c_int, C.c_int64, P(vp)]),
+        "rw_ctx_peer_failed": (i32, [vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -110,6 +113,7 @@ EXPORTED = [
     "rw_predict_u8", "rw_model_upload", "rw_model_free", "rw_predict_u8_device",
     "rw_predict_f32_device", "rw_predict_f32_noalloc", "rw_compute_boundaries", "rw_base_score",
     "rw_debug_level_hist", "rw_debug_expf", "rw_debug_binary_version", "rw_debug_level_step",
+    "rw_debug_peer_wait", "rw_debug_lonely_rank_ctx", "rw_ctx_peer_failed",
 ]
 
 

@@ -67,6 +67,7 @@ struct rw_ctx {
   uint64_t peer_epoch = 0;   // exchanges issued on the region (identical on every rank)
   int peer_mode = -1;        // -1 undecided, 0 NCCL, 1 peer memory
   bool peer_failed = false;  // a bounded wait expired: the region's epochs are unusable
+  bool sym_peer_owned = false;  // test contexts: the peer regions are local allocations
   // in-process ranks: the shared group (each rank), or the ranks this context drives
   // (the context rw_ctx_create returned for several GPUs; it owns no stream itself)
   std::shared_ptr<RankGroup> group;

@@ -175,7 +175,8 @@ void sym_close(rw_ctx* ctx) {
   for (int r = 0; r < kMaxPeers; r++)
     if (ctx->sym_peer[r]) {
       // in-process ranks see each other's regions as plain device pointers (no handle)
-      if (!ctx->group) cudaIpcCloseMemHandle(ctx->sym_peer[r]);
+      if (ctx->sym_peer_owned) cudaFree(ctx->sym_peer[r]);
+      else if (!ctx->group) cudaIpcCloseMemHandle(ctx->sym_peer[r]);
       ctx->sym_peer[r] = nullptr;
     }
   if (ctx->sym) cudaFree(ctx->sym);
@@ -673,6 +674,13 @@ extern "C" void rw_ctx_destroy(rw_ctx* ctx) {
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
   if (ctx->pool) cudaMemPoolDestroy(ctx->pool);
   delete ctx;
+}
+
+extern "C" int rw_ctx_peer_failed(const rw_ctx* ctx) {
+  if (!ctx) return 0;
+  for (auto* c : ctx->members)
+    if (c->peer_failed) return 1;
+  return ctx->peer_failed ? 1 : 0;
 }
 
 extern "C" const char* rw_last_error(const rw_ctx* ctx) {
@@ -1859,6 +1867,99 @@ extern "C" int rw_debug_level_step(rw_dataset* ds, const rw_train_params* p,
   if (bf == 0xffffffffu) bf = 0;
   chosen[0] = bf;
   chosen[1] = best == -INFINITY ? 0u : rec[bf].bin;
+  return RW_OK;
+}
+
+// ---- failure detection on one GPU: a peer that never signals -----------------------
+
+// Two regions of the symmetric-region layout on this context's device: [0] plays this
+// rank (0), [1] a rank 1 that never runs.
+static int fake_peer_regions(rw_ctx* ctx, size_t bytes, char** r0, char** r1) {
+  *r0 = *r1 = nullptr;
+  RW_CU(ctx, cudaMalloc(reinterpret_cast<void**>(r0), bytes));
+  cudaError_t e = cudaMalloc(reinterpret_cast<void**>(r1), bytes);
+  if (e != cudaSuccess) {
+    cudaFree(*r0);
+    *r0 = nullptr;
+    return cuda_fail(ctx, e, "cudaMalloc");
+  }
+  RW_CU(ctx, cudaMemset(*r0, 0, bytes));
+  RW_CU(ctx, cudaMemset(*r1, 0, bytes));
+  return RW_OK;
+}
+
+extern "C" int rw_debug_peer_wait(rw_ctx* ctx, int32_t mode, int64_t timeout_ms,
+                                  int32_t* err_out, float* kernel_ms) {
+  ctx = first_rank(ctx);
+  if (!ctx || !err_out || !kernel_ms || mode < 0 || mode > 3 || timeout_ms < 1 ||
+      timeout_ms > 10000)
+    return fail(ctx, RW_ERR_ARG, "bad argument");
+  RW_CU(ctx, cudaSetDevice(ctx->device));
+  char *r0 = nullptr, *r1 = nullptr;
+  int rc = fake_peer_regions(ctx, kPeerDataOff + (1u << 20), &r0, &r1);
+  if (rc) return rc;
+  PeerSet ps = {};
+  ps.base[0] = r0;
+  ps.base[1] = r1;
+  ps.world = 2;
+  ps.rank = 0;
+  ps.timeout_ns = (uint64_t)timeout_ms * 1000000ull;
+  const uint64_t epoch = 1;
+  DBuf<int> err;
+  DBuf<unsigned long long> data;
+  cudaEvent_t a = nullptr, b = nullptr;
+  cudaError_t e = err.alloc(1);
+  if (e == cudaSuccess) e = data.alloc(16);
+  if (e == cudaSuccess) e = cudaMemset(data.p, 0, 16 * 8);
+  // mode 2: an earlier wait already expired on this rank
+  const int err0 = mode == 2 ? 2 : 0;
+  if (e == cudaSuccess) e = cudaMemcpy(err.p, &err0, 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && (mode == 1 || mode == 3)) {
+    // rank 1's signal in this rank's small word: the epoch, with its error bit (mode 1)
+    const uint64_t v = 2 * epoch + (mode == 1 ? 1u : 0u);
+    e = cudaMemcpy(r0 + sizeof(uint64_t), &v, 8, cudaMemcpyHostToDevice);
+  }
+  if (e == cudaSuccess) e = cudaEventCreate(&a);
+  if (e == cudaSuccess) e = cudaEventCreate(&b);
+  int nl = 0;
+  if (e == cudaSuccess) e = cudaEventRecord(a, ctx->stream);
+  if (e == cudaSuccess) e = launch_peer_small(ps, data.p, 16, 0, epoch, err.p, ctx->stream, &nl);
+  if (e == cudaSuccess) e = cudaEventRecord(b, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e == cudaSuccess) e = cudaEventElapsedTime(kernel_ms, a, b);
+  if (e == cudaSuccess) e = cudaMemcpy(err_out, err.p, 4, cudaMemcpyDeviceToHost);
+  if (a) cudaEventDestroy(a);
+  if (b) cudaEventDestroy(b);
+  cudaFree(r0);
+  cudaFree(r1);
+  ctx->launches += nl;
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "peer wait test");
+  return RW_OK;
+}
+
+extern "C" int rw_debug_lonely_rank_ctx(int gpu_id, int64_t timeout_ms, rw_ctx** out) {
+  if (!out || timeout_ms < 1 || timeout_ms > 10000) return fail(nullptr, RW_ERR_ARG, "bad argument");
+  *out = nullptr;
+  rw_ctx* ctx = nullptr;
+  int rc = rw_ctx_create_rank(gpu_id, 0, 1, nullptr, &ctx);
+  if (rc) return rc;
+  // rank 0 of 2 with peer exchanges on; rank 1's region is a local buffer nobody signals
+  const size_t bytes = 64u << 20;
+  char *r0 = nullptr, *r1 = nullptr;
+  rc = fake_peer_regions(ctx, bytes, &r0, &r1);
+  if (rc) {
+    std::string msg = ctx->last_error;
+    rw_ctx_destroy(ctx);
+    return fail(nullptr, rc, msg);
+  }
+  ctx->world = 2;
+  ctx->sym = r0;
+  ctx->sym_bytes = bytes;
+  ctx->sym_peer[1] = r1;
+  ctx->sym_peer_owned = true;
+  ctx->peer_mode = 1;
+  ctx->timeout_ms = timeout_ms;
+  *out = ctx;
   return RW_OK;
 }
 
