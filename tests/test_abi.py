@@ -88,3 +88,38 @@ def test_host_boundaries_and_base_score_match_oracle(seed, n, nf, nb, uniq):
     y = (rng.random(n) < 0.3).astype(np.float32)
     for obj in ("logistic", "l2"):
         assert np.float32(rb.base_score(y, obj)) == np.float32(oracle.base_score(y, obj))
+
+
+def _c_struct_fields(hdr, name):
+    body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (name, name), hdr, re.S).group(1)
+    body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+    fields = []
+    for decl in body.split(";"):
+        decl = decl.strip()
+        if not decl:
+            continue
+        # "uint32_t n_trees, depth" / "const float* thr" / "double category_ms[7]"
+        names = decl.split(None, 1)[1] if not decl.startswith("const") else decl.split(None, 2)[2]
+        for nm in names.split(","):
+            fields.append(re.sub(r"[\s*]|\[.*\]", "", nm))
+    return fields
+
+
+def _rust_struct_fields(src, name):
+    body = re.search(r"pub struct %s \{(.*?)\n\}" % name, src, re.S).group(1)
+    return re.findall(r"pub (\w+):", body)
+
+
+def test_rust_shim_binds_the_public_abi():
+    """The Rust binding (rustwood_b200/rust/gpu_ffi.rs, what rustwood links) declares every
+    public entry point of include/rwgpu.h, and its #[repr(C)] structs list the C fields in
+    the C order (cargo is not available here to compile it)."""
+    hdr = open(os.path.join(ROOT, "include", "rwgpu.h")).read()
+    src = open(os.path.join(ROOT, "rustwood_b200", "rust", "gpu_ffi.rs")).read()
+    public = [s for s in declared_symbols()
+              if not s.startswith("rw_debug_") and s not in ("rw_compute_boundaries",
+                                                              "rw_base_score")]
+    bound = set(re.findall(r"pub fn (rw_\w+)\(", src))
+    assert not [s for s in public if s not in bound], [s for s in public if s not in bound]
+    for c_name in ("rw_train_params", "rw_profile", "rw_model"):
+        assert _rust_struct_fields(src, c_name) == _c_struct_fields(hdr, c_name), c_name
