@@ -208,6 +208,12 @@ int rw_predict_f32_noalloc(rw_ctx* ctx, const rw_model* m, const float* x_rowmaj
 /* compute_boundaries (src/data.rs:86-146): out[nf*(n_bins-1)]. */
 void rw_compute_boundaries(const float* x_rowmajor, uint64_t n, uint32_t nf, uint32_t n_bins,
                            uint64_t sample, int32_t unique, float* out);
+/* The u8 scorer's bin-space thresholds of a model that carries only raw thresholds (a
+ * .rwood v1 file stores feat/thr/leafval, src/booster.rs:797-824): thr_bin[k] = the
+ * first b with cuts[feat[k]][b] == thr[k], given the cut table cuts[nf*(n_bins-1)] the
+ * model was trained with (bin > b <=> x > cuts[b] for every b holding that value).
+ * RW_ERR_ARG when a threshold is not a cut of its feature in this table. */
+int rw_model_thr_bins(const rw_model* m, const float* cuts, uint32_t n_bins, uint16_t* thr_bin);
 /* base_score (src/booster.rs:201-205 / 280-284). */
 float rw_base_score(const float* y, uint64_t n, int32_t objective);
 

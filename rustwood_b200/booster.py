@@ -264,6 +264,18 @@ class Booster:
         self.ctx.check(N.lib.rw_predict_u8(self.ctx.h, C.byref(m), N.ptr(b), n, nf, N.ptr(out)))
         return out
 
+    def set_cut_table(self, cuts: np.ndarray, n_bins: int | None = None) -> None:
+        """Recover the u8 scorer's thresholds (rw_model_thr_bins) of a model that carries
+        raw thresholds only, e.g. one read from a .rwood v1 file, from the cut table it was
+        trained with; predict_bins() then scores rows binned against that table."""
+        nb = self.cfg.n_bins if n_bins is None else n_bins
+        cuts = N.f32c(cuts)
+        m, _keep = self.model()
+        tb = np.zeros(len(self.feat), np.uint16)
+        N.check(N.lib.rw_model_thr_bins(C.byref(m), N.ptr(cuts), nb, N.ptr(tb)))
+        self.thr_bin = tb
+        self.cuts = cuts
+
     def feature_importance(self):
         return self.fi_gain, self.fi_count
 

@@ -1626,6 +1626,29 @@ extern "C" void rw_compute_boundaries(const float* x, uint64_t n, uint32_t nf, u
   }
 }
 
+extern "C" int rw_model_thr_bins(const rw_model* m, const float* cuts, uint32_t n_bins,
+                                 uint16_t* thr_bin) {
+  // A split tests x > thr with thr = cuts[f][b] (the trainer writes cut values,
+  // src/gpu_kernels.rs:966-967); with bin = #{cut < x}, bin > b <=> x > cuts[f][b] for
+  // every b holding that value, so the first such b serves the u8 scorer.
+  if (!m || !cuts || !thr_bin || n_bins < 2 || n_bins > 256)
+    return fail(nullptr, RW_ERR_ARG, "bad argument");
+  const size_t K = (size_t)m->n_trees * m->depth;
+  if (K && (!m->feat || !m->thr)) return fail(nullptr, RW_ERR_ARG, "NULL model array");
+  const uint32_t nb1 = n_bins - 1;
+  for (size_t k = 0; k < K; k++) {
+    if (m->feat[k] >= m->n_features) return fail(nullptr, RW_ERR_ARG, "feature index out of range");
+    const float* c = cuts + (size_t)m->feat[k] * nb1;
+    const float* it = std::lower_bound(c, c + nb1, m->thr[k]);
+    if (it == c + nb1 || !(*it == m->thr[k]))
+      return fail(nullptr, RW_ERR_ARG,
+                  "split " + std::to_string(k) + ": threshold is not a cut of feature " +
+                      std::to_string(m->feat[k]) + " in this table");
+    thr_bin[k] = (uint16_t)(it - c);
+  }
+  return RW_OK;
+}
+
 extern "C" float rw_base_score(const float* y, uint64_t n, int32_t objective) {
   // src/booster.rs:201-205: f32 sequential mean, clamped, logit for logistic.
   float s = 0.0f;

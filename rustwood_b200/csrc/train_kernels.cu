@@ -504,11 +504,13 @@ __global__ void __launch_bounds__(kGainThreads) k_gain(SplitLaunch a) {
 #pragma unroll
         for (int i = 0; i < 2 * (int)kGainCols; i++) x[i] = pp[i] - x[i];
     }
-    long long* o = a.hf + nd * node_words + cell;
-    reinterpret_cast<longlong2*>(o)[0] = make_longlong2(x[0], x[1]);
-    reinterpret_cast<longlong2*>(o)[1] = make_longlong2(x[2], x[3]);
-    reinterpret_cast<longlong2*>(o + kHistFeat)[0] = make_longlong2(x[4], x[5]);
-    reinterpret_cast<longlong2*>(o + kHistFeat)[1] = make_longlong2(x[6], x[7]);
+    if (!a.last_level) {  // the next level's parent histograms (the last level has none)
+      long long* o = a.hf + nd * node_words + cell;
+      reinterpret_cast<longlong2*>(o)[0] = make_longlong2(x[0], x[1]);
+      reinterpret_cast<longlong2*>(o)[1] = make_longlong2(x[2], x[3]);
+      reinterpret_cast<longlong2*>(o + kHistFeat)[0] = make_longlong2(x[4], x[5]);
+      reinterpret_cast<longlong2*>(o + kHistFeat)[1] = make_longlong2(x[6], x[7]);
+    }
   }
   // inclusive prefixes over bins (exact int64), 8 at once
   long long p[2 * kGainCols];

@@ -126,6 +126,8 @@ extern "C" {
                                  d_out: *mut f32, kernel_ms: *mut f32) -> c_int;
     pub fn rw_predict_f32_noalloc(ctx: *mut rw_ctx, m: *const rw_model, x_rowmajor: *const f32,
                                   n: u64, nf: u32, out: *mut f32) -> c_int;
+    pub fn rw_model_thr_bins(m: *const rw_model, cuts: *const f32, n_bins: u32,
+                             thr_bin: *mut u16) -> c_int;
 }
 
 fn check(ctx: *const rw_ctx, rc: c_int) -> Result<(), Box<dyn Error>> {
