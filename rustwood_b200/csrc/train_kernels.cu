@@ -45,6 +45,14 @@ __device__ __forceinline__ void pdl_enter() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
+// The same in two steps, for kernels that first load data no running grid writes: when
+// a kernel starts, the grid two launches back has completed (its successor let this one
+// launch only after waiting for it), so only the immediately preceding grid may still
+// be writing; loads of anything it does not write may precede the wait.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 constexpr int kHistThreads = 1024;
 // Rows one histogram CTA accumulates into its 32-bit shared cells before adding them to
@@ -381,9 +389,18 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(HistLaunch a, uint32_t ft
     __syncthreads();
     // the global cells of (grp, t) use the shared layout, so consecutive threads add
     // into consecutive int64 words
+    // The CTAs start their passes at different offsets (whole 1024-word steps, so the
+    // adds stay coalesced): at any moment they add into different words instead of all
+    // contending for the same ones in the L2.
     unsigned long long* gout =
         reinterpret_cast<unsigned long long*>(a.out + ((size_t)grp * ftiles + t) * words);
-    for (uint32_t c = threadIdx.x; c < words; c += kHistThreads) {
+    const uint32_t steps = (words + kHistThreads - 1) / kHistThreads;
+    const uint32_t rot = blockIdx.x % steps;
+    for (uint32_t k = 0; k < steps; k++) {
+      uint32_t st = k + rot;
+      st = st >= steps ? st - steps : st;
+      const uint32_t c = st * kHistThreads + threadIdx.x;
+      if (c >= words) continue;
       const uint32_t v = hs[c];
       if (v == 0u) continue;
       hs[c] = 0u;
@@ -455,7 +472,6 @@ __device__ __forceinline__ double q_inv_scale(uint32_t maxbits) {
 constexpr uint32_t kGainCols = 4;
 
 __global__ void __launch_bounds__(kGainThreads) k_gain(SplitLaunch a) {
-  pdl_enter();
   __shared__ long long wsum[kGainThreads / 32][2 * kGainCols];
   __shared__ long long tot[2 * kGainCols];
   const uint32_t nd = blockIdx.x;
@@ -472,37 +488,46 @@ __global__ void __launch_bounds__(kGainThreads) k_gain(SplitLaunch a) {
     fq[i] = t * kHistFeat + 2 * (c % 32) + c / 32;
     any |= fq[i] < nf;
   }
-  if (!any) return;  // uniform per CTA
+  if (!any) {  // uniform per CTA
+    pdl_wait();
+    pdl_trigger();
+    return;
+  }
   long long x[2 * kGainCols];  // g of the 4 columns, then h
 #pragma unroll
   for (int i = 0; i < 2 * (int)kGainCols; i++) x[i] = 0;
+  // 4 consecutive int64 columns (one 32-byte sector) for g and for h
+  auto load4 = [](const long long* src, long long* dst) {
+    const longlong2 u = __ldcg(reinterpret_cast<const longlong2*>(src));
+    const longlong2 v = __ldcg(reinterpret_cast<const longlong2*>(src + 2));
+    dst[0] = u.x;
+    dst[1] = u.y;
+    dst[2] = v.x;
+    dst[3] = v.y;
+  };
+  const size_t cell = ((size_t)t * nb + (b < nb ? b : 0)) * (2 * kHistFeat) + c0;
+  const size_t node_words = (size_t)ftiles * nb * 2 * kHistFeat;
+  const size_t k = (a.mode == 0 ? nd : (nd >> 1)) * node_words + cell;
+  // The parent level's histograms (the previous level's split scan) and the built-child
+  // flags (the previous leaf-index update) come from grids that have completed: load
+  // them while the histogram grid this kernel waits for finishes.
+  long long pp[2 * kGainCols];
+  bool built_here = true;
+  if (a.mode == 1 && b < nb) {
+    load4(a.hp + k, pp);
+    load4(a.hp + k + kHistFeat, pp + kGainCols);
+    built_here = (a.built_odd ? a.built_odd[nd >> 1] != 0 : true) == ((nd & 1u) != 0);
+  }
+  pdl_wait();
+  pdl_trigger();
   if (b < nb) {
-    const size_t cell = ((size_t)t * nb + b) * (2 * kHistFeat) + c0;  // within a node
-    const size_t node_words = (size_t)ftiles * nb * 2 * kHistFeat;
-    // 4 consecutive int64 columns (one 32-byte sector) for g and for h
-    auto load4 = [](const long long* src, long long* dst) {
-      const longlong2 u = __ldcg(reinterpret_cast<const longlong2*>(src));
-      const longlong2 v = __ldcg(reinterpret_cast<const longlong2*>(src + 2));
-      dst[0] = u.x;
-      dst[1] = u.y;
-      dst[2] = v.x;
-      dst[3] = v.y;
-    };
-    const size_t k = (a.mode == 0 ? nd : (nd >> 1)) * node_words + cell;
     load4(a.hb + k, x);
     load4(a.hb + k + kHistFeat, x + kGainCols);
-    if (a.mode == 1) {
+    if (a.mode == 1 && !built_here) {
       // the pair's built child is in hb (keyed by the parent); its sibling is
-      // parent - built. The parent's loads go out with the built child's (one round
-      // trip) and are dropped by the built child.
-      long long pp[2 * kGainCols];
-      load4(a.hp + k, pp);
-      load4(a.hp + k + kHistFeat, pp + kGainCols);
-      const bool built_here =
-          (a.built_odd ? a.built_odd[nd >> 1] != 0 : true) == ((nd & 1u) != 0);
-      if (!built_here)
+      // parent - built
 #pragma unroll
-        for (int i = 0; i < 2 * (int)kGainCols; i++) x[i] = pp[i] - x[i];
+      for (int i = 0; i < 2 * (int)kGainCols; i++) x[i] = pp[i] - x[i];
     }
     if (!a.last_level) {  // the next level's parent histograms (the last level has none)
       long long* o = a.hf + nd * node_words + cell;
@@ -947,7 +972,6 @@ __device__ void choose_split(const ApplyLaunch& a, uint32_t* s_ft, double* red_g
 // the listing levels' register count (and so their occupancy) free of the leaf sums.
 template <bool FINAL>
 __global__ void __launch_bounds__(kApplyThreads, 8) k_apply(ApplyLaunch a) {
-  pdl_enter();
   extern __shared__ __align__(16) uint32_t lsm[];
   __shared__ double red_g[kApplyThreads / 32];
   __shared__ uint32_t red_i[kApplyThreads / 32];
@@ -966,26 +990,30 @@ __global__ void __launch_bounds__(kApplyThreads, 8) k_apply(ApplyLaunch a) {
   long long* s_ls = reinterpret_cast<long long*>(lsm);
   const bool ls_smem = FINAL && a.n_leaves <= kLeafSmem;
   int wg = 0, wh = 0;
-  if (FINAL) {
-    wg = rw_wscale_exp(__ldcg(a.maxbits), a.n_rows);
-    wh = rw_wscale_exp(__ldcg(a.maxbits + 1), a.n_rows);
-    if (ls_smem)
-      for (uint32_t l = threadIdx.x; l < 2 * a.n_leaves; l += blockDim.x) s_ls[l] = 0;
-  }
+  if (FINAL && ls_smem)
+    for (uint32_t l = threadIdx.x; l < 2 * a.n_leaves; l += blockDim.x) s_ls[l] = 0;
   long long* ls = ls_smem ? s_ls : a.leafsum;
   if (listing)
     for (uint32_t g = threadIdx.x; g < G; g += blockDim.x) s_cnt[g] = 0u;
+  // Before the wait (the preceding grid is the split scan, which writes neither): the
+  // next level's built-histogram buffer is zeroed (the level before last used it and
+  // has completed) and the first chunk's leaf indices are loaded (the previous
+  // leaf-index update wrote them).
   if (a.hb_next) {
-    // zero the next level's built-histogram buffer, spread over the grid
     const uint64_t vec = a.hb_next_words / 2, stride = (uint64_t)gridDim.x * blockDim.x;
     for (uint64_t v = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; v < vec; v += stride)
       reinterpret_cast<longlong2*>(a.hb_next)[v] = make_longlong2(0, 0);
   }
   const uint64_t n4 = a.n_pad / 4;
-  // the first chunk's leaf indices do not depend on the split: load them first
   const uint64_t qi0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
   uint2 nd_first = make_uint2(0u, 0u);
   if (qi0 < n4) nd_first = *reinterpret_cast<const uint2*>(a.node + qi0 * 4);
+  pdl_wait();
+  pdl_trigger();
+  if (FINAL) {
+    wg = rw_wscale_exp(__ldcg(a.maxbits), a.n_rows);
+    wh = rw_wscale_exp(__ldcg(a.maxbits + 1), a.n_rows);
+  }
   choose_split(a, s_ft, red_g, red_i);
   const uint32_t f = s_ft[0], t = s_ft[1];
   if (listing) {
