@@ -61,6 +61,9 @@ def parse():
     ap.add_argument("--predict-rows", type=int, default=100_000_000)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-sweep", action="store_true", help="skip the scoring sweep")
+    ap.add_argument("--c4-rows", type=int, default=10_000_000,
+                    help="rows of the C4 multi-GPU line (0 skips it)")
+    ap.add_argument("--c4-trees", type=int, default=20)
     return ap.parse_args()
 
 
@@ -218,6 +221,73 @@ def run_reference(args):
     return 0
 
 
+C4_SHARDS = 8
+
+
+def c4_shard(rows, seed, device):
+    """One C4 shard on the GPU: x ~ N(0,1) [rows][100]; y = the sum of 10 fixed random
+    depth-3 step functions of x (drawn from numpy seed 1234, the same for every shard)
+    plus N(0, 0.1) noise, as rustwood_b200.synth.c4 defines the target."""
+    import torch
+    g = torch.Generator(device=device).manual_seed(1000 + seed)
+    x = torch.randn((rows, 100), generator=g, device=device, dtype=torch.float32)
+    rng = np.random.default_rng(1234)
+    y = torch.zeros(rows, device=device, dtype=torch.float32)
+    for _ in range(10):
+        fs = rng.integers(0, 100, size=3)
+        ts = rng.standard_normal(3).astype(np.float32) * 0.5
+        vals = torch.from_numpy(rng.standard_normal(8).astype(np.float32)).to(device)
+        idx = ((x[:, int(fs[0])] > float(ts[0])).long() * 4 + (x[:, int(fs[1])] > float(ts[1])).long() * 2
+               + (x[:, int(fs[2])] > float(ts[2])).long())
+        y += vals[idx]
+    y += torch.randn(rows, generator=g, device=device, dtype=torch.float32) * 0.1
+    return x, y
+
+
+def run_c4(args, ctx, rank, world, stream, flush_l2, barrier):
+    """The C4 line: this rank's shards on its GPU, the first c4_trees trees timed."""
+    import torch
+    import rustwood_b200 as rb
+    from rustwood_b200.booster import Dataset, fit_dataset
+    if C4_SHARDS % world:
+        return None
+    per = args.c4_rows // C4_SHARDS
+    mine = range(rank * C4_SHARDS // world, (rank + 1) * C4_SHARDS // world)
+    parts = [c4_shard(per, s, "cuda") for s in mine]
+    x = torch.cat([p[0] for p in parts])
+    y = torch.cat([p[1] for p in parts])
+    del parts
+    # the cut table of N(0,1) features from a fixed host sample (identical on every rank)
+    xs = np.random.default_rng(77).standard_normal((200_000, 100)).astype(np.float32)
+    cuts = rb.compute_boundaries(xs, 16)
+    n = x.shape[0]
+    cfg = rb.Config(n_trees=args.c4_trees, depth=8, n_bins=16, pack4=True, goss_top=0.2,
+                    goss_other=0.1, objective="l2", learning_rate=0.1)
+    base = float(y.mean().item())  # every rank: the mean of its own shard is not global;
+    if world > 1:                  # the global mean keeps the model identical at every N
+        import torch.distributed as dist
+        t = torch.tensor([float(y.sum().item())], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t)
+        base = float(np.float32(t.item() / (n * world)))
+    ds = Dataset.from_device(ctx, x.data_ptr(), y.data_ptr(), n, 100, cuts, 16, pack4=True,
+                             n_global=n * world, row_offset=n * rank)
+    del x, y
+    for _ in range(max(1, min(args.warmup, 2))):
+        fit_dataset(ds, cfg, base)
+    barrier()
+    steps = max(2, args.steps // 4)
+    ts = []
+    for i in range(steps):
+        flush_l2(i)
+        ts.append(fit_dataset(ds, cfg, base).profile.total_ms)
+    barrier()
+    ds.close()
+    return {"workload": "C4 first %d trees: %d rows x 100 N(0,1), 16 bins 4-bit, depth 8, "
+                        "GOSS 0.2/0.1, L2 (8 GPU-generated shards, seeds fixed)"
+                        % (args.c4_trees, args.c4_rows),
+            "rows_per_gpu": n, "steps": steps, "seconds": statistics.mean(ts) / 1e3}
+
+
 def run_ours(args):
     import torch
     rank, world, local = dist_env()
@@ -367,6 +437,14 @@ def run_ours(args):
         weak = {"rows_per_gpu": n_all, "global_rows": n_all * world,
                 "seconds_per_fit": statistics.mean(wt) / 1e3}
 
+    # ---- C4: 10M x 100, 16 bins 4-bit, depth 8, GOSS, L2 --------
+    # The configuration whose rows are meant to be sharded over 1/2/4/8 GPUs: the same
+    # dataset at every N (8 fixed shards generated on the GPU from seeds 0..7, rank r
+    # holding a contiguous run of them), the first c4_trees trees timed (strong scaling).
+    c4 = None
+    if args.c4_rows > 0:
+        c4 = run_c4(args, ctx, rank, world, stream, flush_l2, barrier)
+
     # ---- scoring (C5): device-resident u8 rows ----------------------------------------
     pred = None
     sweep = None
@@ -430,10 +508,13 @@ def run_ours(args):
     hist_gbs = hist_bytes / (hist_ms / 1e3) / 1e9 if hist_ms > 0 else 0.0
     pred_rps = pred["rows_per_s_per_gpu"] if pred else 0.0
     agg = max_over_ranks([v_s, e2e_pinned, e2e_pageable, -hist_gbs,
-                          weak["seconds_per_fit"] if weak else 0.0])
+                          weak["seconds_per_fit"] if weak else 0.0,
+                          c4["seconds"] if c4 else 0.0])
     v_s, e2e_pinned, e2e_pageable, hist_gbs_min = agg[0], agg[1], agg[2], -agg[3]
     if weak:
         weak["seconds_per_fit"] = agg[4]
+    if c4:
+        c4["seconds"] = agg[5]
     if world > 1:
         ps = torch.tensor([pred_rps], dtype=torch.float64, device="cuda")
         dist.all_reduce(ps, op=dist.ReduceOp.SUM)
@@ -499,6 +580,7 @@ def run_ours(args):
                     "d2h_bytes_per_step": int(d2h), "host_buffers": "pinned",
                     "pageable_value": e2e_pageable},
             "weak_scaling": weak,
+            "c4_strong": c4,
             "gpu_launches": launches,
             "predict": None if pred is None else dict(pred, rows_per_s_total=pred_total),
             "predict_sweep": sweep,
