@@ -64,6 +64,7 @@ def parse():
     ap.add_argument("--c4-rows", type=int, default=10_000_000,
                     help="rows of the C4 multi-GPU line (0 skips it)")
     ap.add_argument("--c4-trees", type=int, default=20)
+    ap.add_argument("--no-others", action="store_true", help="skip the C1/C3 lines")
     return ap.parse_args()
 
 
@@ -288,6 +289,48 @@ def run_c4(args, ctx, rank, world, stream, flush_l2, barrier):
             "rows_per_gpu": n, "steps": steps, "seconds": statistics.mean(ts) / 1e3}
 
 
+def run_other_configs(args, ctx, flush_l2, barrier):
+    """C1 (100k x 28, 200 trees, lr 0.2) and C3 (50k x 20, 13 target-encoded categorical
+    features, unique bins, monotone +1 on feature 0, 200 trees): the tree loop's device
+    time on one GPU, and beside it one fit of the faithful CPU restatement (oracle_ref)."""
+    import rustwood_b200 as rb
+    from rustwood_b200 import synth
+    from rustwood_b200.booster import Dataset, fit_dataset
+    out = {}
+    specs = {
+        "C1": (lambda: synth.c1(100_000, seed=0),
+               rb.Config(n_trees=200, depth=6, n_bins=255, learning_rate=0.2)),
+        "C3": (lambda: synth.c3(50_000, seed=0),
+               rb.Config(n_trees=200, depth=6, n_bins=255, categorical=list(range(7, 20)),
+                         unique_bins=True, monotone=[1])),
+    }
+    for name, (data, cfg) in specs.items():
+        x, y, _, _ = data()
+        b = rb.Booster(cfg, ctx)
+        xe, cuts, base = b.prepare(x, y)
+        ds = Dataset(ctx, xe, y, cuts, cfg.n_bins)
+        for _ in range(args.warmup):
+            fit_dataset(ds, cfg, base)
+        barrier()
+        ts = []
+        for i in range(args.steps):
+            flush_l2(i)
+            ts.append(fit_dataset(ds, cfg, base).profile.total_ms)
+        ds.close()
+        line = {"rows": int(len(y)), "features": int(xe.shape[1]), "trees": cfg.n_trees,
+                "gpu_seconds_per_fit": statistics.mean(ts) / 1e3}
+        if not args.no_cpu:
+            import oracle
+            nt = oracle.default_threads()
+            r = oracle.train(xe, y, cuts, base, n_trees=cfg.n_trees, depth=cfg.depth,
+                             n_bins=cfg.n_bins, learning_rate=cfg.learning_rate,
+                             monotone=cfg.monotone, exact=False, n_threads=nt)
+            line["cpu_seconds_per_fit"] = r.loop_seconds
+            line["cpu_threads"] = nt
+        out[name] = line
+    return out
+
+
 def run_ours(args):
     import torch
     rank, world, local = dist_env()
@@ -437,6 +480,11 @@ def run_ours(args):
         weak = {"rows_per_gpu": n_all, "global_rows": n_all * world,
                 "seconds_per_fit": statistics.mean(wt) / 1e3}
 
+    # ---- C1 and C3 (BASELINE configs[0] and [2]), one GPU -----------------------------
+    others = None
+    if world == 1 and not args.no_others:
+        others = run_other_configs(args, ctx, flush_l2, barrier)
+
     # ---- C4: 10M x 100, 16 bins 4-bit, depth 8, GOSS, L2 --------
     # The configuration whose rows are meant to be sharded over 1/2/4/8 GPUs: the same
     # dataset at every N (8 fixed shards generated on the GPU from seeds 0..7, rank r
@@ -581,6 +629,7 @@ def run_ours(args):
                     "pageable_value": e2e_pageable},
             "weak_scaling": weak,
             "c4_strong": c4,
+            "other_configs": others,
             "gpu_launches": launches,
             "predict": None if pred is None else dict(pred, rows_per_s_total=pred_total),
             "predict_sweep": sweep,

@@ -147,6 +147,23 @@ void rw_dataset_destroy(rw_dataset* ds);
 /* Copy the binned matrix out, feature-major [nf][n] u8 (unpacked). */
 int rw_dataset_bins(const rw_dataset* ds, uint8_t* out);
 
+/* compute_boundaries (src/data.rs:86-146) on the GPU for row-major x already in device
+ * memory (d_x [n][nf]): every max(n / sample, 1)-th row, per-feature sort, quantile cuts
+ * with the monotone fix or (unique != 0) distinct-value midpoints padded with +inf.
+ * out: host [nf*(n_bins-1)], bit-identical to rw_compute_boundaries on samples without
+ * NaN (whose order the reference leaves undefined). */
+int rw_compute_boundaries_device(rw_ctx* ctx, const float* d_x, uint64_t n, uint32_t nf,
+                                 uint32_t n_bins, uint64_t sample, int32_t unique, float* out);
+
+/* rw_fit with fit_inner's cut table computed on the GPU too (src/booster.rs:246-277:
+ * compute_boundaries then binning): x is uploaded once and serves both. sample/unique
+ * are Config's bin_sample and unique_bins; cuts_out (nullable) receives the table. */
+int rw_fit_with_boundaries(rw_ctx* ctx, const rw_train_params* p, const float* x_rowmajor,
+                           const float* y, uint64_t n, uint32_t nf, uint64_t sample,
+                           int32_t unique, float base_score, float* cuts_out, uint32_t* feat,
+                           float* thr, uint16_t* thr_bin, float* leafval, float* leafvar,
+                           float* fi_gain, float* fi_count, rw_profile* prof);
+
 /* The tree loop of fit_inner (src/booster.rs:349-513). Outputs (caller-allocated):
  * feat/thr/thr_bin [n_trees*depth], leafval [n_trees<<depth], fi_gain/fi_count [nf].
  * thr_bin, leafvar and prof may be NULL; leafvar must be NULL (pgbm unsupported). */

@@ -15,7 +15,8 @@ import sysconfig
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "librwgpu.so")
-SOURCES = ["rwgpu.cu", "train_kernels.cu", "predict_kernels.cu", "noalloc.cu", "peer_kernels.cu"]
+SOURCES = ["rwgpu.cu", "train_kernels.cu", "predict_kernels.cu", "noalloc.cu", "peer_kernels.cu",
+           "boundaries.cu"]
 HEADERS = ["rw_internal.cuh", "rw_expf.h", os.path.join("..", "..", "include", "rwgpu.h")]
 
 

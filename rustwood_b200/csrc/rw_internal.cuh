@@ -5,6 +5,7 @@
 #include <nccl.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <condition_variable>
 #include <functional>
 #include <map>
@@ -179,8 +180,9 @@ struct SplitLaunch {
   const int32_t* monotone;  // device [nf] or null
   long long* mono;      // with monotone: [nf][nb-1][4] exact left/right sums, zero on entry
   double* term;         // [nf][n_nodes][nb-1] per-node gain terms
-  long long* prefix;    // non-last levels with subtraction: [nf][n_nodes][nb][2] exact
-                        // per-node bin prefixes (g, h), for the built-child choice; or null
+  long long* prefix;    // non-last levels with subtraction: [nf][n_nodes][nb] exact
+                        // per-node hessian prefixes over bins, for the built-child choice;
+                        // or null
   float colsample;
   uint32_t tree_seed;
   const float* cuts;
@@ -316,6 +318,18 @@ cudaError_t launch_predict_f32(const float* x, uint64_t n, uint32_t nf, const rw
                                float* out, cudaStream_t s);
 cudaError_t launch_predict_u8(const uint8_t* bins, uint64_t n, uint64_t ld, const rw_dmodel& m,
                               float* out, cudaStream_t s);
+
+// ---- compute_boundaries on the GPU (boundaries.cu) ---------------------------------
+// The sample of n row-major rows (stride max(n / sample, 1)) and its cut table
+// d_out[nf][n_bins-1]; scratch3 holds 3 * nf * m words, m = the sampled row count
+// (returned in m_out; ceil(n / stride)).
+cudaError_t launch_boundaries(const float* d_x, uint64_t n, uint32_t nf, uint32_t n_bins,
+                              uint64_t sample, int unique, uint32_t* scratch3, float* d_out,
+                              cudaStream_t s, uint64_t* m_out);
+inline uint64_t boundary_sample_rows(uint64_t n, uint64_t sample) {
+  const uint64_t st = std::max<uint64_t>(n / std::max<uint64_t>(sample, 1), 1);
+  return (n - 1) / st + 1;
+}
 
 // ---- test hooks ------------------------------------------------------------------
 cudaError_t launch_debug_expf(const float* x, uint64_t n, float* out_rw, float* out_cuda,

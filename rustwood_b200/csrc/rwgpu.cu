@@ -1626,6 +1626,77 @@ extern "C" void rw_compute_boundaries(const float* x, uint64_t n, uint32_t nf, u
   }
 }
 
+extern "C" int rw_compute_boundaries_device(rw_ctx* ctx, const float* d_x, uint64_t n,
+                                            uint32_t nf, uint32_t n_bins, uint64_t sample,
+                                            int32_t unique, float* out) {
+  ctx = first_rank(ctx);
+  if (!ctx) return fail(nullptr, RW_ERR_ARG, "ctx is NULL");
+  if (!d_x || !out || n == 0 || nf == 0 || n_bins < 2 || n_bins > 256)
+    return fail(ctx, RW_ERR_ARG, "bad argument");
+  RW_CU(ctx, cudaSetDevice(ctx->device));
+  const uint64_t m = boundary_sample_rows(n, sample);
+  DBuf<uint32_t> scratch;
+  DBuf<float> dout;
+  RW_CU(ctx, scratch.alloc(ctx, 3 * (size_t)nf * m));
+  RW_CU(ctx, dout.alloc(ctx, (size_t)nf * (n_bins - 1)));
+  uint64_t mm = 0;
+  RW_CU(ctx, launch_boundaries(d_x, n, nf, n_bins, sample, unique, scratch.p, dout.p,
+                               ctx->stream, &mm));
+  ctx->launches += 3;
+  RW_CU(ctx, cudaMemcpyAsync(out, dout.p, (size_t)nf * (n_bins - 1) * 4, cudaMemcpyDeviceToHost,
+                             ctx->stream));
+  RW_CU(ctx, cudaStreamSynchronize(ctx->stream));
+  return RW_OK;
+}
+
+extern "C" int rw_fit_with_boundaries(rw_ctx* ctx, const rw_train_params* p, const float* x,
+                                      const float* y, uint64_t n, uint32_t nf, uint64_t sample,
+                                      int32_t unique, float base_score, float* cuts_out,
+                                      uint32_t* feat, float* thr, uint16_t* thr_bin,
+                                      float* leafval, float* leafvar, float* fi_gain,
+                                      float* fi_count, rw_profile* prof) {
+  if (!ctx) return fail(nullptr, RW_ERR_ARG, "ctx is NULL");
+  if (!p) return fail(ctx, RW_ERR_ARG, "params is NULL");
+  if (!x || !y || n == 0 || nf == 0) return fail(ctx, RW_ERR_ARG, "empty or NULL dataset");
+  if (p->n_bins < 2 || p->n_bins > 256) return fail(ctx, RW_ERR_ARG, "n_bins must be in 2..=256");
+  std::vector<float> cuts((size_t)nf * (p->n_bins - 1));
+  rw_ctx* c0 = first_rank(ctx);
+  RW_CU(c0, cudaSetDevice(c0->device));
+  if (ctx->members.empty()) {
+    // one upload of x serves the sample and the binning
+    DBuf<float> dx;
+    RW_CU(ctx, dx.alloc(ctx, (size_t)n * nf));
+    RW_CU(ctx, cudaMemcpyAsync(dx.p, x, (size_t)n * nf * 4, cudaMemcpyHostToDevice, ctx->stream));
+    int rc = rw_compute_boundaries_device(ctx, dx.p, n, nf, p->n_bins, sample, unique,
+                                          cuts.data());
+    if (rc) return rc;
+    rw_dataset* ds = nullptr;
+    rc = dataset_build(ctx, dx.p, y, false, n, nf, cuts.data(), p->n_bins, p->pack4, n, 0, &ds);
+    if (rc) return rc;
+    rc = rw_fit_dataset(ds, p, base_score, feat, thr, thr_bin, leafval, leafvar, fi_gain,
+                        fi_count, prof);
+    rw_dataset_destroy(ds);
+    if (!rc && cuts_out) memcpy(cuts_out, cuts.data(), cuts.size() * 4);
+    return rc;
+  }
+  // several GPUs: the sampled rows go to the first GPU for the cut table, then every
+  // rank uploads and bins its own shard against it
+  const uint64_t m = boundary_sample_rows(n, sample);
+  const uint64_t stride = std::max<uint64_t>(n / std::max<uint64_t>(sample, 1), 1);
+  std::vector<float> smp((size_t)m * nf);
+  for (uint64_t k = 0; k < m; k++) memcpy(&smp[k * nf], x + k * stride * nf, (size_t)nf * 4);
+  DBuf<float> ds_smp;
+  RW_CU(c0, ds_smp.alloc(c0, smp.size()));
+  RW_CU(c0, cudaMemcpyAsync(ds_smp.p, smp.data(), smp.size() * 4, cudaMemcpyHostToDevice,
+                            c0->stream));
+  int rc = rw_compute_boundaries_device(c0, ds_smp.p, m, nf, p->n_bins, m, unique, cuts.data());
+  if (rc) return fail(ctx, rc, c0->last_error);
+  rc = rw_fit(ctx, p, x, y, n, nf, cuts.data(), base_score, feat, thr, thr_bin, leafval, leafvar,
+              fi_gain, fi_count, prof);
+  if (!rc && cuts_out) memcpy(cuts_out, cuts.data(), cuts.size() * 4);
+  return rc;
+}
+
 extern "C" int rw_model_thr_bins(const rw_model* m, const float* cuts, uint32_t n_bins,
                                  uint16_t* thr_bin) {
   // A split tests x > thr with thr = cuts[f][b] (the trainer writes cut values,

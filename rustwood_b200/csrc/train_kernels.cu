@@ -471,71 +471,20 @@ __device__ __forceinline__ double q_inv_scale(uint32_t maxbits) {
 // and store is a whole-sector vector access.
 constexpr uint32_t kGainCols = 4;
 
-__global__ void __launch_bounds__(kGainThreads) k_gain(SplitLaunch a) {
-  __shared__ long long wsum[kGainThreads / 32][2 * kGainCols];
-  __shared__ long long tot[2 * kGainCols];
-  const uint32_t nd = blockIdx.x;
-  const uint32_t t = blockIdx.y / (kHistFeat / kGainCols);
-  const uint32_t c0 = (blockIdx.y % (kHistFeat / kGainCols)) * kGainCols;
+// One node of k_gain: this thread's bin b of the 4 columns (x: g of the 4, then h), the
+// node's full histogram for the next level, the exact prefixes over bins, and the gain
+// terms. All threads of the block call it (it synchronises).
+__device__ __forceinline__ void gain_node(const SplitLaunch& a, uint32_t nd, const long long* x,
+                                          const uint32_t* fq, size_t cell, size_t node_words,
+                                          long long (*wsum)[2 * kGainCols], long long* tot) {
   const uint32_t nf = a.nf, nb = a.nb, nsplit = nb - 1, b = threadIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const uint32_t ftiles = (nf + kHistFeat - 1) / kHistFeat;
-  uint32_t fq[kGainCols];
-  bool any = false;
-#pragma unroll
-  for (int i = 0; i < (int)kGainCols; i++) {
-    const uint32_t c = c0 + i;  // column -> feature: j -> 2j, 32 + j -> 2j + 1
-    fq[i] = t * kHistFeat + 2 * (c % 32) + c / 32;
-    any |= fq[i] < nf;
-  }
-  if (!any) {  // uniform per CTA
-    pdl_wait();
-    pdl_trigger();
-    return;
-  }
-  long long x[2 * kGainCols];  // g of the 4 columns, then h
-#pragma unroll
-  for (int i = 0; i < 2 * (int)kGainCols; i++) x[i] = 0;
-  // 4 consecutive int64 columns (one 32-byte sector) for g and for h
-  auto load4 = [](const long long* src, long long* dst) {
-    const longlong2 u = __ldcg(reinterpret_cast<const longlong2*>(src));
-    const longlong2 v = __ldcg(reinterpret_cast<const longlong2*>(src + 2));
-    dst[0] = u.x;
-    dst[1] = u.y;
-    dst[2] = v.x;
-    dst[3] = v.y;
-  };
-  const size_t cell = ((size_t)t * nb + (b < nb ? b : 0)) * (2 * kHistFeat) + c0;
-  const size_t node_words = (size_t)ftiles * nb * 2 * kHistFeat;
-  const size_t k = (a.mode == 0 ? nd : (nd >> 1)) * node_words + cell;
-  // The parent level's histograms (the previous level's split scan) and the built-child
-  // flags (the previous leaf-index update) come from grids that have completed: load
-  // them while the histogram grid this kernel waits for finishes.
-  long long pp[2 * kGainCols];
-  bool built_here = true;
-  if (a.mode == 1 && b < nb) {
-    load4(a.hp + k, pp);
-    load4(a.hp + k + kHistFeat, pp + kGainCols);
-    built_here = (a.built_odd ? a.built_odd[nd >> 1] != 0 : true) == ((nd & 1u) != 0);
-  }
-  pdl_wait();
-  pdl_trigger();
-  if (b < nb) {
-    load4(a.hb + k, x);
-    load4(a.hb + k + kHistFeat, x + kGainCols);
-    if (a.mode == 1 && !built_here) {
-      // the pair's built child is in hb (keyed by the parent); its sibling is
-      // parent - built
-#pragma unroll
-      for (int i = 0; i < 2 * (int)kGainCols; i++) x[i] = pp[i] - x[i];
-    }
-    if (!a.last_level) {  // the next level's parent histograms (the last level has none)
-      long long* o = a.hf + nd * node_words + cell;
-      reinterpret_cast<longlong2*>(o)[0] = make_longlong2(x[0], x[1]);
-      reinterpret_cast<longlong2*>(o)[1] = make_longlong2(x[2], x[3]);
-      reinterpret_cast<longlong2*>(o + kHistFeat)[0] = make_longlong2(x[4], x[5]);
-      reinterpret_cast<longlong2*>(o + kHistFeat)[1] = make_longlong2(x[6], x[7]);
-    }
+  if (!a.last_level && b < nb) {  // the next level's parent histograms
+    long long* o = a.hf + nd * node_words + cell;
+    reinterpret_cast<longlong2*>(o)[0] = make_longlong2(x[0], x[1]);
+    reinterpret_cast<longlong2*>(o)[1] = make_longlong2(x[2], x[3]);
+    reinterpret_cast<longlong2*>(o + kHistFeat)[0] = make_longlong2(x[4], x[5]);
+    reinterpret_cast<longlong2*>(o + kHistFeat)[1] = make_longlong2(x[6], x[7]);
   }
   // inclusive prefixes over bins (exact int64), 8 at once
   long long p[2 * kGainCols];
@@ -565,14 +514,18 @@ __global__ void __launch_bounds__(kGainThreads) k_gain(SplitLaunch a) {
   __syncthreads();
 #pragma unroll
   for (int i = 0; i < 2 * (int)kGainCols; i++) p[i] += wsum[warp][i];
+  long long tg_[kGainCols], th_[kGainCols];
+#pragma unroll
+  for (int i = 0; i < (int)kGainCols; i++) {
+    tg_[i] = tot[i];
+    th_[i] = tot[kGainCols + i];
+  }
+  __syncthreads();  // wsum and tot are free for the next node
   if (a.prefix && b < nb) {
-    // prefixes for k_best: the next level's built-child choice and, at the last level,
-    // the leaf values of whichever threshold it picks
+    // the hessian prefixes k_best reads for the next level's built-child choice
 #pragma unroll
     for (int i = 0; i < (int)kGainCols; i++)
-      if (fq[i] < nf)
-        reinterpret_cast<longlong2*>(a.prefix)[((size_t)fq[i] * a.n_nodes + nd) * nb + b] =
-            make_longlong2(p[i], p[kGainCols + i]);
+      if (fq[i] < nf) a.prefix[((size_t)fq[i] * a.n_nodes + nd) * nb + b] = p[kGainCols + i];
   }
   if (b >= nsplit) return;
   const double inv_g = q_inv_scale(a.maxbits[0]), inv_h = q_inv_scale(a.maxbits[1]);
@@ -582,7 +535,7 @@ __global__ void __launch_bounds__(kGainThreads) k_gain(SplitLaunch a) {
     const uint32_t f = fq[i];
     if (f >= nf) continue;
     const long long pgi = p[i], phi = p[kGainCols + i];
-    const long long tg = tot[i], th = tot[kGainCols + i];
+    const long long tg = tg_[i], th = th_[i];
     const double gt = (double)tg * inv_g, ht = (double)th * inv_h;
     const double parent = gt * gt / (ht + lambda);
     const double gl = (double)pgi * inv_g, hl = (double)phi * inv_h;
@@ -608,6 +561,71 @@ __global__ void __launch_bounds__(kGainThreads) k_gain(SplitLaunch a) {
       atomicAdd(m + 3, (unsigned long long)(th - phi));
     }
   }
+}
+
+// One CTA per (node, 4-column sector); with subtraction the node's histogram is its
+// pair's built child (hb, keyed by the parent) or the sibling parent - built. Thread b
+// owns bin b of the 4 features in those columns; a 32-byte sector of the layout holds
+// exactly 4 columns, so every load and store is a whole-sector vector access. (One CTA
+// per node pair, loading the pair once for both children, measured slower: half the
+// CTAs, each twice as long.)
+__global__ void __launch_bounds__(kGainThreads) k_gain(SplitLaunch a) {
+  __shared__ long long wsum[kGainThreads / 32][2 * kGainCols];
+  __shared__ long long tot[2 * kGainCols];
+  const uint32_t nd = blockIdx.x;
+  const uint32_t t = blockIdx.y / (kHistFeat / kGainCols);
+  const uint32_t c0 = (blockIdx.y % (kHistFeat / kGainCols)) * kGainCols;
+  const uint32_t nf = a.nf, nb = a.nb, b = threadIdx.x;
+  const uint32_t ftiles = (nf + kHistFeat - 1) / kHistFeat;
+  uint32_t fq[kGainCols];
+  bool any = false;
+#pragma unroll
+  for (int i = 0; i < (int)kGainCols; i++) {
+    const uint32_t c = c0 + i;  // column -> feature: j -> 2j, 32 + j -> 2j + 1
+    fq[i] = t * kHistFeat + 2 * (c % 32) + c / 32;
+    any |= fq[i] < nf;
+  }
+  if (!any) {  // uniform per CTA
+    pdl_wait();
+    pdl_trigger();
+    return;
+  }
+  // 4 consecutive int64 columns (one 32-byte sector) for g and for h
+  auto load4 = [](const long long* src, long long* dst) {
+    const longlong2 u = __ldcg(reinterpret_cast<const longlong2*>(src));
+    const longlong2 v = __ldcg(reinterpret_cast<const longlong2*>(src + 2));
+    dst[0] = u.x;
+    dst[1] = u.y;
+    dst[2] = v.x;
+    dst[3] = v.y;
+  };
+  const size_t cell = ((size_t)t * nb + (b < nb ? b : 0)) * (2 * kHistFeat) + c0;
+  const size_t node_words = (size_t)ftiles * nb * 2 * kHistFeat;
+  const size_t k = (size_t)(a.mode == 0 ? nd : (nd >> 1)) * node_words + cell;
+  // The parent level's histograms (the previous level's split scan) and the built-child
+  // flag (the previous leaf-index update) come from grids that have completed: load
+  // them while the histogram grid this kernel waits for finishes.
+  long long pp[2 * kGainCols], x[2 * kGainCols];
+#pragma unroll
+  for (int i = 0; i < 2 * (int)kGainCols; i++) pp[i] = x[i] = 0;
+  bool built_here = true;
+  if (a.mode == 1) {
+    if (b < nb) {
+      load4(a.hp + k, pp);
+      load4(a.hp + k + kHistFeat, pp + kGainCols);
+    }
+    built_here = (a.built_odd ? a.built_odd[nd >> 1] != 0 : true) == ((nd & 1u) != 0);
+  }
+  pdl_wait();
+  pdl_trigger();
+  if (b < nb) {
+    load4(a.hb + k, x);
+    load4(a.hb + k + kHistFeat, x + kGainCols);
+    if (!built_here)
+#pragma unroll
+      for (int i = 0; i < 2 * (int)kGainCols; i++) x[i] = pp[i] - x[i];
+  }
+  gain_node(a, nd, x, fq, cell, node_words, wsum, tot);
 }
 
 __global__ void __launch_bounds__(kBestThreads) k_best(SplitLaunch a) {
@@ -687,9 +705,8 @@ __global__ void __launch_bounds__(kBestThreads) k_best(SplitLaunch a) {
   // every rank makes the same choice.
   if (!a.last_level && a.choice && a.prefix)
     for (uint32_t nd = threadIdx.x; nd < a.n_nodes; nd += kBestThreads) {
-      const longlong2* pr =
-          reinterpret_cast<const longlong2*>(a.prefix) + ((size_t)f * a.n_nodes + nd) * nb;
-      const long long hl = __ldcg(pr + bs).y, ht = __ldcg(pr + nb - 1).y;
+      const long long* pr = a.prefix + ((size_t)f * a.n_nodes + nd) * nb;
+      const long long hl = __ldcg(pr + bs), ht = __ldcg(pr + nb - 1);
       a.choice[(size_t)f * a.n_nodes + nd] = (ht - hl) <= hl ? 1 : 0;
     }
 }

@@ -128,6 +128,15 @@ extern "C" {
                                   n: u64, nf: u32, out: *mut f32) -> c_int;
     pub fn rw_model_thr_bins(m: *const rw_model, cuts: *const f32, n_bins: u32,
                              thr_bin: *mut u16) -> c_int;
+    pub fn rw_compute_boundaries_device(ctx: *mut rw_ctx, d_x: *const f32, n: u64, nf: u32,
+                                        n_bins: u32, sample: u64, unique: i32,
+                                        out: *mut f32) -> c_int;
+    pub fn rw_fit_with_boundaries(ctx: *mut rw_ctx, p: *const rw_train_params,
+                                  x_rowmajor: *const f32, y: *const f32, n: u64, nf: u32,
+                                  sample: u64, unique: i32, base_score: f32, cuts_out: *mut f32,
+                                  feat: *mut u32, thr: *mut f32, thr_bin: *mut u16,
+                                  leafval: *mut f32, leafvar: *mut f32, fi_gain: *mut f32,
+                                  fi_count: *mut f32, prof: *mut rw_profile) -> c_int;
 }
 
 fn check(ctx: *const rw_ctx, rc: c_int) -> Result<(), Box<dyn Error>> {
