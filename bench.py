@@ -421,12 +421,17 @@ def run_ours(args):
     p = train_params(cfg)
     cuts_c = np.ascontiguousarray(cuts, np.float32)
 
+    cuts_gpu = np.empty_like(cuts_c)
+
     def e2e_fit(xh, yh):
         if world == 1:
-            ctx.check(N.lib.rw_fit(ctx.h, C.byref(p), C.c_void_p(xh), C.c_void_p(yh), n, nf,
-                                   N.ptr(cuts_c), float(base),
-                                   *(N.ptr(out[k]) for k in ("feat", "thr", "thr_bin", "leafval")),
-                                   None, N.ptr(out["fi_gain"]), N.ptr(out["fi_count"]), None))
+            # fit_inner's whole GPU path: upload, cut table (compute_boundaries) and
+            # binning on the GPU from the one upload, the tree loop, the model download
+            ctx.check(N.lib.rw_fit_with_boundaries(
+                ctx.h, C.byref(p), C.c_void_p(xh), C.c_void_p(yh), n, nf, cfg.bin_sample, 0,
+                float(base), N.ptr(cuts_gpu),
+                *(N.ptr(out[k]) for k in ("feat", "thr", "thr_bin", "leafval")),
+                None, N.ptr(out["fi_gain"]), N.ptr(out["fi_count"]), None))
         else:
             h = C.c_void_p()
             ctx.check(N.lib.rw_dataset_create(ctx.h, C.c_void_p(xh), C.c_void_p(yh), n, nf,
@@ -456,8 +461,10 @@ def run_ours(args):
     e2e_pinned = time_e2e(xp.data_ptr(), yp.data_ptr())
     del xp, yp
     e2e_pageable = time_e2e(x.ctypes.data, y.ctypes.data)
-    h2d = x.nbytes + y.nbytes + cuts_c.nbytes
-    d2h = sum(v.nbytes for v in out.values())
+    if world == 1:  # the GPU cut table is the host one (bit-exact)
+        assert np.array_equal(cuts_gpu.view(np.uint32), cuts_c.view(np.uint32))
+    h2d = x.nbytes + y.nbytes + (0 if world == 1 else cuts_c.nbytes)
+    d2h = sum(v.nbytes for v in out.values()) + (cuts_gpu.nbytes if world == 1 else 0)
 
     # ---- weak scaling (N > 1): 1M rows per GPU, one dataset of N x 1M rows -----------
     weak = None
@@ -626,7 +633,12 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_pinned, "unit": "s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h), "host_buffers": "pinned",
-                    "pageable_value": e2e_pageable},
+                    "pageable_value": e2e_pageable,
+                    "includes": "H2D of x and y, the cut table (compute_boundaries) and "
+                                "binning on the GPU, the 200-tree loop, the model D2H"
+                                if world == 1 else
+                                "H2D of x and y, binning on the GPU, the 200-tree loop, the "
+                                "model D2H (cut table from the host)"},
             "weak_scaling": weak,
             "c4_strong": c4,
             "other_configs": others,

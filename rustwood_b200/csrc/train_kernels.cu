@@ -196,6 +196,74 @@ __device__ void block_exclusive_scan(const uint32_t* in, uint32_t n, uint32_t* o
   __syncthreads();
 }
 
+// Exclusive prefixes of two arrays at once: in_k[0..n_k) (n_k <= 4 * blockDim.x, global,
+// written by an earlier kernel) into out_k[0..n_k], out_k[n_k] = the total. Both arrays'
+// loads are issued together and share the block barriers. warp_sums has 66 words. All
+// threads of the block call it.
+__device__ void block_exclusive_scan2(const uint32_t* in0, uint32_t n0, uint32_t* out0,
+                                      const uint32_t* in1, uint32_t n1, uint32_t* out1,
+                                      uint32_t* warp_sums) {
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x / 32;
+  const uint32_t per0 = (n0 + blockDim.x - 1) / blockDim.x, per1 = (n1 + blockDim.x - 1) / blockDim.x;
+  const uint32_t b0 = threadIdx.x * per0, b1 = threadIdx.x * per1;
+  uint32_t v0[4], v1[4], sum0 = 0, sum1 = 0;
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    v0[k] = (k < (int)per0 && b0 + k < n0) ? __ldcg(in0 + b0 + k) : 0u;
+    v1[k] = (k < (int)per1 && b1 + k < n1) ? __ldcg(in1 + b1 + k) : 0u;
+  }
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    sum0 += v0[k];
+    sum1 += v1[k];
+  }
+  uint32_t incl0 = sum0, incl1 = sum1;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const uint32_t y0 = __shfl_up_sync(0xffffffffu, incl0, d);
+    const uint32_t y1 = __shfl_up_sync(0xffffffffu, incl1, d);
+    if (lane >= (uint32_t)d) {
+      incl0 += y0;
+      incl1 += y1;
+    }
+  }
+  if (lane == 31) {
+    warp_sums[warp] = incl0;
+    warp_sums[33 + warp] = incl1;
+  }
+  __syncthreads();
+  if (warp < 2) {
+    uint32_t* ws_arr = warp_sums + 33 * warp;
+    const uint32_t ws = lane < nw ? ws_arr[lane] : 0u;
+    uint32_t wi = ws;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, wi, d);
+      if (lane >= (uint32_t)d) wi += y;
+    }
+    if (lane < nw) ws_arr[lane] = wi - ws;  // exclusive warp offsets
+    if (lane == nw - 1) ws_arr[32] = wi;    // block total
+  }
+  __syncthreads();
+  uint32_t run0 = warp_sums[warp] + incl0 - sum0, run1 = warp_sums[33 + warp] + incl1 - sum1;
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    if (k < (int)per0 && b0 + k < n0) {
+      out0[b0 + k] = run0;
+      run0 += v0[k];
+    }
+    if (k < (int)per1 && b1 + k < n1) {
+      out1[b1 + k] = run1;
+      run1 += v1[k];
+    }
+  }
+  if (threadIdx.x == 0) {
+    out0[n0] = warp_sums[32];
+    out1[n1] = warp_sums[65];
+  }
+  __syncthreads();
+}
+
 // Histogram of one level over a row list (or all rows), exact in fixed point.
 //
 // Row bins are tile-major: tile t's row r is the kHistFeat-byte (u8) or kHistFeat/2-byte
@@ -214,13 +282,15 @@ __device__ void block_exclusive_scan(const uint32_t* in, uint32_t n, uint32_t* o
 // 32+j feature 2j+1 -- and cleared.
 template <bool PACKED>
 __global__ void __launch_bounds__(kHistThreads) k_hist(HistLaunch a, uint32_t ftiles) {
-  pdl_enter();
   extern __shared__ __align__(16) uint32_t hs[];
   __shared__ __align__(8) uint64_t bar[kStreamStages];
   __shared__ int s_abort;
   constexpr uint32_t TB = PACKED ? kHistFeat / 2 : kHistFeat;  // tile bytes per row
-  __shared__ uint32_t warp_sums[33];
+  __shared__ uint32_t warp_sums[66];
   const uint32_t nb = a.nb, words = nb * 2 * kHistFeat;
+  // the cells are cleared while the preceding grid still runs (shared memory only)
+  for (uint32_t c = threadIdx.x; c < words; c += kHistThreads) hs[c] = 0u;
+  pdl_enter();
   unsigned char* stage0 = reinterpret_cast<unsigned char*>(hs + words + 2 * kHistFeat);
   // list segments: lpre = prefix of the group lengths (list index -> group), start = each
   // group's first entry in `entries` (from the prefix of the parents' row counts)
@@ -228,14 +298,15 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(HistLaunch a, uint32_t ft
   uint32_t* s_start = s_lpre + a.groups + 1;
   uint32_t* s_cap = s_start + a.groups;
   if (a.entries) {
-    block_exclusive_scan(a.pcount, a.parents, s_cap, warp_sums);
-    block_exclusive_scan(a.glen, a.groups, s_lpre, warp_sums);
+    block_exclusive_scan2(a.pcount, a.parents, s_cap, a.glen, a.groups, s_lpre, warp_sums);
     for (uint32_t g = threadIdx.x; g < a.groups; g += kHistThreads) {
       if (a.pairs) {
         s_start[g] = s_cap[g];
       } else {
+        // the second child's run starts after the first child's rows of the parent
         const uint32_t k = g >> 1;
-        s_start[g] = s_cap[k] + ((g & 1u) ? __ldcg(a.pcount + k) - __ldcg(a.glen + g) : 0u);
+        s_start[g] = s_cap[k] + ((g & 1u) ? (s_cap[k + 1] - s_cap[k]) - (s_lpre[g + 1] - s_lpre[g])
+                                          : 0u);
       }
     }
     __syncthreads();
@@ -250,7 +321,6 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(HistLaunch a, uint32_t ft
   if (w >= w_end) return;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   constexpr uint32_t kStageBytes = kStreamRows * (TB + 8);
-  for (uint32_t c = threadIdx.x; c < words; c += kHistThreads) hs[c] = 0u;
   if (threadIdx.x == 0) {
     s_abort = 0;
     if (!a.entries) {
@@ -394,17 +464,25 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(HistLaunch a, uint32_t ft
     // contending for the same ones in the L2.
     unsigned long long* gout =
         reinterpret_cast<unsigned long long*>(a.out + ((size_t)grp * ftiles + t) * words);
+    // Eight cells per thread are read before their adds are issued, so the pass is not
+    // one shared-memory round trip per cell.
     const uint32_t steps = (words + kHistThreads - 1) / kHistThreads;
     const uint32_t rot = blockIdx.x % steps;
-    for (uint32_t k = 0; k < steps; k++) {
-      uint32_t st = k + rot;
-      st = st >= steps ? st - steps : st;
-      const uint32_t c = st * kHistThreads + threadIdx.x;
-      if (c >= words) continue;
-      const uint32_t v = hs[c];
-      if (v == 0u) continue;
-      hs[c] = 0u;
-      atomicAdd(gout + c, (unsigned long long)(long long)(int32_t)v);
+    for (uint32_t k0 = 0; k0 < steps; k0 += 8) {
+      uint32_t c[8], v[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        uint32_t st = k0 + u + rot;
+        st = st >= steps ? st - steps : st;
+        c[u] = st * kHistThreads + threadIdx.x;
+        v[u] = (k0 + u < steps && c[u] < words) ? hs[c[u]] : 0u;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; u++)
+        if (v[u] != 0u) {
+          hs[c[u]] = 0u;
+          atomicAdd(gout + c[u], (unsigned long long)(long long)(int32_t)v[u]);
+        }
     }
     w += i1 - i0;
   }
