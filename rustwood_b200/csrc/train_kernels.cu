@@ -313,13 +313,51 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(HistLaunch a, uint32_t ft
   }
   const uint32_t L = a.entries ? s_lpre[a.groups] : a.n_ident;
   const uint64_t total = (uint64_t)L * ftiles;
-  // identity slices are whole stages (n_ident is a multiple of kStreamRows)
-  uint64_t per = (total + gridDim.x - 1) / gridDim.x;
-  if (!a.entries) per = (per + kStreamRows - 1) / kStreamRows * kStreamRows;
-  uint64_t w = (uint64_t)blockIdx.x * per;
-  const uint64_t w_end = min(total, w + per);
-  if (w >= w_end) return;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint64_t w, w_end;
+  const uint32_t units = a.entries ? ftiles * a.groups : 0u;  // (tile, group) units
+  if (units != 0 && units <= 32 && units * 4 <= gridDim.x) {
+    // Few units: each nonempty unit u gets its own CTAs, 1 + floor(len_u * (grid -
+    // units) / total) of them (at most the grid in all), which split it evenly. No CTA
+    // straddles two units, so every CTA flushes once; a CTA's share is within
+    // total / (grid - units) rows.
+    __shared__ unsigned long long s_range[2];
+    if (warp == 0) {
+      uint32_t c = 0;
+      uint64_t u_start = 0, u_len = 0;
+      if ((uint32_t)lane < units) {
+        const uint32_t t = (uint32_t)lane / a.groups, g = (uint32_t)lane % a.groups;
+        u_len = s_lpre[g + 1] - s_lpre[g];
+        u_start = (uint64_t)t * L + s_lpre[g];
+        c = u_len ? (uint32_t)(u_len * (gridDim.x - units) / total) + 1u : 0u;
+      }
+      uint32_t incl = c;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += y;
+      }
+      const uint32_t first = incl - c;
+      if (lane == 0) s_range[0] = s_range[1] = 0;
+      __syncwarp();
+      if (blockIdx.x >= first && blockIdx.x < incl) {  // at most one lane
+        const uint32_t k = blockIdx.x - first;
+        s_range[0] = u_start + u_len * k / c;
+        s_range[1] = u_start + u_len * (k + 1) / c;
+      }
+    }
+    __syncthreads();
+    w = s_range[0];
+    w_end = s_range[1];
+  } else {
+    // contiguous slices of the work space; identity slices are whole stages (n_ident is
+    // a multiple of kStreamRows)
+    uint64_t per = (total + gridDim.x - 1) / gridDim.x;
+    if (!a.entries) per = (per + kStreamRows - 1) / kStreamRows * kStreamRows;
+    w = (uint64_t)blockIdx.x * per;
+    w_end = min(total, w + per);
+  }
+  if (w >= w_end) return;
   constexpr uint32_t kStageBytes = kStreamRows * (TB + 8);
   if (threadIdx.x == 0) {
     s_abort = 0;
