@@ -152,20 +152,17 @@ __device__ __forceinline__ void hist_add_row(uint32_t* hs, uint32_t bb, int2 qq,
   atomicAdd(&hs[c1 + kHistFeat], (uint32_t)qq.y);
 }
 
-// Exclusive prefix of n (<= 4 * blockDim.x) values in[i] (global, written by an earlier
-// kernel) into out[0..n], out[n] = the total; warp_sums has 33 words. All threads of
-// the block call it.
-__device__ void block_exclusive_scan(const uint32_t* in, uint32_t n, uint32_t* out,
-                                     uint32_t* warp_sums) {
+// Exclusive prefix of n (<= 4 * blockDim.x) values into out[0..n], out[n] = the total;
+// thread i holds values i * per .. i * per + per - 1 (per = ceil(n / blockDim.x), zero
+// past n) in v; warp_sums has 33 words. All threads of the block call it.
+__device__ void block_exclusive_scan_vals(const uint32_t (&v)[4], uint32_t n, uint32_t* out,
+                                          uint32_t* warp_sums) {
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x / 32;
   const uint32_t per = (n + blockDim.x - 1) / blockDim.x;
   const uint32_t b0 = threadIdx.x * per;
-  uint32_t v[4], sum = 0;
+  uint32_t sum = 0;
 #pragma unroll
-  for (int k = 0; k < 4; k++) {
-    v[k] = (k < (int)per && b0 + k < n) ? __ldcg(in + b0 + k) : 0u;
-    sum += v[k];
-  }
+  for (int k = 0; k < 4; k++) sum += v[k];
   uint32_t incl = sum;
 #pragma unroll
   for (int d = 1; d < 32; d <<= 1) {
@@ -194,6 +191,16 @@ __device__ void block_exclusive_scan(const uint32_t* in, uint32_t n, uint32_t* o
     }
   if (threadIdx.x == 0) out[n] = warp_sums[32];
   __syncthreads();
+}
+
+// The same over in[0..n) (global, written by an earlier kernel).
+__device__ void block_exclusive_scan(const uint32_t* in, uint32_t n, uint32_t* out,
+                                     uint32_t* warp_sums) {
+  const uint32_t per = (n + blockDim.x - 1) / blockDim.x, b0 = threadIdx.x * per;
+  uint32_t v[4];
+#pragma unroll
+  for (int k = 0; k < 4; k++) v[k] = (k < (int)per && b0 + k < n) ? __ldcg(in + b0 + k) : 0u;
+  block_exclusive_scan_vals(v, n, out, warp_sums);
 }
 
 // Exclusive prefixes of two arrays at once: in_k[0..n_k) (n_k <= 4 * blockDim.x, global,
@@ -745,12 +752,14 @@ __global__ void __launch_bounds__(kGainThreads) k_gain(SplitLaunch a) {
 }
 
 __global__ void __launch_bounds__(kBestThreads) k_best(SplitLaunch a) {
-  pdl_enter();
   __shared__ double red_g[kBestThreads / 32];
   __shared__ uint32_t red_i[kBestThreads / 32];
   __shared__ uint32_t s_b;
   const uint32_t f = blockIdx.x;
   const uint32_t nb = a.nb, nsplit = nb - 1, b = threadIdx.x;
+  // Before the wait: everything here comes from grids at least two launches back (the
+  // previous level's leaf-index update, this round's gradients, the cut table), and the
+  // words written are read by no grid before the leaf-index update that follows.
   if (f == 0) {
     // this level's per-node row counts (from the previous level's lists) and the cursors
     // the leaf-index update fills for the next level
@@ -770,17 +779,29 @@ __global__ void __launch_bounds__(kBestThreads) k_best(SplitLaunch a) {
       for (uint32_t w = threadIdx.x; w < a.cursor_next_words; w += kBestThreads)
         a.cursor_next[w] = 0u;
   }
-  const double inv_g = q_inv_scale(a.maxbits[0]), inv_h = q_inv_scale(a.maxbits[1]);
+  const double inv_g = q_inv_scale(__ldcg(a.maxbits)), inv_h = q_inv_scale(__ldcg(a.maxbits + 1));
   const double lambda = a.lambda;
-  double key = -RW_INF;
   const float thr_own = b < nsplit ? __ldg(a.cuts + (size_t)f * nsplit + b) : 0.0f;
+  const int mono = a.mono ? a.monotone[f] : 0;
+  pdl_wait();
+  pdl_trigger();
+  double key = -RW_INF;
   if (b < nsplit) {
+    // the node-order sum (src/cpu.rs adds the nodes' gains in node order); the terms are
+    // loaded eight at a time so the loads overlap
     double gain = 0.0;
     const double* t = a.term + (size_t)f * a.n_nodes * nsplit + b;
-    for (uint32_t nd = 0; nd < a.n_nodes; nd++) gain += __ldcg(t + (size_t)nd * nsplit);
+    uint32_t nd = 0;
+    for (; nd + 8 <= a.n_nodes; nd += 8) {
+      double v[8];
+#pragma unroll
+      for (int k = 0; k < 8; k++) v[k] = __ldcg(t + (size_t)(nd + k) * nsplit);
+#pragma unroll
+      for (int k = 0; k < 8; k++) gain += v[k];
+    }
+    for (; nd < a.n_nodes; nd++) gain += __ldcg(t + (size_t)nd * nsplit);
     key = gain;
     // candidate masks (extensions): per-tree column sampling and monotone direction
-    const int mono = a.mono ? a.monotone[f] : 0;
     const bool dropped = a.colsample < 1.0f &&
                          (float)hash01_bits(f, a.tree_seed ^ 0x5bd1e995u) / 16777215.0f >=
                              a.colsample;
@@ -1061,13 +1082,20 @@ constexpr int kApplyThreads = 256;
 constexpr uint32_t kLeafSmem = 1024;
 
 // The level's split from the per-feature records (every CTA), and by CTA 0 the model
-// slot and feature importance. Leaves (feature, bin) in s_ft.
-__device__ void choose_split(const ApplyLaunch& a, uint32_t* s_ft, double* red_g,
-                             uint32_t* red_i) {
+// slot and feature importance. Leaves (feature, bin) in s_ft. `r0` is this thread's
+// record of feature threadIdx.x (loaded by the caller together with its other reads);
+// s_bin holds the bins of the first blockDim.x features.
+static_assert(sizeof(SplitRec) == 16, "a record is one 16-byte load (the buffers are allocation-aligned)");
+__device__ void choose_split(const ApplyLaunch& a, const SplitRec& r0, uint32_t* s_ft,
+                             double* red_g, uint32_t* red_i, uint32_t* s_bin) {
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   double bk = -RW_INF;
   uint32_t bf = 0xffffffffu;
-  for (uint32_t ff = threadIdx.x; ff < a.nf; ff += blockDim.x)
+  if (threadIdx.x < a.nf) {
+    argmax_merge(bk, bf, r0.gain, threadIdx.x);
+    s_bin[threadIdx.x] = r0.bin;
+  }
+  for (uint32_t ff = threadIdx.x + blockDim.x; ff < a.nf; ff += blockDim.x)
     argmax_merge(bk, bf, __ldcg(&a.rec[ff].gain), ff);
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) {
@@ -1083,7 +1111,7 @@ __device__ void choose_split(const ApplyLaunch& a, uint32_t* s_ft, double* red_g
   if (threadIdx.x == 0) {
     for (uint32_t w = 1; w < blockDim.x / 32; w++) argmax_merge(bk, bf, red_g[w], red_i[w]);
     if (bk == -RW_INF) bf = 0;
-    const uint32_t bb = __ldcg(&a.rec[bf].bin);
+    const uint32_t bb = bf < blockDim.x ? s_bin[bf] : __ldcg(&a.rec[bf].bin);
     s_ft[0] = bf;
     s_ft[1] = bb;
     if (blockIdx.x == 0) {
@@ -1110,6 +1138,7 @@ __global__ void __launch_bounds__(kApplyThreads, 8) k_apply(ApplyLaunch a) {
   __shared__ uint32_t red_i[kApplyThreads / 32];
   __shared__ uint32_t s_ft[2];
   __shared__ uint32_t warp_sums[33];
+  __shared__ uint32_t s_bin[kApplyThreads];
   const uint32_t lane = threadIdx.x & 31;
   const LevelLists& L = a.lists;
   const bool listing = !FINAL && L.entries;
@@ -1141,16 +1170,29 @@ __global__ void __launch_bounds__(kApplyThreads, 8) k_apply(ApplyLaunch a) {
   const uint64_t qi0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
   uint2 nd_first = make_uint2(0u, 0u);
   if (qi0 < n4) nd_first = *reinterpret_cast<const uint2*>(a.node + qi0 * 4);
-  pdl_wait();
-  pdl_trigger();
-  if (FINAL) {
+  if (FINAL) {  // this round's scales (the gradient pass, long completed)
     wg = rw_wscale_exp(__ldcg(a.maxbits), a.n_rows);
     wh = rw_wscale_exp(__ldcg(a.maxbits + 1), a.n_rows);
   }
-  choose_split(a, s_ft, red_g, red_i);
+  pdl_wait();
+  pdl_trigger();
+  // the split records and the node row counts (both from the split scan) in one round
+  SplitRec r0 = {};
+  if (threadIdx.x < a.nf) {
+    const double2 rv = __ldcg(reinterpret_cast<const double2*>(a.rec + threadIdx.x));
+    r0.gain = rv.x;
+    r0.bin = (uint32_t)__double_as_longlong(rv.y);
+  }
+  uint32_t nc[4] = {0u, 0u, 0u, 0u};
+  const uint32_t nc_per = (n_nodes + blockDim.x - 1) / blockDim.x, nc0 = threadIdx.x * nc_per;
+  if (listing)
+#pragma unroll
+    for (int k = 0; k < 4; k++)
+      if (k < (int)nc_per && nc0 + k < n_nodes) nc[k] = __ldcg(L.ncount + nc0 + k);
+  choose_split(a, r0, s_ft, red_g, red_i, s_bin);
   const uint32_t f = s_ft[0], t = s_ft[1];
   if (listing) {
-    block_exclusive_scan(L.ncount, n_nodes, s_cap, warp_sums);
+    block_exclusive_scan_vals(nc, n_nodes, s_cap, warp_sums);
     if (L.subtract)
       for (uint32_t nd = threadIdx.x; nd < n_nodes; nd += blockDim.x) {
         const uint8_t c = __ldcg(L.choice + (size_t)f * n_nodes + nd);
