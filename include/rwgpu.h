@@ -62,7 +62,7 @@ typedef struct rw_train_params {
   float goss_other;
   float clamp_hessian;    /* experimental in the reference; must be 0 here */
   int32_t pack4;          /* 4-bit bins when n_bins <= 16 */
-  int32_t pgbm;           /* leaf variances; must be 0 here */
+  int32_t pgbm;           /* Config::pgbm; the variances are computed when leafvar != NULL */
   int32_t objective;      /* RW_OBJ_LOGISTIC or RW_OBJ_L2 */
   uint32_t replicas;      /* accepted, ignored */
   int32_t smem_hist, f16_hist, int_hist; /* accepted, ignored */
@@ -166,7 +166,11 @@ int rw_fit_with_boundaries(rw_ctx* ctx, const rw_train_params* p, const float* x
 
 /* The tree loop of fit_inner (src/booster.rs:349-513). Outputs (caller-allocated):
  * feat/thr/thr_bin [n_trees*depth], leafval [n_trees<<depth], fi_gain/fi_count [nf].
- * thr_bin, leafvar and prof may be NULL; leafvar must be NULL (pgbm unsupported). */
+ * thr_bin, leafvar and prof may be NULL. leafvar [n_trees<<depth], when not NULL,
+ * receives the PGBM leaf variances (src/gpu_kernels.rs:1015-1080): lr^2 * max(S2/H -
+ * (G/H)^2, 0) for leaves with H > 1, else 0, where G, H and S2 are the leaf's sums of g,
+ * h and g*g over the tree's sampled rows -- here exact wide-fixed-point sums evaluated in
+ * f64 and rounded once to f32 (the reference sums in f32 atomics). */
 int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float base_score,
                    uint32_t* feat, float* thr, uint16_t* thr_bin, float* leafval,
                    float* leafvar, float* fi_gain, float* fi_count, rw_profile* prof);
@@ -185,6 +189,12 @@ int rw_fit(rw_ctx* ctx, const rw_train_params* p, const float* x_rowmajor, const
  * src/booster.rs:582-601). */
 int rw_predict_f32(rw_ctx* ctx, const rw_model* m, const float* x_rowmajor, uint64_t n,
                    uint32_t nf, float* out);
+/* PGBM predict_var (src/gpu_kernels.rs:1084-1120, Booster::predict_std before its
+ * square root, src/booster.rs:559-577): per row the sum over trees, in tree order in f32
+ * from 0, of the variance leafvar[t << depth | leaf] of the leaf the row reaches; m's
+ * leafval and base_score are not used. leafvar is rw_fit's PGBM output. */
+int rw_predict_var_f32(rw_ctx* ctx, const rw_model* m, const float* leafvar,
+                       const float* x_rowmajor, uint64_t n, uint32_t nf, float* out);
 /* Same margins from pre-binned feature-major u8 rows bins[nf][n] and thr_bin. */
 int rw_predict_u8(rw_ctx* ctx, const rw_model* m, const uint8_t* bins_featmajor, uint64_t n,
                   uint32_t nf, float* out);

@@ -28,7 +28,7 @@ class _Params(C.Structure):
         ("subsample", C.c_float), ("colsample", C.c_float), ("goss_top", C.c_float),
         ("goss_other", C.c_float), ("objective", C.c_int32), ("subtract", C.c_int32),
         ("monotone", C.POINTER(C.c_int32)), ("n_monotone", C.c_uint32), ("exact", C.c_int32),
-        ("n_threads", C.c_int32),
+        ("n_threads", C.c_int32), ("leafvar", C.POINTER(C.c_float)),
     ]
 
 
@@ -110,7 +110,7 @@ class OracleFit:
 def train(x, y, cuts, base, *, n_trees, depth, n_bins, learning_rate=0.1, lambda_=1.0,
           min_child_h=1e-3, subsample=1.0, colsample=1.0, goss_top=0.0, goss_other=0.1,
           objective="logistic", subtract=True, monotone=(), exact=True, n_threads=0,
-          trace_levels=False, trace_trees=0) -> OracleFit:
+          trace_levels=False, trace_trees=0, pgbm=False) -> OracleFit:
     """orc_train: exact=True is oracle_exact (the GPU's arithmetic), False is oracle_ref
     (faithful src/cpu.rs with n_threads rayon chunks). trace_trees > 0 records the first
     trees' g, h ([k][n] f32, 0 outside the sample) and final leaves ([k][n] u16)."""
@@ -135,6 +135,12 @@ def train(x, y, cuts, base, *, n_trees, depth, n_bins, learning_rate=0.1, lambda
     r.leafval = np.zeros(n_trees << depth, np.float32)
     r.fi_gain = np.zeros(nf, np.float32)
     r.fi_count = np.zeros(nf, np.float32)
+    r.leafvar = None
+    if pgbm:  # PGBM leaf variances (exact mode only)
+        if not exact:
+            raise ValueError("pgbm leaf variances are computed in exact mode only")
+        r.leafvar = np.zeros(n_trees << depth, np.float32)
+        p.leafvar = r.leafvar.ctypes.data_as(C.POINTER(C.c_float))
     tr = _Trace()
     hists = []
     if trace_levels:

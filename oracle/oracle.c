@@ -673,6 +673,7 @@ int orc_train(const orc_params* p, const float* x, const float* y, uint64_t n, u
       }
     }
     int e_g = 0, e_h = 0, w_g = 0, w_h = 0;
+    uint32_t bits_g = 0; /* IEEE bits of the round's max |g| (exact mode) */
     if (exact) {
       /* per-round fixed-point scales from the maxima over the sampled rows */
       float mg = 0.0f, mh = 0.0f;
@@ -685,6 +686,7 @@ int orc_train(const orc_params* p, const float* x, const float* y, uint64_t n, u
       uint32_t bg, bh;
       memcpy(&bg, &mg, 4);
       memcpy(&bh, &mh, 4);
+      bits_g = bg;
       e_g = rw_qscale_exp(bg);
       e_h = rw_qscale_exp(bh);
       w_g = rw_wscale_exp(bg, n);
@@ -816,10 +818,14 @@ int orc_train(const orc_params* p, const float* x, const float* y, uint64_t n, u
        * (rw_wquantize), so the leaf values do not depend on the histogram's 17-bit q */
       int64_t* sg = (int64_t*)calloc(leaves, sizeof(int64_t));
       int64_t* sh = (int64_t*)calloc(leaves, sizeof(int64_t));
+      int64_t* s2 = p->leafvar ? (int64_t*)calloc(leaves, sizeof(int64_t)) : NULL;
+      /* the g^2 scale: (max |g|)^2 in f32 bounds every g*g (f32 rounding is monotone) */
+      const int w_g2 = p->leafvar ? rw_wscale_exp(rw_sq_maxbits(bits_g), n) : 0;
       for (uint64_t q = 0; q < m; q++) {
         uint32_t r = samp[q];
         sg[node[r]] += rw_wquantize(g[r], w_g);
         sh[node[r]] += rw_wquantize(hess[r], w_h);
+        if (s2) s2[node[r]] += rw_wquantize(g[r] * g[r], w_g2);
       }
       lg = (double*)malloc(leaves * sizeof(double));
       lc = (double*)malloc(leaves * sizeof(double));
@@ -827,6 +833,11 @@ int orc_train(const orc_params* p, const float* x, const float* y, uint64_t n, u
         lg[l] = rw_wvalue(sg[l], w_g);
         lc[l] = rw_wvalue(sh[l], w_h);
       }
+      if (s2)
+        for (uint32_t l = 0; l < leaves; l++)
+          p->leafvar[(size_t)t * leaves + l] =
+              rw_leaf_variance(lg[l], lc[l], rw_wvalue(s2[l], w_g2), lr);
+      free(s2);
       free(sg);
       free(sh);
     } else {

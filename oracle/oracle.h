@@ -48,6 +48,10 @@ typedef struct orc_params {
   uint32_t n_monotone;
   int32_t exact;     /* 0 = oracle_ref, 1 = oracle_exact */
   int32_t n_threads; /* rayon pool size nt (cpu.rs:138-143); <= 0 -> the reference rule */
+  /* nullable, exact mode only: PGBM per-leaf variances [n_trees][2^depth]
+   * (gpu_kernels.rs:1046-1080: lr^2 * max(S2/H - (G/H)^2, 0) when H > 1, else 0, with
+   * S2 the leaf's sum of g^2), from exact wide-fixed-point sums evaluated in f64 */
+  float* leafvar;
 } orc_params;
 
 /* Optional per-level trace of the FIRST tree (exact mode only): the full level

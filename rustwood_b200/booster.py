@@ -149,6 +149,7 @@ class FitResult:
         self.thr = np.zeros(T * D, dtype=np.float32)
         self.thr_bin = np.zeros(T * D, dtype=np.uint16)
         self.leafval = np.zeros(T << D, dtype=np.float32)
+        self.leafvar = np.zeros(0, dtype=np.float32)  # PGBM leaf variances (cfg.pgbm)
         self.fi_gain = np.zeros(nf, dtype=np.float32)
         self.fi_count = np.zeros(nf, dtype=np.float32)
         self.profile = N.Profile()
@@ -159,8 +160,11 @@ def fit_dataset(ds: Dataset, cfg: Config, base: float, profile: bool = False) ->
     r = FitResult(cfg.n_trees, cfg.depth, ds.nf)
     p = train_params(cfg)
     r.profile.enable = int(profile)
+    if cfg.pgbm:  # fit_inner keeps the leaf variances when cfg.pgbm (src/booster.rs:511-513)
+        r.leafvar = np.zeros(cfg.n_trees << cfg.depth, dtype=np.float32)
     ds.ctx.check(N.lib.rw_fit_dataset(ds.h, C.byref(p), base, N.ptr(r.feat), N.ptr(r.thr),
-                                      N.ptr(r.thr_bin), N.ptr(r.leafval), None, N.ptr(r.fi_gain),
+                                      N.ptr(r.thr_bin), N.ptr(r.leafval),
+                                      N.ptr(r.leafvar) if cfg.pgbm else None, N.ptr(r.fi_gain),
                                       N.ptr(r.fi_count), C.byref(r.profile)))
     return r
 
@@ -180,6 +184,7 @@ class Booster:
         self.thr = np.zeros(0, np.float32)
         self.thr_bin = np.zeros(0, np.uint16)
         self.leafval = np.zeros(0, np.float32)
+        self.leafvar = np.zeros(0, np.float32)
         self.encoders: list[dict] = []
         self.gmean = 0.0
         self.fi_gain = np.zeros(0, np.float32)
@@ -224,6 +229,7 @@ class Booster:
 
     def _take(self, r: FitResult):
         self.feat, self.thr, self.thr_bin, self.leafval = r.feat, r.thr, r.thr_bin, r.leafval
+        self.leafvar = r.leafvar
         self.fi_gain, self.fi_count = r.fi_gain, r.fi_count
         self.last_profile = r.profile
 
@@ -254,6 +260,23 @@ class Booster:
         self.ctx.check(N.lib.rw_predict_f32(self.ctx.h, C.byref(m), N.ptr(x), n, x.shape[1],
                                             N.ptr(out)))
         return out
+
+    def predict_std(self, x: np.ndarray) -> np.ndarray:
+        """Booster::predict_std (src/booster.rs:559-577): per row the square root of the
+        summed PGBM leaf variances (rw_predict_var_f32), max(0).sqrt() in f32."""
+        if self.cfg.n_trees and len(self.leafvar) != (self.cfg.n_trees << self.cfg.depth):
+            raise RuntimeError("no leaf variances: fit with pgbm=True")
+        x = np.array(x, dtype=np.float32, order="C", copy=bool(self.cfg.categorical))
+        if self.cfg.categorical:
+            encoding.transform(x, self.cfg.categorical, self.encoders, self.gmean,
+                               self.cfg.cat_hash_buckets)
+        n = x.shape[0]
+        var = np.empty(n, dtype=np.float32)
+        m, _keep = self.model()
+        lv = np.ascontiguousarray(self.leafvar, np.float32)
+        self.ctx.check(N.lib.rw_predict_var_f32(self.ctx.h, C.byref(m), N.ptr(lv), N.ptr(x), n,
+                                                x.shape[1], N.ptr(var)))
+        return np.sqrt(np.maximum(var, np.float32(0.0)))
 
     def predict_bins(self, bins_featmajor: np.ndarray) -> np.ndarray:
         """Raw margins from pre-binned feature-major u8 rows (rw_predict_u8)."""

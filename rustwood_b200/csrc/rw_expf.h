@@ -192,4 +192,26 @@ RW_HD double rw_wvalue(int64_t s, int w) {
   return RW_DMUL((double)s, rw_pow2i(-w));
 }
 
+/* PGBM (gpu_kernels.rs:1046-1080): IEEE bits of M*M in f32 for the bits of a
+ * non-negative M, clamped to the largest finite float; since f32 rounding is monotone,
+ * every g*g with |g| <= M is at most this value, so it sets the g^2 sums' wide scale. */
+RW_HD uint32_t rw_sq_maxbits(uint32_t max_bits) {
+  float m;
+  memcpy(&m, &max_bits, 4);
+  float m2 = m * m;
+  if (!(m2 <= 3.4028234663852886e38f)) m2 = 3.4028234663852886e38f; /* inf or NaN */
+  uint32_t b;
+  memcpy(&b, &m2, 4);
+  return b;
+}
+
+/* A leaf's PGBM variance from its exact sums (G, H, S2 = sum of g^2), evaluated in f64:
+ * lr^2 * max(S2/H - (G/H)^2, 0) when H > 1, else 0; rounded once to f32. */
+RW_HD float rw_leaf_variance(double G, double H, double S2, double lr) {
+  if (!(H > 1.0)) return 0.0f;
+  const double m = G / H;
+  const double v = RW_DADD(S2 / H, -RW_DMUL(m, m));
+  return (float)RW_DMUL(RW_DMUL(lr, lr), v > 0.0 ? v : 0.0);
+}
+
 #endif /* RW_EXPF_H */

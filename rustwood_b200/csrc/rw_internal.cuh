@@ -223,8 +223,22 @@ struct LeafValues {
   uint64_t n_rows;  // global row count (the wide scale's row bound)
   double lr, lambda;
   float* leafval;   // out: the tree's slot of the model's leaf values
+  const long long* leafsum2 = nullptr;  // PGBM: per-leaf wide sums of g^2, or null
+  float* leafvar = nullptr;  // PGBM out: the tree's slot of the leaf variances (with leafsum2)
 };
 cudaError_t launch_leafval(const LeafValues& a, cudaStream_t s, int* nl);
+// PGBM: every row's g^2 (f32) in the wide fixed point into its leaf's exact int64 sum
+// (the leaf_g2 sums of gpu_kernels.rs:1015-1043); run after the tree's last level.
+struct LeafSquares {
+  const uint16_t* node;  // the rows' leaf indices (low 15 bits)
+  const float* g;        // 0 for unsampled and padded rows
+  uint64_t n_pad;
+  const uint32_t* maxbits;
+  uint64_t n_rows;  // global row count (the wide scale's row bound)
+  uint32_t n_leaves;
+  long long* leafsum2;  // [n_leaves], zeroed with the other leaf sums
+};
+cudaError_t launch_leafsq(const LeafSquares& a, cudaStream_t s, int* nl);
 // The previous tree's pred update, done by the next round's gradient kernel:
 // pred += leafval[node & 0x7fff] for every row (src/cpu.rs:319-320).
 struct PrevTree {

@@ -458,7 +458,6 @@ int check_params(rw_ctx* ctx, const rw_train_params* p, uint32_t n_bins) {
     return fail(ctx, RW_ERR_ARG, "params n_bins differs from the dataset's n_bins");
   if (p->objective != RW_OBJ_LOGISTIC && p->objective != RW_OBJ_L2)
     return fail(ctx, RW_ERR_ARG, "unknown objective");
-  if (p->pgbm) return fail(ctx, RW_ERR_UNSUPPORTED, "pgbm leaf variances are not supported");
   if (p->clamp_hessian != 0.0f)
     return fail(ctx, RW_ERR_UNSUPPORTED, "clamp_hessian is not supported");
   return RW_OK;
@@ -928,7 +927,6 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
   rw_ctx* ctx = ds->ctx;
   int rc = check_params(ctx, p, ds->n_bins);
   if (rc) return rc;
-  if (leafvar) return fail(ctx, RW_ERR_UNSUPPORTED, "leafvar output is not supported");
   if (p->n_trees > 0 && (!feat || !thr || !leafval))
     return fail(ctx, RW_ERR_ARG, "NULL model output");
   if (!fi_gain || !fi_count) return fail(ctx, RW_ERR_ARG, "NULL feature-importance output");
@@ -937,6 +935,10 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
 
   const uint32_t T = p->n_trees, D = p->depth, NL = 1u << D, nf = ds->nf, nb = ds->n_bins;
   const uint64_t n = ds->n, n_pad = ds->n_pad;
+  // PGBM (gpu_kernels.rs:1015-1080): with a leafvar output the last level also sums g^2
+  // per leaf (a third row of the leaf sums) and the leaf pass writes the variances
+  const bool want_var = leafvar != nullptr;
+  const uint32_t LS = (want_var ? 3u : 2u) * NL;  // leaf-sum words
   const bool subtract = p->subtract != 0;
   const bool logistic = p->objective == RW_OBJ_LOGISTIC;
   const bool goss = p->goss_top > 0.0f;
@@ -963,7 +965,7 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
   WsBuf<long long> hb0, hb1, hf0, hf1;
   WsBuf<uint32_t> d_feat, maxbits;
   WsBuf<SplitRec> rec;
-  WsBuf<long long> leafsum;  // [2][NL] per-leaf wide-fixed-point sums of g and h
+  WsBuf<long long> leafsum;  // [2 or 3][NL] per-leaf wide-fixed-point sums of g, h (, g^2)
   WsBuf<double> term;
   WsBuf<long long> mono_sums;
   WsBuf<int32_t> d_mono;
@@ -1017,6 +1019,8 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
   RW_CU(ctx, d_thr.get(ds, "thr", (size_t)T * D));
   RW_CU(ctx, d_thr_bin.get(ds, "thr_bin", (size_t)T * D));
   RW_CU(ctx, d_leafval.get(ds, "leafval", (size_t)T * NL));
+  WsBuf<float> d_leafvar;
+  if (want_var) RW_CU(ctx, d_leafvar.get(ds, "leafvar", (size_t)T * NL));
   RW_CU(ctx, d_fi_gain.get(ds, "fi_gain", nf));
   RW_CU(ctx, d_fi_count.get(ds, "fi_count", nf));
   RW_CU(ctx, maxbits.get(ds, "maxbits", (size_t)std::max<uint32_t>(T, 1) * 2));
@@ -1024,7 +1028,7 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
   RW_CU(ctx, kerr.get(ds, "kernel_err", 1));
   RW_CU(ctx, cudaMemsetAsync(kerr.p, 0, sizeof(int), s));
   RW_CU(ctx, rec.get(ds, "split_rec", nf));
-  RW_CU(ctx, leafsum.get(ds, "leaf_sums", 2 * (size_t)NL));
+  RW_CU(ctx, leafsum.get(ds, "leaf_sums", (size_t)LS));
   RW_CU(ctx, term.get(ds, "gain_terms", (size_t)nf * (NL / 2) * (nb - 1)));
   WsBuf<long long> prefix;
   RW_CU(ctx, prefix.get(ds, "leaf_prefix", (size_t)nf * (NL / 2) * nb * 2));
@@ -1116,7 +1120,7 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
       RW_CU(ctx, launch_peer_small(ps, mb, 2, 1, ++ctx->peer_epoch, kerr.p, s, &nl));
     else if (ctx->comm)
       RW_NC(ctx, ncclAllReduce(mb, mb, 2, ncclUint32, ncclMax, ctx->comm, s));
-    RW_CU(ctx, launch_quant(g.p, h.p, mb, n_pad, q.p, node.p, hbp[0], cell, leafsum.p, 2 * NL,
+    RW_CU(ctx, launch_quant(g.p, h.p, mb, n_pad, q.p, node.p, hbp[0], cell, leafsum.p, LS,
                             ncount[0], s, &nl));
     pt.mark(RW_CAT_GRADIENTS);
 
@@ -1224,14 +1228,28 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
       al.hb_next = groups_next ? hb_next : nullptr;
       al.hb_next_words = (uint64_t)groups_next * cell;
       RW_CU(ctx, launch_apply(al, s, &nl));
+      if (want_var && d == D - 1) {
+        LeafSquares sq;
+        sq.node = node.p;
+        sq.g = g.p;
+        sq.n_pad = n_pad;
+        sq.maxbits = mb;
+        sq.n_rows = ds->n_global;
+        sq.n_leaves = NL;
+        sq.leafsum2 = leafsum.p + 2 * (size_t)NL;
+        RW_CU(ctx, launch_leafsq(sq, s, &nl));
+      }
       pt.mark(d == D - 1 ? RW_CAT_UPDATE_PRED : RW_CAT_APPLY);
     }
     // every rank's leaf sums (exact integers: any order gives the same totals)
     if (peer) {
       RW_CU(ctx, launch_peer_small(ps, leafsum.p, 2 * NL, 0, ++ctx->peer_epoch, kerr.p, s, &nl));
+      if (want_var)  // the g^2 sums in a second exchange (the small slots hold 2 * 4096)
+        RW_CU(ctx, launch_peer_small(ps, leafsum.p + 2 * (size_t)NL, NL, 0, ++ctx->peer_epoch,
+                                     kerr.p, s, &nl));
       pt.mark(RW_CAT_ALLREDUCE);
     } else if (ctx->comm) {
-      RW_NC(ctx, ncclAllReduce(leafsum.p, leafsum.p, 2 * (size_t)NL, ncclInt64, ncclSum, ctx->comm,
+      RW_NC(ctx, ncclAllReduce(leafsum.p, leafsum.p, (size_t)LS, ncclInt64, ncclSum, ctx->comm,
                                s));
       pt.mark(RW_CAT_ALLREDUCE);
     }
@@ -1243,6 +1261,8 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
     lv.lr = (double)p->learning_rate;
     lv.lambda = (double)p->lambda;
     lv.leafval = d_leafval.p + (size_t)t * NL;
+    lv.leafsum2 = want_var ? leafsum.p + 2 * (size_t)NL : nullptr;
+    lv.leafvar = want_var ? d_leafvar.p + (size_t)t * NL : nullptr;
     RW_CU(ctx, launch_leafval(lv, s, &nl));
     pt.mark(RW_CAT_UPDATE_PRED);
   }
@@ -1257,6 +1277,8 @@ extern "C" int rw_fit_dataset(rw_dataset* ds, const rw_train_params* p, float ba
     if (thr_bin)
       RW_CU(ctx, cudaMemcpy(thr_bin, d_thr_bin.p, (size_t)T * D * 2, cudaMemcpyDeviceToHost));
     RW_CU(ctx, cudaMemcpy(leafval, d_leafval.p, (size_t)T * NL * 4, cudaMemcpyDeviceToHost));
+    if (want_var)
+      RW_CU(ctx, cudaMemcpy(leafvar, d_leafvar.p, (size_t)T * NL * 4, cudaMemcpyDeviceToHost));
   }
   int kerr_h = 0;
   RW_CU(ctx, cudaMemcpy(&kerr_h, kerr.p, sizeof(int), cudaMemcpyDeviceToHost));
@@ -1302,7 +1324,6 @@ static int group_fit(rw_dataset* gd, const rw_train_params* p, float base_score,
   rw_ctx* front = gd->ctx;
   int rc = check_params(front, p, gd->n_bins);
   if (rc) return rc;
-  if (leafvar) return fail(front, RW_ERR_UNSUPPORTED, "leafvar output is not supported");
   if (p->n_trees > 0 && (!feat || !thr || !leafval))
     return fail(front, RW_ERR_ARG, "NULL model output");
   if (!fi_gain || !fi_count) return fail(front, RW_ERR_ARG, "NULL feature-importance output");
@@ -1311,7 +1332,7 @@ static int group_fit(rw_dataset* gd, const rw_train_params* p, float base_score,
   const size_t nf = gd->nf;
   struct Out {
     std::vector<uint32_t> feat;
-    std::vector<float> thr, leafval, fig, fic;
+    std::vector<float> thr, leafval, leafvar, fig, fic;
     std::vector<uint16_t> tb;
     rw_profile prof;
   };
@@ -1321,6 +1342,7 @@ static int group_fit(rw_dataset* gd, const rw_train_params* p, float base_score,
     q.thr.resize(std::max<size_t>(K, 1));
     q.tb.resize(std::max<size_t>(K, 1));
     q.leafval.resize(std::max<size_t>(L, 1));
+    if (leafvar) q.leafvar.resize(std::max<size_t>(L, 1));  // every rank runs the same exchanges
     q.fig.resize(nf);
     q.fic.resize(nf);
     memset(&q.prof, 0, sizeof q.prof);
@@ -1331,8 +1353,8 @@ static int group_fit(rw_dataset* gd, const rw_train_params* p, float base_score,
       [&](int i) {
         Out& q = o[i];
         return rw_fit_dataset(gd->shards[i], p, base_score, q.feat.data(), q.thr.data(),
-                              q.tb.data(), q.leafval.data(), nullptr, q.fig.data(), q.fic.data(),
-                              &q.prof);
+                              q.tb.data(), q.leafval.data(), leafvar ? q.leafvar.data() : nullptr,
+                              q.fig.data(), q.fic.data(), &q.prof);
       },
       true);
   if (rc) return rc;
@@ -1342,6 +1364,7 @@ static int group_fit(rw_dataset* gd, const rw_train_params* p, float base_score,
         memcmp(o[i].thr.data(), o[0].thr.data(), K * 4) ||
         memcmp(o[i].tb.data(), o[0].tb.data(), K * 2) ||
         memcmp(o[i].leafval.data(), o[0].leafval.data(), L * 4) ||
+        (leafvar && memcmp(o[i].leafvar.data(), o[0].leafvar.data(), L * 4)) ||
         memcmp(o[i].fig.data(), o[0].fig.data(), nf * 4) ||
         memcmp(o[i].fic.data(), o[0].fic.data(), nf * 4))
       return fail(front, RW_ERR_CUDA, "ranks produced different models");
@@ -1350,6 +1373,7 @@ static int group_fit(rw_dataset* gd, const rw_train_params* p, float base_score,
     memcpy(thr, o[0].thr.data(), K * 4);
     if (thr_bin) memcpy(thr_bin, o[0].tb.data(), K * 2);
     memcpy(leafval, o[0].leafval.data(), L * 4);
+    if (leafvar) memcpy(leafvar, o[0].leafvar.data(), L * 4);
   }
   memcpy(fi_gain, o[0].fig.data(), nf * 4);
   memcpy(fi_count, o[0].fic.data(), nf * 4);
@@ -1494,6 +1518,19 @@ extern "C" int rw_predict_f32_device(rw_ctx* ctx, const rw_dmodel* dm, const flo
 
 // Row ranges of a multi-GPU context's ranks for n rows (contiguous, in rank order).
 static uint64_t rank_lo(uint64_t n, int i, int W) { return n * (uint64_t)i / (uint64_t)W; }
+
+// PGBM predict_var (gpu_kernels.rs:1084-1120): the same traversal as the margins, summing
+// the leaves' variances in tree order in f32 from 0 -- exactly rw_predict_f32 over a model
+// whose leaf table is leafvar and whose base score is 0.
+extern "C" int rw_predict_var_f32(rw_ctx* ctx, const rw_model* m, const float* leafvar,
+                                  const float* x, uint64_t n, uint32_t nf, float* out) {
+  if (!m) return fail(ctx, RW_ERR_ARG, "model is NULL");
+  if (!leafvar && m->n_trees > 0) return fail(ctx, RW_ERR_ARG, "leafvar is NULL");
+  rw_model mv = *m;
+  mv.leafval = leafvar;
+  mv.base_score = 0.0f;
+  return rw_predict_f32(ctx, &mv, x, n, nf, out);
+}
 
 extern "C" int rw_predict_f32(rw_ctx* ctx, const rw_model* m, const float* x, uint64_t n,
                               uint32_t nf, float* out) {

@@ -323,11 +323,13 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(HistLaunch a, uint32_t ft
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   uint64_t w, w_end;
   const uint32_t units = a.entries ? ftiles * a.groups : 0u;  // (tile, group) units
-  if (units != 0 && units <= 32 && units * 4 <= gridDim.x) {
-    // Few units: each nonempty unit u gets its own CTAs, 1 + floor(len_u * (grid -
-    // units) / total) of them (at most the grid in all), which split it evenly. No CTA
-    // straddles two units, so every CTA flushes once; a CTA's share is within
-    // total / (grid - units) rows.
+  if (units != 0 && units <= 32 && units * 4 <= gridDim.x &&
+      total <= (uint64_t)gridDim.x * 2 * kMaxRowsPerCta) {
+    // Few units and short slices: each nonempty unit u gets its own CTAs, 1 + floor(len_u
+    // * (grid - units) / total) of them (at most the grid in all), which split it evenly.
+    // No CTA straddles two units, so every CTA flushes once; a CTA's share is within
+    // total / (grid - units) rows. (With long slices a CTA flushes several times anyway,
+    // and the contiguous slices below balance the rows better.)
     __shared__ unsigned long long s_range[2];
     if (warp == 0) {
       uint32_t c = 0;
@@ -787,19 +789,10 @@ __global__ void __launch_bounds__(kBestThreads) k_best(SplitLaunch a) {
   pdl_trigger();
   double key = -RW_INF;
   if (b < nsplit) {
-    // the node-order sum (src/cpu.rs adds the nodes' gains in node order); the terms are
-    // loaded eight at a time so the loads overlap
+    // the node-order sum (src/cpu.rs adds the nodes' gains in node order)
     double gain = 0.0;
     const double* t = a.term + (size_t)f * a.n_nodes * nsplit + b;
-    uint32_t nd = 0;
-    for (; nd + 8 <= a.n_nodes; nd += 8) {
-      double v[8];
-#pragma unroll
-      for (int k = 0; k < 8; k++) v[k] = __ldcg(t + (size_t)(nd + k) * nsplit);
-#pragma unroll
-      for (int k = 0; k < 8; k++) gain += v[k];
-    }
-    for (; nd < a.n_nodes; nd++) gain += __ldcg(t + (size_t)nd * nsplit);
+    for (uint32_t nd = 0; nd < a.n_nodes; nd++) gain += __ldcg(t + (size_t)nd * nsplit);
     key = gain;
     // candidate masks (extensions): per-tree column sampling and monotone direction
     const bool dropped = a.colsample < 1.0f &&
@@ -961,14 +954,50 @@ __device__ void block_max2_atomic(uint32_t mg, uint32_t mh, uint32_t* maxbits) {
 // (-lr * G / (H + lambda)) as f32), one thread per leaf.
 __global__ void k_leafval(LeafValues a) {
   pdl_enter();
-  const int wg = rw_wscale_exp(__ldcg(a.maxbits), a.n_rows);
+  const uint32_t mg = __ldcg(a.maxbits);
+  const int wg = rw_wscale_exp(mg, a.n_rows);
   const int wh = rw_wscale_exp(__ldcg(a.maxbits + 1), a.n_rows);
+  const int wg2 = rw_wscale_exp(rw_sq_maxbits(mg), a.n_rows);
   for (uint32_t l = blockIdx.x * blockDim.x + threadIdx.x; l < a.n_leaves;
        l += gridDim.x * blockDim.x) {
     const double G = rw_wvalue(__ldcg(a.leafsum + l), wg);
     const double H = rw_wvalue(__ldcg(a.leafsum + a.n_leaves + l), wh);
     a.leafval[l] = (float)(-a.lr * G / (H + a.lambda));
+    if (a.leafvar)  // PGBM (gpu_kernels.rs:1046-1080), from the exact sums
+      a.leafvar[l] = rw_leaf_variance(G, H, rw_wvalue(__ldcg(a.leafsum2 + l), wg2), a.lr);
   }
+}
+
+// PGBM: the leaves' g^2 sums (gpu_kernels.rs:1015-1043 adds gi * gi per row), exact in the
+// wide fixed point whose scale comes from (max |g|)^2. Per CTA in shared memory (at most
+// 4096 leaves), then one global add per nonzero sum. The preceding grid (the tree's last
+// leaf-index update) writes the leaf indices, so they are read after the wait.
+constexpr int kLeafSqThreads = 256;
+__global__ void __launch_bounds__(kLeafSqThreads) k_leafsq(LeafSquares a) {
+  __shared__ long long s2[4096];
+  for (uint32_t l = threadIdx.x; l < a.n_leaves; l += blockDim.x) s2[l] = 0;
+  const int w2 = rw_wscale_exp(rw_sq_maxbits(__ldcg(a.maxbits)), a.n_rows);
+  pdl_enter();
+  __syncthreads();
+  const uint64_t n4 = a.n_pad / 4;
+  for (uint64_t qi = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; qi < n4;
+       qi += (uint64_t)gridDim.x * blockDim.x) {
+    const uint2 nd2 = __ldcg(reinterpret_cast<const uint2*>(a.node + qi * 4));
+    const float4 g4 = __ldcg(reinterpret_cast<const float4*>(a.g + qi * 4));
+    const uint32_t leaf[4] = {nd2.x & 0x7fffu, (nd2.x >> 16) & 0x7fffu, nd2.y & 0x7fffu,
+                              (nd2.y >> 16) & 0x7fffu};
+    const float gv[4] = {g4.x, g4.y, g4.z, g4.w};
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const long long v = rw_wquantize(gv[k] * gv[k], w2);
+      if (v && leaf[k] < a.n_leaves)
+        atomicAdd(reinterpret_cast<unsigned long long*>(s2 + leaf[k]), (unsigned long long)v);
+    }
+  }
+  __syncthreads();
+  for (uint32_t l = threadIdx.x; l < a.n_leaves; l += blockDim.x)
+    if (s2[l]) atomicAdd(reinterpret_cast<unsigned long long*>(a.leafsum2 + l),
+                         (unsigned long long)s2[l]);
 }
 
 // Gradients (src/cpu.rs:181-193), stride row sampling (src/cpu.rs:172-176, 202-204)
@@ -1554,6 +1583,17 @@ cudaError_t launch_leafval(const LeafValues& a, cudaStream_t s, int* nl) {
   if (!a.leafsum || !a.leafval || !a.maxbits || a.n_leaves == 0) return cudaErrorInvalidValue;
   const unsigned blocks = (a.n_leaves + 255) / 256;
   cudaError_t e = launch_pdl(k_leafval, dim3(blocks), dim3(256), 0, s, a);
+  if (e != cudaSuccess) return e;
+  if (nl) (*nl)++;
+  return cudaGetLastError();
+}
+
+cudaError_t launch_leafsq(const LeafSquares& a, cudaStream_t s, int* nl) {
+  if (!a.node || !a.g || !a.maxbits || !a.leafsum2 || a.n_leaves == 0 || a.n_leaves > 4096 ||
+      a.n_pad % 4 != 0)
+    return cudaErrorInvalidValue;
+  cudaError_t e = launch_pdl(k_leafsq, dim3(grid_for(a.n_pad / 4, kLeafSqThreads)),
+                             dim3(kLeafSqThreads), 0, s, a);
   if (e != cudaSuccess) return e;
   if (nl) (*nl)++;
   return cudaGetLastError();

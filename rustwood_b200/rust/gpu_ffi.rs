@@ -126,6 +126,8 @@ extern "C" {
                                  d_out: *mut f32, kernel_ms: *mut f32) -> c_int;
     pub fn rw_predict_f32_noalloc(ctx: *mut rw_ctx, m: *const rw_model, x_rowmajor: *const f32,
                                   n: u64, nf: u32, out: *mut f32) -> c_int;
+    pub fn rw_predict_var_f32(ctx: *mut rw_ctx, m: *const rw_model, leafvar: *const f32,
+                              x_rowmajor: *const f32, n: u64, nf: u32, out: *mut f32) -> c_int;
     pub fn rw_model_thr_bins(m: *const rw_model, cuts: *const f32, n_bins: u32,
                              thr_bin: *mut u16) -> c_int;
     pub fn rw_compute_boundaries_device(ctx: *mut rw_ctx, d_x: *const f32, n: u64, nf: u32,
@@ -181,6 +183,8 @@ pub struct FitOut {
     pub thr: Vec<f32>,
     pub thr_bin: Vec<u16>,
     pub leafval: Vec<f32>,
+    /// PGBM leaf variances (filled when `p.pgbm != 0`, as fit_inner keeps `leafvar`)
+    pub leafvar: Vec<f32>,
     pub fi_gain: Vec<f32>,
     pub fi_count: Vec<f32>,
     pub profile: rw_profile,
@@ -198,6 +202,7 @@ pub fn fit(ctx: &Context, p: &rw_train_params, x: &[f32], y: &[f32], nf: usize, 
         thr: vec![0.0; t * d],
         thr_bin: vec![0; t * d],
         leafval: vec![0.0; t << d],
+        leafvar: if p.pgbm != 0 { vec![0.0; t << d] } else { Vec::new() },
         fi_gain: vec![0.0; nf],
         fi_count: vec![0.0; nf],
         profile: rw_profile { enable: profile as i32, ..Default::default() },
@@ -205,7 +210,9 @@ pub fn fit(ctx: &Context, p: &rw_train_params, x: &[f32], y: &[f32], nf: usize, 
     check(ctx.raw, unsafe {
         rw_fit(ctx.raw, p, x.as_ptr(), y.as_ptr(), n as u64, nf as u32, cuts.as_ptr(), base_score,
                o.feat.as_mut_ptr(), o.thr.as_mut_ptr(), o.thr_bin.as_mut_ptr(),
-               o.leafval.as_mut_ptr(), ptr::null_mut(), o.fi_gain.as_mut_ptr(),
+               o.leafval.as_mut_ptr(),
+               if p.pgbm != 0 { o.leafvar.as_mut_ptr() } else { ptr::null_mut() },
+               o.fi_gain.as_mut_ptr(),
                o.fi_count.as_mut_ptr(), &mut o.profile)
     })?;
     Ok(o)
@@ -232,4 +239,27 @@ pub fn predict(ctx: &Context, n_trees: usize, depth: usize, n_features: usize, b
         rw_predict_f32(ctx.raw, &m, x.as_ptr(), n as u64, n_features as u32, out.as_mut_ptr())
     })?;
     Ok(out)
+}
+
+/// `Booster::predict_std` (src/booster.rs:559-577): the square root of each row's summed
+/// PGBM leaf variance (`predict_var` on the GPU, then `max(0).sqrt()` as the reference).
+pub fn predict_std(ctx: &Context, n_trees: usize, depth: usize, n_features: usize, feat: &[u32],
+                   thr: &[f32], leafvar: &[f32], x: &[f32]) -> Result<Vec<f32>, Box<dyn Error>> {
+    let n = x.len() / n_features.max(1);
+    let m = rw_model {
+        n_trees: n_trees as u32,
+        depth: depth as u32,
+        n_features: n_features as u32,
+        base_score: 0.0,
+        feat: feat.as_ptr(),
+        thr: thr.as_ptr(),
+        thr_bin: ptr::null(),
+        leafval: leafvar.as_ptr(),
+    };
+    let mut var = vec![0.0f32; n];
+    check(ctx.raw, unsafe {
+        rw_predict_var_f32(ctx.raw, &m, leafvar.as_ptr(), x.as_ptr(), n as u64,
+                           n_features as u32, var.as_mut_ptr())
+    })?;
+    Ok(var.iter().map(|&v| v.max(0.0).sqrt()).collect())
 }

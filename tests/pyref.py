@@ -147,7 +147,7 @@ def _rayon_tree(vecs, lo, hi, zero):
 
 def train(x, y, cuts, base, *, n_trees, depth, n_bins, learning_rate=0.1, lambda_=1.0,
           min_child_h=1e-3, objective="logistic", subtract=True, exact=True, n_threads=1,
-          subsample=1.0):
+          subsample=1.0, pgbm=False):
     n, nf = x.shape
     nb1 = n_bins - 1
     leaves = 1 << depth
@@ -157,6 +157,7 @@ def train(x, y, cuts, base, *, n_trees, depth, n_bins, learning_rate=0.1, lambda
     pred = [F32(base)] * n
     feat, thr, thr_bin = [], [], []
     leafval = [F32(0)] * (n_trees * leaves)
+    leafvar = [F32(0)] * (n_trees * leaves)  # PGBM (exact mode)
     fi_gain = [F32(0)] * nf
     fi_count = [F32(0)] * nf
     stride = 1
@@ -278,6 +279,22 @@ def train(x, y, cuts, base, *, n_trees, depth, n_bins, learning_rate=0.1, lambda
                 sh[node[r]] += wquantize(h[r], wh)
             lg = [math.ldexp(float(v), -wg) for v in sg]
             lc = [math.ldexp(float(v), -wh) for v in sh]
+            if pgbm:
+                # gpu_kernels.rs:1015-1080: per-leaf sum of g*g (f32 products); the wide
+                # scale comes from (max |g|)^2 in f32, which bounds every product
+                m2 = F32(mg * mg)
+                if not np.isfinite(m2):
+                    m2 = np.finfo(np.float32).max
+                w2 = wscale_exp(m2, n)
+                s2 = [0] * leaves
+                for r in samp:
+                    s2[node[r]] += wquantize(F32(g[r] * g[r]), w2)
+                for l in range(leaves):
+                    G, H, S2 = lg[l], lc[l], math.ldexp(float(s2[l]), -w2)
+                    if H > 1.0:
+                        m = G / H
+                        v = S2 / H - m * m
+                        leafvar[t * leaves + l] = F32(lr * lr * (v if v > 0.0 else 0.0))
         else:
             m = len(samp)
             chunk = -(-m // n_threads)
@@ -298,6 +315,7 @@ def train(x, y, cuts, base, *, n_trees, depth, n_bins, learning_rate=0.1, lambda
             pred[r] = F32(pred[r] + leafval[t * leaves + node[r]])
     return dict(feat=np.array(feat, np.uint32), thr=np.array(thr, np.float32),
                 thr_bin=np.array(thr_bin, np.uint32), leafval=np.array(leafval, np.float32),
+                leafvar=np.array(leafvar, np.float32),
                 fi_gain=np.array(fi_gain, np.float32), fi_count=np.array(fi_count, np.float32))
 
 

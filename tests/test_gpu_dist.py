@@ -61,13 +61,13 @@ def _bounds(n, world, seed):
     return [0] + [int(c) for c in cuts] + [n]
 
 
-def _oracle(case, x, y, cuts, base):
+def _oracle(case, x, y, cuts, base, pgbm=False):
     cfg = _cfg(case)
     return oracle.train(x, y, cuts, base, n_trees=cfg.n_trees, depth=cfg.depth,
                         n_bins=cfg.n_bins, learning_rate=cfg.learning_rate, lambda_=cfg.lambda_,
                         min_child_h=cfg.min_child_h, subsample=cfg.subsample,
                         goss_top=cfg.goss_top, goss_other=cfg.goss_other,
-                        objective=cfg.objective, exact=True, n_threads=4)
+                        objective=cfg.objective, exact=True, n_threads=4, pgbm=pgbm)
 
 
 def _assert_model(m, o, who):
@@ -164,13 +164,15 @@ def _in_process_main(world, case, q):
         T, D = cfg.n_trees, cfg.depth
         out = dict(feat=np.zeros(T * D, np.uint32), thr=np.zeros(T * D, np.float32),
                    thr_bin=np.zeros(T * D, np.uint16), leafval=np.zeros(T << D, np.float32),
+                   leafvar=np.zeros(T << D, np.float32),  # PGBM variances (every rank)
                    fi_gain=np.zeros(nf, np.float32), fi_count=np.zeros(nf, np.float32))
         p = train_params(cfg)
         p.pack4 = int(case.get("pack4", False))
         ctx.check(N.lib.rw_fit(ctx.h, C.byref(p), N.ptr(x), N.ptr(y), n, nf, N.ptr(cuts),
                                float(base),
-                               *(N.ptr(out[k]) for k in ("feat", "thr", "thr_bin", "leafval")),
-                               None, N.ptr(out["fi_gain"]), N.ptr(out["fi_count"]), None))
+                               *(N.ptr(out[k]) for k in ("feat", "thr", "thr_bin", "leafval",
+                                                         "leafvar")),
+                               N.ptr(out["fi_gain"]), N.ptr(out["fi_count"]), None))
         # scoring through the same context (row shards over the GPUs)
         b = rb.Booster(cfg, ctx)
         b.n_features, b.base_score = nf, np.float32(base)
@@ -197,7 +199,8 @@ IN_PROCESS_CASES = [CASES[0], CASES[1], CASES[3]]
 @pytest.mark.parametrize("case", IN_PROCESS_CASES, ids=[c["id"] for c in IN_PROCESS_CASES])
 def test_one_context_over_several_gpus_matches_oracle_exact(case, world):
     """rw_ctx_create(gpu_ids, world): the single-process Booster trains and scores on
-    several GPUs and gets the 1-GPU oracle_exact model bit for bit."""
+    several GPUs and gets the 1-GPU oracle_exact model bit for bit, PGBM leaf variances
+    included (their g^2 sums take a second exchange)."""
     if _n_gpus() < world:
         pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
@@ -213,8 +216,9 @@ def test_one_context_over_several_gpus_matches_oracle_exact(case, world):
             p.join()
     assert status == "ok", res
     x, y = _case_data(case)
-    o = _oracle(case, x, y, res["cuts"], float(res["base"]))
+    o = _oracle(case, x, y, res["cuts"], float(res["base"]), pgbm=True)
     _assert_model(res, o, f"{world}-GPU context")
+    np.testing.assert_array_equal(res["leafvar"].view(np.uint32), o.leafvar.view(np.uint32))
     cfg = _cfg(case)
     want = oracle.predict(np.ascontiguousarray(x[:50_007]), o.feat, o.thr, o.leafval,
                           float(res["base"]), cfg.n_trees, cfg.depth)

@@ -250,6 +250,6 @@ def test_errors_are_reported(ctx):
         fit_dataset(ds, rb.Config(n_trees=1, depth=4, n_bins=32), 0.0)
     assert ei.value.code == -1
     with pytest.raises(N.RwError) as ei:
-        fit_dataset(ds, rb.Config(n_trees=1, depth=4, n_bins=64, pgbm=True), 0.0)
+        fit_dataset(ds, rb.Config(n_trees=1, depth=4, n_bins=64, clamp_hessian=0.5), 0.0)
     assert ei.value.code == -5
     ds.close()

@@ -56,6 +56,25 @@ def test_oracle_matches_python_restatement(exact, nt, obj, subtract):
         np.testing.assert_array_equal(a[k].view(np.uint32), getattr(b, k).view(np.uint32))
 
 
+@pytest.mark.parametrize("obj,subsample", [("logistic", 1.0), ("l2", 0.5)])
+def test_pgbm_leaf_variances_match_python_restatement(obj, subsample):
+    """PGBM leaf variances (gpu_kernels.rs:1015-1080) from exact sums: the C oracle and the
+    Python restatement agree bit for bit, and the margins' leaf values are unchanged."""
+    rng = np.random.default_rng(5)
+    n, nf, nb = 300, 3, 9
+    x = rng.standard_normal((n, nf)).astype(np.float32)
+    y = ((rng.random(n) < 0.4) if obj == "logistic" else 3 * rng.standard_normal(n)).astype(np.float32)
+    cuts = pyref.boundaries(x, nb)
+    base = np.float32(oracle.base_score(y, obj))
+    kw = dict(n_trees=3, depth=3, n_bins=nb, learning_rate=0.3, objective=obj, subsample=subsample)
+    a = pyref.train(x, y, cuts, base, exact=True, pgbm=True, **kw)
+    b = oracle.train(x, y, cuts, float(base), exact=True, pgbm=True, **kw)
+    c = oracle.train(x, y, cuts, float(base), exact=True, **kw)
+    np.testing.assert_array_equal(a["leafvar"].view(np.uint32), b.leafvar.view(np.uint32))
+    np.testing.assert_array_equal(b.leafval.view(np.uint32), c.leafval.view(np.uint32))
+    assert (b.leafvar >= 0).all() and (b.leafvar > 0).any()
+
+
 def test_kat_shared_memory_spike():
     """src/main.rs:27-47: 256 rows with bins i % 16 and unit weight give 16 per bin."""
     n = 256
