@@ -196,12 +196,13 @@ def _raw_twin(bins, feat, thr_bin, nf, seed):
 
 @pytest.mark.parametrize("depth,trees,nf,n", [
     (1, 7, 3, 1), (4, 100, 20, 4097), (6, 500, 54, 2049), (8, 1200, 10, 5000),
-    (10, 50, 30, 3000), (6, 64, 120, 2000),
+    (10, 50, 30, 3000), (6, 64, 120, 2000), (6, 500, 54, 4100), (3, 33, 5, 1028),
+    (6, 251, 54, 4096), (7, 300, 64, 8200),
 ])
 def test_predict_u8_shapes(ctx, depth, trees, nf, n):
     """The u8 scorers (tiled shared-memory kernel for depth <= 8 with tree chunks, the
-    older byte-SIMD kernel for wide rows, the scalar kernel for depth > 8) against
-    predict_cpu on the raw-threshold twin of the same model."""
+    older byte-SIMD kernel for wide rows, the scalar kernel for depth > 8 or a row stride
+    not a multiple of 4) against predict_cpu on the raw-threshold twin of the same model."""
     feat, thr_bin, leafval = synth.c5_model(n_trees=trees, depth=depth, nf=nf, seed=depth)
     bins = synth.c5_bins(n, nf, seed=depth + 1)
     x, thr = _raw_twin(bins, feat, thr_bin, nf, seed=depth + 2)
