@@ -132,9 +132,11 @@ class Dataset:
         return out
 
     def close(self):
-        if self.h:
+        # a dataset lives in its context's memory pool: once the context is destroyed the
+        # dataset's memory is gone with it and the handle must not be used again
+        if self.h and self.ctx.h:
             N.lib.rw_dataset_destroy(self.h)
-            self.h = None
+        self.h = None
 
     def __del__(self):
         try:

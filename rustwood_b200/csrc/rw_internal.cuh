@@ -73,6 +73,14 @@ struct rw_ctx {
   // (the context rw_ctx_create returned for several GPUs; it owns no stream itself)
   std::shared_ptr<RankGroup> group;
   std::vector<rw_ctx*> members;
+  // Large pageable host inputs are copied through pinned slots (two per worker thread,
+  // created on first use): the workers' memcpy into one slot overlaps the copy engine's
+  // drain of the other. See upload_h2d.
+  static constexpr int kStageWorkers = 4;
+  void* stage_host[2 * kStageWorkers] = {};
+  cudaEvent_t stage_ev[2 * kStageWorkers] = {};
+  bool stage_used[2 * kStageWorkers] = {};
+  cudaStream_t stage_stream[kStageWorkers] = {};
 };
 
 // Bins are stored twice in HBM:

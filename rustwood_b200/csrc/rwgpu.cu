@@ -669,6 +669,12 @@ extern "C" void rw_ctx_destroy(rw_ctx* ctx) {
     }
   }
   sym_close(ctx);
+  for (int i = 0; i < 2 * rw_ctx::kStageWorkers; i++) {
+    if (ctx->stage_ev[i]) cudaEventDestroy(ctx->stage_ev[i]);
+    if (ctx->stage_host[i]) cudaFreeHost(ctx->stage_host[i]);
+  }
+  for (int w = 0; w < rw_ctx::kStageWorkers; w++)
+    if (ctx->stage_stream[w]) cudaStreamDestroy(ctx->stage_stream[w]);
   if (ctx->comm) ncclCommDestroy(ctx->comm);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
   if (ctx->pool) cudaMemPoolDestroy(ctx->pool);
@@ -696,6 +702,86 @@ extern "C" int rw_ctx_set_timeout(rw_ctx* ctx, int64_t ms) {
   ctx->timeout_ms = ms;
   for (auto* c : ctx->members) c->timeout_ms = ms;
   return RW_OK;
+}
+
+// =================================================================================
+// host-to-device uploads
+
+constexpr size_t kStageSlot = 8u << 20;       // bytes per pinned slot
+constexpr size_t kStageMin = 32u << 20;       // smaller pageable copies go to the driver
+
+// Copies `bytes` of host memory at src to the device at dst, ordered on the context
+// stream like cudaMemcpyAsync, and like it from pageable memory: src has been read when
+// the call returns. Pinned or registered sources (and copies under kStageMin) go straight
+// to the copy engine. A large pageable source is split into kStageSlot chunks dealt
+// round-robin to kStageWorkers host threads; each worker copies its chunk into one of its
+// two pinned slots (after the slot's previous transfer has drained) and queues the
+// transfer on its own stream, so host copies by several cores overlap the copy engine.
+// The destination's allocation is ordered before the workers' transfers, and the context
+// stream waits for all of them.
+static cudaError_t upload_h2d(rw_ctx* ctx, void* dst, const void* src, size_t bytes) {
+  cudaPointerAttributes at;
+  bool pageable = true;
+  if (cudaPointerGetAttributes(&at, src) == cudaSuccess) pageable = at.type == cudaMemoryTypeUnregistered;
+  else cudaGetLastError();  // clear: plain host pointers are pageable
+  if (!pageable || bytes < kStageMin)
+    return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, ctx->stream);
+  constexpr int W = rw_ctx::kStageWorkers;
+  cudaError_t e = cudaSuccess;
+  for (int w = 0; w < W && e == cudaSuccess; w++)
+    if (!ctx->stage_stream[w]) e = cudaStreamCreateWithFlags(&ctx->stage_stream[w], cudaStreamNonBlocking);
+  for (int i = 0; i < 2 * W && e == cudaSuccess; i++) {
+    if (!ctx->stage_host[i]) e = cudaMallocHost(&ctx->stage_host[i], kStageSlot);
+    if (e == cudaSuccess && !ctx->stage_ev[i])
+      e = cudaEventCreateWithFlags(&ctx->stage_ev[i], cudaEventDisableTiming);
+  }
+  if (e != cudaSuccess) return e;
+  // the destination (a stream-ordered allocation) before any worker transfer
+  cudaEvent_t ready = nullptr;
+  e = cudaEventCreateWithFlags(&ready, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventRecord(ready, ctx->stream);
+  for (int w = 0; w < W && e == cudaSuccess; w++)
+    e = cudaStreamWaitEvent(ctx->stage_stream[w], ready, 0);
+  if (e != cudaSuccess) {
+    if (ready) cudaEventDestroy(ready);
+    return e;
+  }
+  const size_t chunks = (bytes + kStageSlot - 1) / kStageSlot;
+  cudaError_t err[W];
+  int last_slot[W];
+  auto work = [&](int w) {
+    cudaError_t r = cudaSetDevice(ctx->device);
+    last_slot[w] = -1;
+    int j = 0;
+    for (size_t k = (size_t)w; k < chunks && r == cudaSuccess; k += W, j ^= 1) {
+      const int slot = 2 * w + j;
+      const size_t off = k * kStageSlot, len = std::min(kStageSlot, bytes - off);
+      if (ctx->stage_used[slot]) r = cudaEventSynchronize(ctx->stage_ev[slot]);
+      if (r != cudaSuccess) break;
+      memcpy(ctx->stage_host[slot], static_cast<const char*>(src) + off, len);
+      r = cudaMemcpyAsync(static_cast<char*>(dst) + off, ctx->stage_host[slot], len,
+                          cudaMemcpyHostToDevice, ctx->stage_stream[w]);
+      if (r == cudaSuccess) r = cudaEventRecord(ctx->stage_ev[slot], ctx->stage_stream[w]);
+      if (r == cudaSuccess) {
+        ctx->stage_used[slot] = true;
+        last_slot[w] = slot;
+      }
+    }
+    err[w] = r;
+  };
+  std::vector<std::thread> th;
+  for (int w = 1; w < W; w++) th.emplace_back(work, w);
+  work(0);
+  for (auto& t : th) t.join();
+  cudaSetDevice(ctx->device);
+  cudaEventDestroy(ready);
+  for (int w = 0; w < W; w++)
+    if (err[w] != cudaSuccess) return err[w];
+  // the context stream waits for every worker's last transfer (a stream's last event
+  // follows all its earlier work)
+  for (int w = 0; w < W && e == cudaSuccess; w++)
+    if (last_slot[w] >= 0) e = cudaStreamWaitEvent(ctx->stream, ctx->stage_ev[last_slot[w]], 0);
+  return e;
 }
 
 // =================================================================================
@@ -850,8 +936,7 @@ extern "C" int rw_dataset_create(rw_ctx* ctx, const float* x, const float* y, ui
   RW_CU(ctx, cudaSetDevice(ctx->device));
   DBuf<float> dx;
   RW_CU(ctx, dx.alloc(ctx, (size_t)n * nf));
-  RW_CU(ctx, cudaMemcpyAsync(dx.p, x, (size_t)n * nf * sizeof(float), cudaMemcpyHostToDevice,
-                             ctx->stream));
+  RW_CU(ctx, upload_h2d(ctx, dx.p, x, (size_t)n * nf * sizeof(float)));
   return dataset_build(ctx, dx.p, y, false, n, nf, cuts, n_bins, pack4, n_global, row_offset,
                        out);
 }
@@ -1556,7 +1641,7 @@ extern "C" int rw_predict_f32(rw_ctx* ctx, const rw_model* m, const float* x, ui
   cudaError_t e = dx.alloc((size_t)n * nf);
   if (e == cudaSuccess) e = dout.alloc(n);
   if (e == cudaSuccess)
-    e = cudaMemcpyAsync(dx.p, x, (size_t)n * nf * 4, cudaMemcpyHostToDevice, ctx->stream);
+    e = upload_h2d(ctx, dx.p, x, (size_t)n * nf * 4);
   if (e != cudaSuccess) {
     rw_model_free(dm);
     return cuda_fail(ctx, e, "predict upload");
@@ -1703,7 +1788,7 @@ extern "C" int rw_fit_with_boundaries(rw_ctx* ctx, const rw_train_params* p, con
     // one upload of x serves the sample and the binning
     DBuf<float> dx;
     RW_CU(ctx, dx.alloc(ctx, (size_t)n * nf));
-    RW_CU(ctx, cudaMemcpyAsync(dx.p, x, (size_t)n * nf * 4, cudaMemcpyHostToDevice, ctx->stream));
+    RW_CU(ctx, upload_h2d(ctx, dx.p, x, (size_t)n * nf * 4));
     int rc = rw_compute_boundaries_device(ctx, dx.p, n, nf, p->n_bins, sample, unique,
                                           cuts.data());
     if (rc) return rc;

@@ -193,16 +193,6 @@ __device__ void block_exclusive_scan_vals(const uint32_t (&v)[4], uint32_t n, ui
   __syncthreads();
 }
 
-// The same over in[0..n) (global, written by an earlier kernel).
-__device__ void block_exclusive_scan(const uint32_t* in, uint32_t n, uint32_t* out,
-                                     uint32_t* warp_sums) {
-  const uint32_t per = (n + blockDim.x - 1) / blockDim.x, b0 = threadIdx.x * per;
-  uint32_t v[4];
-#pragma unroll
-  for (int k = 0; k < 4; k++) v[k] = (k < (int)per && b0 + k < n) ? __ldcg(in + b0 + k) : 0u;
-  block_exclusive_scan_vals(v, n, out, warp_sums);
-}
-
 // Exclusive prefixes of two arrays at once: in_k[0..n_k) (n_k <= 4 * blockDim.x, global,
 // written by an earlier kernel) into out_k[0..n_k], out_k[n_k] = the total. Both arrays'
 // loads are issued together and share the block barriers. warp_sums has 66 words. All

@@ -113,6 +113,27 @@ def test_level_hist_matches_oracle(ctx, nf, nb, groups, odd, packed):
     np.testing.assert_array_equal(got, want)
 
 
+def test_large_pageable_inputs_upload_exactly(ctx):
+    """Pageable host inputs of 32 MiB and more take the library's staged upload (pinned
+    slots filled by several host threads, chunks not a multiple of the slot): the binned
+    dataset and the margins equal the host restatements bit for bit."""
+    x, y, _, _ = synth.c2(170_003)  # 36.7 MB of f32 rows
+    cuts = rb.compute_boundaries(x, 255)
+    cfg = rb.Config(n_trees=3, depth=4, n_bins=255)
+    base = rb.base_score(y, cfg.objective)
+    ds = Dataset(ctx, x, y, cuts, 255)
+    try:
+        np.testing.assert_array_equal(ds.bins(), oracle.bin_rowmajor(x, cuts, 255).T)
+        r = fit_dataset(ds, cfg, base)
+    finally:
+        ds.close()
+    b = rb.Booster(cfg, ctx)
+    b.n_features, b.base_score = x.shape[1], np.float32(base)
+    b._take(r)
+    want = oracle.predict(x, r.feat, r.thr, r.leafval, base, cfg.n_trees, cfg.depth)
+    np.testing.assert_array_equal(b.predict(x).view(np.uint32), want.view(np.uint32))
+
+
 CASES = {
     "c1": dict(data=lambda: synth.c1(30_000), cfg=dict(n_trees=25, depth=6, n_bins=255,
                                                          learning_rate=0.2)),
