@@ -62,7 +62,7 @@ constexpr uint32_t kMaxRowsPerCta = 1u << (30 - RW_QBITS);
 static_assert(kMaxRowsPerCta >= 1024, "quantisation too fine for the histogram row bound");
 // A listed level gathers its rows through a ring of kListSlots shared-memory slots of
 // kListRows rows: the rows' list entries (row id, q) and their bin runs (cp.async 16-byte
-// copies, one per thread), issued two slots ahead of the slot being accumulated.
+// copies, one per thread), issued kListSlots - 1 slots ahead of the slot being accumulated.
 constexpr uint32_t kListRows = 256;
 constexpr int kListSlots = 3;
 static_assert(kListRows * 4 == kHistThreads, "one 16-byte bin chunk per thread per slot");
@@ -464,16 +464,17 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(HistLaunch a, uint32_t ft
               live ? e : make_int4(0, 0, 0, 0);
         cp_async_commit();
       };
-      int4 e_next = load_entry(0);
-      if (nsl > 0) issue(0, e_next);
-      else cp_async_commit();
-      e_next = load_entry(1);
-      if (nsl > 1) issue(1, e_next);
-      else cp_async_commit();
-      e_next = load_entry(2);
+      int4 e_next;
+#pragma unroll
+      for (uint32_t k = 0; k + 1 < (uint32_t)kListSlots; k++) {
+        e_next = load_entry(k);
+        if (k < nsl) issue(k, e_next);
+        else cp_async_commit();
+      }
+      e_next = load_entry(kListSlots - 1);
       for (uint32_t j = 0; j < nsl; j++) {
-        cp_async_wait<1>();  // this thread's copies for slot j have landed
-        __syncthreads();     // ... and everyone else's
+        cp_async_wait<kListSlots - 2>();  // this thread's copies for slot j have landed
+        __syncthreads();                  // ... and everyone else's
         const unsigned char* sp = stage0 + (size_t)(j % kListSlots) * kSlotBytes;
         const int4* se = reinterpret_cast<const int4*>(sp + kListRows * TB);
         const uint32_t here = min(kListRows, cnt - j * kListRows);
@@ -487,9 +488,9 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(HistLaunch a, uint32_t ft
           hist_add_row<PACKED>(hs, bb, make_int2(e.y, e.z), lane, v0, v1, nb);
         }
         __syncthreads();  // slot j is free again
-        if (j + 2 < nsl) issue(j + 2, e_next);
+        if (j + kListSlots - 1 < nsl) issue(j + kListSlots - 1, e_next);
         else cp_async_commit();
-        e_next = load_entry(j + 3);
+        e_next = load_entry(j + kListSlots);
       }
       cp_async_wait<0>();
     }
