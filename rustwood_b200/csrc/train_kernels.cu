@@ -63,12 +63,19 @@ static_assert(kMaxRowsPerCta >= 1024, "quantisation too fine for the histogram r
 // A listed level gathers its rows through a ring of kListSlots shared-memory slots of
 // kListRows rows: the rows' list entries (row id, q) and their bin runs (cp.async 16-byte
 // copies, one per thread), issued kListSlots - 1 slots ahead of the slot being accumulated.
-constexpr uint32_t kListRows = 256;
+#ifndef RW_LIST_ROWS
+#define RW_LIST_ROWS 256
+#endif
+#ifndef RW_STREAM_ROWS
+#define RW_STREAM_ROWS 512
+#endif
+constexpr uint32_t kListRows = RW_LIST_ROWS;
 constexpr int kListSlots = 3;
-static_assert(kListRows * 4 == kHistThreads, "one 16-byte bin chunk per thread per slot");
+static_assert(kListRows * 4 <= kHistThreads && kListRows % (kHistThreads / 32) == 0,
+              "at most one 16-byte bin chunk per thread per slot, whole rows per warp");
 // The all-rows level streams its rows through shared memory in stages of kStreamRows
 // (one TMA bulk copy of the stage's bin rows and one of its q values), kStreamStages deep.
-constexpr uint32_t kStreamRows = 512;
+constexpr uint32_t kStreamRows = RW_STREAM_ROWS;
 constexpr int kStreamStages = 2;
 constexpr uint32_t kStreamRowsPerWarp = kStreamRows / (kHistThreads / 32);
 static_assert(kStreamRows % (kHistThreads / 32) == 0, "whole rows per warp per stage");
@@ -448,18 +455,19 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(HistLaunch a, uint32_t ft
       const uint32_t my_row = threadIdx.x / 4, my_part = threadIdx.x % 4;
       auto load_entry = [&](uint32_t j) {  // this thread's entry of slot j (row my_row)
         const uint32_t li = j * kListRows + my_row;
-        return li < cnt && ebase + li < a.n_pad ? __ldcg(a.entries + ebase + li)
-                                                : make_int4(0, 0, 0, 0);
+        return my_row < kListRows && li < cnt && ebase + li < a.n_pad
+                   ? __ldcg(a.entries + ebase + li)
+                   : make_int4(0, 0, 0, 0);
       };
       auto issue = [&](uint32_t j, int4 e) {
         unsigned char* sp = stage0 + (size_t)(j % kListSlots) * kSlotBytes;
         // rows outside the table never reach memory (defensive: lists hold rows < n_pad)
         const bool live = j * kListRows + my_row < cnt && (uint32_t)e.x < a.n_pad;
-        if (my_part * 16 < TB)
+        if (my_row < kListRows && my_part * 16 < TB)
           cp_async16(sp + my_row * TB + my_part * 16,
                      tile + (size_t)(live ? (uint32_t)e.x : 0u) * TB + my_part * 16,
                      live ? 16u : 0u);
-        if (my_part == 0)
+        if (my_row < kListRows && my_part == 0)
           reinterpret_cast<int4*>(sp + kListRows * TB)[my_row] =
               live ? e : make_int4(0, 0, 0, 0);
         cp_async_commit();
