@@ -230,6 +230,33 @@ int rw_predict_f32_device(rw_ctx* ctx, const rw_dmodel* dm, const float* d_x, ui
 int rw_predict_f32_noalloc(rw_ctx* ctx, const rw_model* m, const float* x_rowmajor,
                            uint64_t n, uint32_t nf, float* out);
 
+/* ---- categorical target encoding on the GPU ----------------------------------- */
+
+/* encoding.rs fit_transform_train (src/encoding.rs:44-95): every categorical column of the
+ * row-major rows becomes its smoothed out-of-fold target mean (folds = row index mod
+ * max(k_folds, 2)); gmean_out receives the global label mean and enc_out (nullable) the
+ * test-set maps (free with rw_encoders_free). The sums are exact fixed-point integers, so
+ * the values equal the reference's sequential f64 sums wherever those are exact (0/1 or
+ * small integer labels; see DESIGN). RW_ERR_UNSUPPORTED when a feature's key range is too
+ * wide for dense tables (more than 2^26 keys over all features): encode on the host.
+ * rw_target_encode_device works on device rows and labels in place; rw_target_encode
+ * takes host buffers and writes the encoded rows back into x_rowmajor. */
+typedef struct rw_encoders rw_encoders;
+int rw_target_encode_device(rw_ctx* ctx, float* d_x, const float* d_y, uint64_t n, uint32_t nf,
+                            const uint32_t* categorical, uint32_t n_cat, float smoothing,
+                            uint32_t k_folds, uint64_t hash_buckets, float* gmean_out,
+                            rw_encoders** enc_out);
+int rw_target_encode(rw_ctx* ctx, float* x_rowmajor, const float* y, uint64_t n, uint32_t nf,
+                     const uint32_t* categorical, uint32_t n_cat, float smoothing,
+                     uint32_t k_folds, uint64_t hash_buckets, float* gmean_out,
+                     rw_encoders** enc_out);
+/* Feature i's map: keys key_lo .. key_lo + n_keys - 1; value[j] holds key_lo + j's encoded
+ * value where present[j] != 0 (unseen keys take gmean, src/encoding.rs:99-115). The
+ * pointers stay valid until rw_encoders_free. */
+int rw_encoders_table(const rw_encoders* enc, uint32_t i, int64_t* key_lo, uint64_t* n_keys,
+                      const float** value, const uint8_t** present);
+void rw_encoders_free(rw_encoders* enc);
+
 /* ---- host helpers kept from the reference host code --------------------------- */
 
 /* compute_boundaries (src/data.rs:86-146): out[nf*(n_bins-1)]. */

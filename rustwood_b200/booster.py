@@ -82,6 +82,36 @@ def train_params(cfg: Config) -> N.TrainParams:
     return p
 
 
+def target_encode_gpu(ctx: "Context", x: np.ndarray, y: np.ndarray, categorical, smoothing: float,
+                      k_folds: int = 5, hash_buckets: int = 0):
+    """encoding.fit_transform_train on the GPU (rw_target_encode): x (row-major float32,
+    C-contiguous) is encoded in place; returns (encoders, gmean) like the host version,
+    encoders[i] a dict code -> float32. Raises N.RwError (code RW_ERR_UNSUPPORTED) when a
+    feature's key range is too wide for the GPU's dense tables."""
+    assert x.dtype == np.float32 and x.flags.c_contiguous
+    y = N.f32c(y)
+    cat = np.ascontiguousarray(categorical, np.uint32)
+    gmean = C.c_float()
+    enc = C.c_void_p()
+    n, nf = x.shape
+    ctx.check(N.lib.rw_target_encode(ctx.h, N.ptr(x), N.ptr(y), n, nf, N.ptr(cat), len(cat),
+                                     float(smoothing), int(k_folds), int(hash_buckets),
+                                     C.byref(gmean), C.byref(enc)))
+    encoders = []
+    try:
+        for i in range(len(cat)):
+            lo, nk = C.c_int64(), C.c_uint64()
+            val, pres = C.POINTER(C.c_float)(), C.POINTER(C.c_uint8)()
+            N.lib.rw_encoders_table(enc, i, C.byref(lo), C.byref(nk), C.byref(val), C.byref(pres))
+            v = np.ctypeslib.as_array(val, (nk.value,)).copy() if nk.value else np.zeros(0, np.float32)
+            pr = np.ctypeslib.as_array(pres, (nk.value,)).copy() if nk.value else np.zeros(0, np.uint8)
+            idx = np.nonzero(pr)[0]
+            encoders.append({int(lo.value + j): np.float32(v[j]) for j in idx})
+    finally:
+        N.lib.rw_encoders_free(enc)
+    return encoders, np.float32(gmean.value)
+
+
 def compute_boundaries(x: np.ndarray, n_bins: int, sample: int = 200_000,
                        unique: bool = False) -> np.ndarray:
     """src/data.rs:86-146 (native)."""
@@ -209,8 +239,17 @@ class Booster:
         x = np.array(x, dtype=np.float32, order="C", copy=True)
         y = N.f32c(y)
         if cfg.categorical:
-            self.encoders, self.gmean = encoding.fit_transform_train(
-                x, y, cfg.categorical, cfg.te_smoothing, 5, cfg.cat_hash_buckets)
+            # on the GPU (exact fixed-point sums); the host restatement when there is no
+            # GPU or the key range is too wide for the GPU's dense tables
+            try:
+                self.encoders, self.gmean = target_encode_gpu(
+                    self.ctx, x, y, cfg.categorical, cfg.te_smoothing, 5, cfg.cat_hash_buckets)
+            except N.RwError as e:
+                if e.code == N.RW_ERR_UNSUPPORTED or self._ctx is None:
+                    self.encoders, self.gmean = encoding.fit_transform_train(
+                        x, y, cfg.categorical, cfg.te_smoothing, 5, cfg.cat_hash_buckets)
+                else:
+                    raise
         cuts = compute_boundaries(x, cfg.n_bins, cfg.bin_sample, cfg.unique_bins)
         return x, cuts, base_score(y, cfg.objective)
 

@@ -16,7 +16,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "librwgpu.so")
 SOURCES = ["rwgpu.cu", "train_kernels.cu", "predict_kernels.cu", "noalloc.cu", "peer_kernels.cu",
-           "boundaries.cu"]
+           "boundaries.cu", "encode.cu"]
 HEADERS = ["rw_internal.cuh", "rw_expf.h", os.path.join("..", "..", "include", "rwgpu.h")]
 
 

@@ -235,6 +235,21 @@ struct LeafValues {
   float* leafvar = nullptr;  // PGBM out: the tree's slot of the leaf variances (with leafsum2)
 };
 cudaError_t launch_leafval(const LeafValues& a, cudaStream_t s, int* nl);
+// Target encoding on the GPU (encode.cu): the test-set maps of the categorical features,
+// as dense tables over each feature's key range.
+struct rw_encoders {
+  std::vector<long long> key_lo;   // [n_cat] first key of each feature's table
+  std::vector<uint64_t> koff;      // [n_cat] first slot of each feature in value/present
+  std::vector<uint64_t> n_keys;    // [n_cat] slots per feature
+  std::vector<float> value;        // smoothed full-train mean per key
+  std::vector<uint8_t> present;    // key seen in training
+  float gmean = 0.0f;
+};
+int target_encode_device(rw_ctx* ctx, float* d_x, const float* d_y, uint64_t n, uint32_t nf,
+                         const uint32_t* cat, uint32_t n_cat, float smoothing, uint32_t k_folds,
+                         uint64_t hash_buckets, float* gmean_out, rw_encoders* enc,
+                         std::string* why);
+
 // PGBM: every row's g^2 (f32) in the wide fixed point into its leaf's exact int64 sum
 // (the leaf_g2 sums of gpu_kernels.rs:1015-1043); run after the tree's last level.
 struct LeafSquares {

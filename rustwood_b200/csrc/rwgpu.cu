@@ -785,6 +785,66 @@ static cudaError_t upload_h2d(rw_ctx* ctx, void* dst, const void* src, size_t by
 }
 
 // =================================================================================
+// categorical target encoding (encode.cu)
+
+static rw_ctx* first_rank(rw_ctx* ctx);
+
+extern "C" int rw_target_encode_device(rw_ctx* ctx, float* d_x, const float* d_y, uint64_t n,
+                                       uint32_t nf, const uint32_t* categorical, uint32_t n_cat,
+                                       float smoothing, uint32_t k_folds, uint64_t hash_buckets,
+                                       float* gmean_out, rw_encoders** enc_out) {
+  if (!ctx) return fail(nullptr, RW_ERR_ARG, "context is NULL");
+  rw_ctx* c = first_rank(ctx);
+  if (!d_x || !d_y || (n_cat && !categorical) || n == 0 || nf == 0)
+    return fail(ctx, RW_ERR_ARG, "bad target-encoding arguments");
+  if (enc_out) *enc_out = nullptr;
+  RW_CU(c, cudaSetDevice(c->device));
+  auto* enc = enc_out ? new rw_encoders() : nullptr;
+  std::string why;
+  const int rc = target_encode_device(c, d_x, d_y, n, nf, categorical, n_cat, smoothing, k_folds,
+                                      hash_buckets, gmean_out, enc, &why);
+  if (rc) {
+    delete enc;
+    return fail(ctx, rc, why);
+  }
+  if (enc_out) *enc_out = enc;
+  return RW_OK;
+}
+
+extern "C" int rw_target_encode(rw_ctx* ctx, float* x, const float* y, uint64_t n, uint32_t nf,
+                                const uint32_t* categorical, uint32_t n_cat, float smoothing,
+                                uint32_t k_folds, uint64_t hash_buckets, float* gmean_out,
+                                rw_encoders** enc_out) {
+  if (!ctx) return fail(nullptr, RW_ERR_ARG, "context is NULL");
+  if (!x || !y || n == 0 || nf == 0) return fail(ctx, RW_ERR_ARG, "bad target-encoding arguments");
+  rw_ctx* c = first_rank(ctx);
+  RW_CU(c, cudaSetDevice(c->device));
+  DBuf<float> dx, dy;
+  RW_CU(c, dx.alloc((size_t)n * nf));
+  RW_CU(c, dy.alloc(n));
+  RW_CU(c, upload_h2d(c, dx.p, x, (size_t)n * nf * 4));
+  RW_CU(c, cudaMemcpyAsync(dy.p, y, n * 4, cudaMemcpyHostToDevice, c->stream));
+  int rc = rw_target_encode_device(ctx, dx.p, dy.p, n, nf, categorical, n_cat, smoothing,
+                                   k_folds, hash_buckets, gmean_out, enc_out);
+  if (rc) return rc;
+  RW_CU(c, cudaMemcpyAsync(x, dx.p, (size_t)n * nf * 4, cudaMemcpyDeviceToHost, c->stream));
+  RW_CU(c, cudaStreamSynchronize(c->stream));
+  return RW_OK;
+}
+
+extern "C" int rw_encoders_table(const rw_encoders* enc, uint32_t i, int64_t* key_lo,
+                                 uint64_t* n_keys, const float** value, const uint8_t** present) {
+  if (!enc || i >= enc->key_lo.size()) return RW_ERR_ARG;
+  if (key_lo) *key_lo = enc->key_lo[i];
+  if (n_keys) *n_keys = enc->n_keys[i];
+  if (value) *value = enc->value.data() + enc->koff[i];
+  if (present) *present = enc->present.data() + enc->koff[i];
+  return RW_OK;
+}
+
+extern "C" void rw_encoders_free(rw_encoders* enc) { delete enc; }
+
+// =================================================================================
 // datasets
 
 static int dataset_build(rw_ctx* ctx, const float* d_x, const float* y, bool y_on_device,

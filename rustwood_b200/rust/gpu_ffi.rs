@@ -31,6 +31,10 @@ pub struct rw_dataset {
 pub struct rw_dmodel {
     _p: [u8; 0],
 }
+#[repr(C)]
+pub struct rw_encoders {
+    _p: [u8; 0],
+}
 
 /// rw_train_params: the Config fields fit_inner reads (src/config.rs:19-88).
 #[repr(C)]
@@ -128,6 +132,17 @@ extern "C" {
                                   n: u64, nf: u32, out: *mut f32) -> c_int;
     pub fn rw_predict_var_f32(ctx: *mut rw_ctx, m: *const rw_model, leafvar: *const f32,
                               x_rowmajor: *const f32, n: u64, nf: u32, out: *mut f32) -> c_int;
+    pub fn rw_target_encode(ctx: *mut rw_ctx, x_rowmajor: *mut f32, y: *const f32, n: u64, nf: u32,
+                            categorical: *const u32, n_cat: u32, smoothing: f32, k_folds: u32,
+                            hash_buckets: u64, gmean_out: *mut f32,
+                            enc_out: *mut *mut rw_encoders) -> c_int;
+    pub fn rw_target_encode_device(ctx: *mut rw_ctx, d_x: *mut f32, d_y: *const f32, n: u64,
+                                   nf: u32, categorical: *const u32, n_cat: u32, smoothing: f32,
+                                   k_folds: u32, hash_buckets: u64, gmean_out: *mut f32,
+                                   enc_out: *mut *mut rw_encoders) -> c_int;
+    pub fn rw_encoders_table(enc: *const rw_encoders, i: u32, key_lo: *mut i64, n_keys: *mut u64,
+                             value: *mut *const f32, present: *mut *const u8) -> c_int;
+    pub fn rw_encoders_free(enc: *mut rw_encoders);
     pub fn rw_model_thr_bins(m: *const rw_model, cuts: *const f32, n_bins: u32,
                              thr_bin: *mut u16) -> c_int;
     pub fn rw_compute_boundaries_device(ctx: *mut rw_ctx, d_x: *const f32, n: u64, nf: u32,
