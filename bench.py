@@ -319,6 +319,25 @@ def run_other_configs(args, ctx, flush_l2, barrier):
         ds.close()
         line = {"rows": int(len(y)), "features": int(xe.shape[1]), "trees": cfg.n_trees,
                 "gpu_seconds_per_fit": statistics.mean(ts) / 1e3}
+        if cfg.categorical:
+            # target encoding (src/encoding.rs fit_transform_train): the library's GPU
+            # encoder through its public call (H2D, encode, D2H; wall clock, best of 3)
+            # beside the host restatement the Python mirror falls back to
+            from rustwood_b200 import encoding
+            from rustwood_b200.booster import target_encode_gpu
+            tg = []
+            for _ in range(3):
+                xg = np.array(x, np.float32, order="C", copy=True)
+                t0 = time.perf_counter()
+                target_encode_gpu(ctx, xg, y, cfg.categorical, cfg.te_smoothing, 5,
+                                  cfg.cat_hash_buckets)
+                tg.append(time.perf_counter() - t0)
+            xh = np.array(x, np.float32, order="C", copy=True)
+            t0 = time.perf_counter()
+            encoding.fit_transform_train(xh, y, cfg.categorical, cfg.te_smoothing, 5,
+                                         cfg.cat_hash_buckets)
+            line["target_encode_seconds"] = {"gpu_call": min(tg),
+                                             "host_python": time.perf_counter() - t0}
         if not args.no_cpu:
             import oracle
             nt = oracle.default_threads()
