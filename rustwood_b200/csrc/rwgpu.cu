@@ -776,7 +776,12 @@ static cudaError_t upload_h2d(rw_ctx* ctx, void* dst, const void* src, size_t by
   cudaSetDevice(ctx->device);
   cudaEventDestroy(ready);
   for (int w = 0; w < W; w++)
-    if (err[w] != cudaSuccess) return err[w];
+    if (err[w] != cudaSuccess) {
+      // transfers already queued must not outlive the caller's error path (which frees
+      // the destination on the context stream)
+      for (int v = 0; v < W; v++) cudaStreamSynchronize(ctx->stage_stream[v]);
+      return err[w];
+    }
   // the context stream waits for every worker's last transfer (a stream's last event
   // follows all its earlier work)
   for (int w = 0; w < W && e == cudaSuccess; w++)
