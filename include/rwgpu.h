@@ -237,7 +237,7 @@ int rw_predict_f32_noalloc(rw_ctx* ctx, const rw_model* m, const float* x_rowmaj
  * max(k_folds, 2)); gmean_out receives the global label mean and enc_out (nullable) the
  * test-set maps (free with rw_encoders_free). The sums are exact fixed-point integers, so
  * the values equal the reference's sequential f64 sums wherever those are exact (0/1 or
- * small integer labels; see DESIGN). RW_ERR_UNSUPPORTED when a feature's key range is too
+ * small integer labels: no partial sum rounds). RW_ERR_UNSUPPORTED when a feature's key range is too
  * wide for dense tables (more than 2^26 keys over all features): encode on the host.
  * rw_target_encode_device works on device rows and labels in place; rw_target_encode
  * takes host buffers and writes the encoded rows back into x_rowmajor. */
