@@ -3,12 +3,14 @@
 //! Drop-in for rustwood's src/ as `src/gpu_ffi.rs` (with `mod gpu_ffi;` in main.rs and
 //! the `build.rs` beside this file). It replaces the cuda-oxide module loading and kernel
 //! launches of `Booster::fit_inner` (src/booster.rs:227-517) and `Booster::predict`
-//! (src/booster.rs:531-555); the host prep before them (target encoding,
-//! `compute_boundaries`, base score) stays in Rust and feeds the `cuts` and
-//! `base_score` arguments. Error codes become `Box<dyn Error>`, so `serve_handle` keeps
+//! (src/booster.rs:531-555); the host prep before them (`compute_boundaries`, base score)
+//! stays in Rust and feeds the `cuts` and `base_score` arguments, and target encoding can
+//! move to the GPU through `target_encode` below (same `Encoders` type as
+//! src/encoding.rs). Error codes become `Box<dyn Error>`, so `serve_handle` keeps
 //! printing `ERROR ...` lines (src/main.rs:406-409).
 #![allow(non_camel_case_types)]
 
+use std::collections::HashMap;
 use std::error::Error;
 use std::ffi::CStr;
 use std::os::raw::{c_char, c_int, c_void};
@@ -277,4 +279,38 @@ pub fn predict_std(ctx: &Context, n_trees: usize, depth: usize, n_features: usiz
                            n_features as u32, var.as_mut_ptr())
     })?;
     Ok(var.iter().map(|&v| v.max(0.0).sqrt()).collect())
+}
+
+/// `encoding::fit_transform_train` (src/encoding.rs:44-95) on the GPU: encodes the
+/// categorical columns of row-major `x` in place and returns `(encoders, gmean)` in the
+/// reference's types. Equal to the host function wherever its f64 sums are exact (0/1 or
+/// small integer labels); `RW_ERR_UNSUPPORTED` (key range too wide for the GPU's dense
+/// tables) means: call the host function instead.
+pub fn target_encode(ctx: &Context, x: &mut [f32], n: usize, nf: usize, y: &[f32],
+                     categorical: &[usize], smoothing: f32, k_folds: usize, hash_buckets: u64)
+                     -> Result<(Vec<HashMap<i64, f32>>, f32), Box<dyn Error>> {
+    assert_eq!(x.len(), n * nf);
+    let cat: Vec<u32> = categorical.iter().map(|&c| c as u32).collect();
+    let mut gmean = 0.0f32;
+    let mut enc: *mut rw_encoders = ptr::null_mut();
+    check(ctx.raw, unsafe {
+        rw_target_encode(ctx.raw, x.as_mut_ptr(), y.as_ptr(), n as u64, nf as u32, cat.as_ptr(),
+                         cat.len() as u32, smoothing, k_folds as u32, hash_buckets, &mut gmean,
+                         &mut enc)
+    })?;
+    let mut out = Vec::with_capacity(cat.len());
+    for i in 0..cat.len() {
+        let (mut lo, mut nk) = (0i64, 0u64);
+        let (mut val, mut pres): (*const f32, *const u8) = (ptr::null(), ptr::null());
+        unsafe { rw_encoders_table(enc, i as u32, &mut lo, &mut nk, &mut val, &mut pres) };
+        let mut m = HashMap::new();
+        for j in 0..nk as usize {
+            if unsafe { *pres.add(j) } != 0 {
+                m.insert(lo + j as i64, unsafe { *val.add(j) });
+            }
+        }
+        out.push(m);
+    }
+    unsafe { rw_encoders_free(enc) };
+    Ok((out, gmean))
 }
