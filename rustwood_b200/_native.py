@@ -93,6 +93,8 @@ def _load() -> C.CDLL:
         "rw_target_encode_device": (i32, [vp, vp, vp, u64, u32, vp, u32, f32, u32, u64, vp, vp]),
         "rw_encoders_table": (i32, [vp, u32, vp, vp, vp, vp]),
         "rw_encoders_free": (None, [vp]),
+        "rw_encoders_create": (i32, [u32, vp, vp, vp, vp, f32, vp]),
+        "rw_target_transform": (i32, [vp, vp, u64, u32, vp, u32, vp, u64]),
         "rw_compute_boundaries": (None, [vp, u64, u32, u32, u64, i32, vp]),
         "rw_base_score": (f32, [vp, u64, i32]),
         "rw_model_thr_bins": (i32, [P(Model), vp, u32, vp]),
@@ -121,7 +123,8 @@ EXPORTED = [
     "rw_dataset_destroy", "rw_dataset_bins", "rw_fit_dataset", "rw_fit", "rw_predict_f32",
     "rw_predict_u8", "rw_model_upload", "rw_model_free", "rw_predict_u8_device",
     "rw_predict_f32_device", "rw_predict_f32_noalloc", "rw_predict_var_f32",
-    "rw_target_encode", "rw_target_encode_device", "rw_encoders_table", "rw_encoders_free", "rw_compute_boundaries", "rw_base_score",
+    "rw_target_encode", "rw_target_encode_device", "rw_encoders_table", "rw_encoders_free",
+    "rw_encoders_create", "rw_target_transform", "rw_compute_boundaries", "rw_base_score",
     "rw_model_thr_bins", "rw_compute_boundaries_device", "rw_fit_with_boundaries",
     "rw_debug_level_hist", "rw_debug_expf", "rw_debug_binary_version", "rw_debug_level_step",
     "rw_debug_peer_wait", "rw_debug_lonely_rank_ctx", "rw_ctx_peer_failed",

@@ -112,6 +112,49 @@ def target_encode_gpu(ctx: "Context", x: np.ndarray, y: np.ndarray, categorical,
     return encoders, np.float32(gmean.value)
 
 
+def target_transform_gpu(ctx: "Context", x: np.ndarray, categorical, encoders, gmean,
+                         hash_buckets: int = 0, max_slots: int = 1 << 26) -> bool:
+    """encoding.transform on the GPU (rw_target_transform) from dense tables of the
+    encoders (dicts code -> float32): x (row-major float32, C-contiguous) is transformed in
+    place. Returns False, leaving x untouched, when the encoders' key ranges would need more
+    than max_slots table slots (the caller then uses the host transform)."""
+    assert x.dtype == np.float32 and x.flags.c_contiguous
+    lo, nk, tables = [], [], []
+    for m in encoders:
+        if m:
+            keys = np.fromiter(m.keys(), dtype=np.int64, count=len(m))
+            a, b = int(keys.min()), int(keys.max())
+            lo.append(a)
+            nk.append(b - a + 1)
+        else:
+            lo.append(0)
+            nk.append(0)
+        if sum(nk) > max_slots:
+            return False
+    value = np.zeros(sum(nk), np.float32)
+    present = np.zeros(sum(nk), np.uint8)
+    base = 0
+    for m, a, k in zip(encoders, lo, nk):
+        for key, v in m.items():
+            value[base + key - a] = v
+            present[base + key - a] = 1
+        base += k
+    lo_a, nk_a = np.asarray(lo, np.int64), np.asarray(nk, np.uint64)
+    cat = np.ascontiguousarray(categorical, np.uint32)
+    enc = C.c_void_p()
+    rc = N.lib.rw_encoders_create(len(cat), N.ptr(lo_a), N.ptr(nk_a), N.ptr(value),
+                                  N.ptr(present), float(gmean), C.byref(enc))
+    if rc != N.RW_OK:
+        raise N.RwError(rc, "rw_encoders_create")
+    try:
+        n, nf = x.shape
+        ctx.check(N.lib.rw_target_transform(ctx.h, N.ptr(x), n, nf, N.ptr(cat), len(cat), enc,
+                                            int(hash_buckets)))
+    finally:
+        N.lib.rw_encoders_free(enc)
+    return True
+
+
 def compute_boundaries(x: np.ndarray, n_bins: int, sample: int = 200_000,
                        unique: bool = False) -> np.ndarray:
     """src/data.rs:86-146 (native)."""
@@ -289,12 +332,20 @@ class Booster:
             m.thr_bin = keep[-1].ctypes.data_as(C.POINTER(C.c_uint16))
         return m, keep
 
+    def _encode_rows(self, x: np.ndarray) -> None:
+        """encoding::transform of new rows (src/encoding.rs:96-115), in place: on the GPU
+        from dense tables of the encoders (rw_target_transform), on the host when their
+        key range is too wide for dense tables."""
+        if not target_transform_gpu(self.ctx, x, self.cfg.categorical, self.encoders,
+                                    self.gmean, self.cfg.cat_hash_buckets):
+            encoding.transform(x, self.cfg.categorical, self.encoders, self.gmean,
+                               self.cfg.cat_hash_buckets)
+
     def predict(self, x: np.ndarray) -> np.ndarray:
         """Raw margins on the GPU (Booster::predict)."""
         x = np.array(x, dtype=np.float32, order="C", copy=bool(self.cfg.categorical))
         if self.cfg.categorical:
-            encoding.transform(x, self.cfg.categorical, self.encoders, self.gmean,
-                               self.cfg.cat_hash_buckets)
+            self._encode_rows(x)
         n = x.shape[0]
         out = np.empty(n, dtype=np.float32)
         m, _keep = self.model()
@@ -309,8 +360,7 @@ class Booster:
             raise RuntimeError("no leaf variances: fit with pgbm=True")
         x = np.array(x, dtype=np.float32, order="C", copy=bool(self.cfg.categorical))
         if self.cfg.categorical:
-            encoding.transform(x, self.cfg.categorical, self.encoders, self.gmean,
-                               self.cfg.cat_hash_buckets)
+            self._encode_rows(x)
         n = x.shape[0]
         var = np.empty(n, dtype=np.float32)
         m, _keep = self.model()

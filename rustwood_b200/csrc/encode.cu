@@ -315,3 +315,109 @@ int target_encode_device(rw_ctx* ctx, float* d_x, const float* d_y, uint64_t n, 
   }
   return rc;
 }
+
+// =================================================================================
+// encoding::transform (src/encoding.rs:96-115) on the GPU: every categorical value of the
+// rows becomes its key's test-set value, unseen keys the training mean.
+
+namespace {
+
+struct TeMaps {
+  float* x;
+  uint64_t n;
+  uint32_t nf, n_cat;
+  const uint32_t* cat;        // [n_cat]
+  const long long* key_lo;    // [n_cat]
+  const uint64_t* koff;       // [n_cat]
+  const uint64_t* n_keys;     // [n_cat]
+  const float* value;         // [slots]
+  const uint8_t* present;     // [slots]
+  float gmean;
+  unsigned long long buckets;
+};
+
+__global__ void k_te_transform(TeMaps m) {
+  const uint64_t total = m.n * m.n_cat;
+  for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+       t += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t j = (uint32_t)(t / m.n);
+    const uint64_t i = t % m.n;
+    float* v = m.x + i * m.nf + m.cat[j];
+    // the slot of key - key_lo, unsigned so keys below key_lo fall outside too
+    const unsigned long long d =
+        (unsigned long long)te_key(*v, m.buckets) - (unsigned long long)m.key_lo[j];
+    float out = m.gmean;
+    if (d < m.n_keys[j] && m.present[m.koff[j] + d]) out = m.value[m.koff[j] + d];
+    *v = out;
+  }
+}
+
+}  // namespace
+
+int target_transform_device(rw_ctx* ctx, float* d_x, uint64_t n, uint32_t nf, const uint32_t* cat,
+                            uint32_t n_cat, const rw_encoders& enc, uint64_t hash_buckets,
+                            std::string* why) {
+  if (enc.key_lo.size() != n_cat) {
+    *why = "the encoders hold a different number of categorical features";
+    return RW_ERR_ARG;
+  }
+  for (uint32_t j = 0; j < n_cat; j++)
+    if (cat[j] >= nf) {
+      *why = "categorical feature index out of range";
+      return RW_ERR_ARG;
+    }
+  if (n == 0 || n_cat == 0) return RW_OK;
+  cudaStream_t s = ctx->stream;
+  const uint64_t slots = enc.value.size();
+  uint32_t* d_cat = nullptr;
+  long long* d_lo = nullptr;
+  uint64_t *d_koff = nullptr, *d_nk = nullptr;
+  float* d_val = nullptr;
+  uint8_t* d_pres = nullptr;
+  cudaError_t e = cudaMalloc(&d_cat, (size_t)n_cat * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&d_lo, (size_t)n_cat * 8);
+  if (e == cudaSuccess) e = cudaMalloc(&d_koff, (size_t)n_cat * 8);
+  if (e == cudaSuccess) e = cudaMalloc(&d_nk, (size_t)n_cat * 8);
+  if (e == cudaSuccess) e = cudaMalloc(&d_val, std::max<uint64_t>(slots, 1) * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&d_pres, std::max<uint64_t>(slots, 1));
+  if (e == cudaSuccess) e = cudaMemcpyAsync(d_cat, cat, (size_t)n_cat * 4, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(d_lo, enc.key_lo.data(), (size_t)n_cat * 8, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(d_koff, enc.koff.data(), (size_t)n_cat * 8, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(d_nk, enc.n_keys.data(), (size_t)n_cat * 8, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess && slots)
+    e = cudaMemcpyAsync(d_val, enc.value.data(), slots * 4, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess && slots)
+    e = cudaMemcpyAsync(d_pres, enc.present.data(), slots, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) {
+    TeMaps m;
+    m.x = d_x;
+    m.n = n;
+    m.nf = nf;
+    m.n_cat = n_cat;
+    m.cat = d_cat;
+    m.key_lo = d_lo;
+    m.koff = d_koff;
+    m.n_keys = d_nk;
+    m.value = d_val;
+    m.present = d_pres;
+    m.gmean = enc.gmean;
+    m.buckets = hash_buckets;
+    k_te_transform<<<te_grid(n * n_cat), 256, 0, s>>>(m);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  cudaFree(d_cat);
+  cudaFree(d_lo);
+  cudaFree(d_koff);
+  cudaFree(d_nk);
+  cudaFree(d_val);
+  cudaFree(d_pres);
+  if (e != cudaSuccess) {
+    *why = std::string("target transform: ") + cudaGetErrorString(e);
+    return RW_ERR_CUDA;
+  }
+  return RW_OK;
+}

@@ -249,6 +249,9 @@ int target_encode_device(rw_ctx* ctx, float* d_x, const float* d_y, uint64_t n, 
                          const uint32_t* cat, uint32_t n_cat, float smoothing, uint32_t k_folds,
                          uint64_t hash_buckets, float* gmean_out, rw_encoders* enc,
                          std::string* why);
+int target_transform_device(rw_ctx* ctx, float* d_x, uint64_t n, uint32_t nf, const uint32_t* cat,
+                            uint32_t n_cat, const rw_encoders& enc, uint64_t hash_buckets,
+                            std::string* why);
 
 // PGBM: every row's g^2 (f32) in the wide fixed point into its leaf's exact int64 sum
 // (the leaf_g2 sums of gpu_kernels.rs:1015-1043); run after the tree's last level.

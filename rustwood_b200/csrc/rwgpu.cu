@@ -849,6 +849,50 @@ extern "C" int rw_encoders_table(const rw_encoders* enc, uint32_t i, int64_t* ke
 
 extern "C" void rw_encoders_free(rw_encoders* enc) { delete enc; }
 
+extern "C" int rw_encoders_create(uint32_t n_cat, const int64_t* key_lo, const uint64_t* n_keys,
+                                  const float* value, const uint8_t* present, float gmean,
+                                  rw_encoders** out) {
+  if (!out || (n_cat && (!key_lo || !n_keys))) return RW_ERR_ARG;
+  *out = nullptr;
+  auto* enc = new rw_encoders();
+  uint64_t slots = 0;
+  for (uint32_t j = 0; j < n_cat; j++) {
+    enc->key_lo.push_back(key_lo[j]);
+    enc->koff.push_back(slots);
+    enc->n_keys.push_back(n_keys[j]);
+    slots += n_keys[j];
+  }
+  if (slots && (!value || !present)) {
+    delete enc;
+    return RW_ERR_ARG;
+  }
+  enc->value.assign(value, value + slots);
+  enc->present.assign(present, present + slots);
+  enc->gmean = gmean;
+  *out = enc;
+  return RW_OK;
+}
+
+extern "C" int rw_target_transform(rw_ctx* ctx, float* x, uint64_t n, uint32_t nf,
+                                   const uint32_t* categorical, uint32_t n_cat,
+                                   const rw_encoders* enc, uint64_t hash_buckets) {
+  if (!ctx) return fail(nullptr, RW_ERR_ARG, "context is NULL");
+  if (!x || !enc || (n_cat && !categorical)) return fail(ctx, RW_ERR_ARG, "bad transform arguments");
+  if (n == 0 || n_cat == 0) return RW_OK;
+  rw_ctx* c = first_rank(ctx);
+  RW_CU(c, cudaSetDevice(c->device));
+  DBuf<float> dx;
+  RW_CU(c, dx.alloc((size_t)n * nf));
+  RW_CU(c, upload_h2d(c, dx.p, x, (size_t)n * nf * 4));
+  std::string why;
+  const int rc = target_transform_device(c, dx.p, n, nf, categorical, n_cat, *enc, hash_buckets,
+                                         &why);
+  if (rc) return fail(ctx, rc, why);
+  RW_CU(c, cudaMemcpyAsync(x, dx.p, (size_t)n * nf * 4, cudaMemcpyDeviceToHost, c->stream));
+  RW_CU(c, cudaStreamSynchronize(c->stream));
+  return RW_OK;
+}
+
 // =================================================================================
 // datasets
 

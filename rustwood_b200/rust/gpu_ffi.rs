@@ -145,6 +145,12 @@ extern "C" {
     pub fn rw_encoders_table(enc: *const rw_encoders, i: u32, key_lo: *mut i64, n_keys: *mut u64,
                              value: *mut *const f32, present: *mut *const u8) -> c_int;
     pub fn rw_encoders_free(enc: *mut rw_encoders);
+    pub fn rw_encoders_create(n_cat: u32, key_lo: *const i64, n_keys: *const u64,
+                              value: *const f32, present: *const u8, gmean: f32,
+                              out: *mut *mut rw_encoders) -> c_int;
+    pub fn rw_target_transform(ctx: *mut rw_ctx, x_rowmajor: *mut f32, n: u64, nf: u32,
+                               categorical: *const u32, n_cat: u32, enc: *const rw_encoders,
+                               hash_buckets: u64) -> c_int;
     pub fn rw_model_thr_bins(m: *const rw_model, cuts: *const f32, n_bins: u32,
                              thr_bin: *mut u16) -> c_int;
     pub fn rw_compute_boundaries_device(ctx: *mut rw_ctx, d_x: *const f32, n: u64, nf: u32,

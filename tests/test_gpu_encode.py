@@ -57,3 +57,38 @@ def test_gpu_target_encoding_refuses_wide_key_ranges(ctx):
     want = x.copy()
     encoding.fit_transform_train(want, y, CATS, cfg.te_smoothing, 5, 0)
     np.testing.assert_array_equal(xe.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("hash_buckets", [0, 7])
+def test_gpu_transform_matches_host_transform(ctx, hash_buckets):
+    """encoding::transform on the GPU (rw_target_transform) equals the host transform for
+    seen, unseen (beyond and inside the training range), negative and NaN codes."""
+    from rustwood_b200.booster import target_transform_gpu
+    x, y, xt, _ = synth.c3(20_000, n_test=6_007, seed=5)
+    x = np.ascontiguousarray(x, np.float32)
+    enc, gm = target_encode_gpu(ctx, x.copy(), y, CATS, 10.0, 5, hash_buckets)
+    xt = np.ascontiguousarray(xt, np.float32)
+    xt[::5, 7] = 77.0    # unseen, above the training codes
+    xt[::7, 8] = -2.0    # unseen, below
+    xt[::11, 9] = np.nan
+    want = xt.copy()
+    encoding.transform(want, CATS, enc, gm, hash_buckets)
+    got = xt.copy()
+    assert target_transform_gpu(ctx, got, CATS, enc, gm, hash_buckets)
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+    # too many slots for the dense tables: nothing is touched, the caller falls back
+    untouched = xt.copy()
+    assert not target_transform_gpu(ctx, untouched, CATS, enc, gm, hash_buckets, max_slots=4)
+    np.testing.assert_array_equal(untouched.view(np.uint32), xt.view(np.uint32))
+
+
+def test_booster_categorical_fit_and_predict_use_the_gpu_encoder(ctx):
+    x, y, xt, _ = synth.c3(20_000, n_test=3_000, seed=6)
+    cfg = rb.Config(n_trees=15, depth=5, n_bins=64, categorical=CATS)
+    b = rb.Booster(cfg, ctx)
+    b.fit(x, y)
+    got = b.predict(xt)
+    xe = np.array(xt, np.float32, order="C", copy=True)
+    encoding.transform(xe, CATS, b.encoders, b.gmean, cfg.cat_hash_buckets)
+    want = oracle.predict(xe, b.feat, b.thr, b.leafval, b.base_score, cfg.n_trees, cfg.depth)
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
