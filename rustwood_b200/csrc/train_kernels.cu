@@ -69,6 +69,9 @@ static_assert(kMaxRowsPerCta >= 1024, "quantisation too fine for the histogram r
 #ifndef RW_STREAM_ROWS
 #define RW_STREAM_ROWS 512
 #endif
+#ifndef RW_STREAM_STAGES
+#define RW_STREAM_STAGES 2
+#endif
 constexpr uint32_t kListRows = RW_LIST_ROWS;
 constexpr int kListSlots = 3;
 static_assert(kListRows * 4 <= kHistThreads && kListRows % (kHistThreads / 32) == 0,
@@ -76,7 +79,7 @@ static_assert(kListRows * 4 <= kHistThreads && kListRows % (kHistThreads / 32) =
 // The all-rows level streams its rows through shared memory in stages of kStreamRows
 // (one TMA bulk copy of the stage's bin rows and one of its q values), kStreamStages deep.
 constexpr uint32_t kStreamRows = RW_STREAM_ROWS;
-constexpr int kStreamStages = 2;
+constexpr int kStreamStages = RW_STREAM_STAGES;
 constexpr uint32_t kStreamRowsPerWarp = kStreamRows / (kHistThreads / 32);
 static_assert(kStreamRows % (kHistThreads / 32) == 0, "whole rows per warp per stage");
 
