@@ -12,11 +12,20 @@
 // byte-SIMD compare (__vcmpgtu4) against the broadcast threshold produces the 4 split
 // bits, and the 4 leaf indices advance in the bytes of one register
 // (leaf4 = 2*leaf4 + bits; depth <= 8 keeps every byte below 256).
+//
+// Small batches (a few thousand rows at most) take a different shape: one CTA per row,
+// its threads walking different trees at once straight from the model in global memory
+// (it stays in L1/L2 across the CTAs), each tree's leaf value into shared memory, then
+// one thread adds them in tree order. A row then costs a few dependent memory round
+// trips instead of a walk over every tree, and nothing is staged.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 #include <algorithm>
+#include <mutex>
+#include <tuple>
+#include <vector>
 
 #include "rw_internal.cuh"
 
@@ -29,12 +38,60 @@ __device__ __forceinline__ void stage_model(uint32_t t0, uint32_t tc, uint32_t d
                                             const uint32_t* __restrict__ g_split,
                                             const float* __restrict__ g_leaf, uint32_t* s_split,
                                             float* s_leaf) {
-  const uint32_t nl = 1u << depth;
   for (uint32_t i = threadIdx.x; i < tc * depth; i += blockDim.x)
     s_split[i] = g_split[(size_t)t0 * depth + i];
   for (uint32_t i = threadIdx.x; i < (tc << depth); i += blockDim.x)
     s_leaf[i] = g_leaf[((size_t)t0 << depth) + i];
-  (void)nl;
+}
+
+// Small batches: CTA r scores row r. Thread i walks trees i, i + blockDim.x, ...: the
+// tree's D split words and the row's D values are loaded together (independent of each
+// other), the leaf index is assembled MSB first, and the tree's leaf value lands in
+// s_val[t]; thread 0 then adds base + s_val[0] + s_val[1] + ... in f32, in tree order --
+// the same sequence predict_cpu (src/booster.rs:582-601) and the other scorers add.
+// U8: feature-major bins [nf][ld], split words (feature << 8) | thr_bin, bit = bin > t.
+// F32: row-major x [n][nf], feat/thr, bit = x > thr (NaN gives 0).
+constexpr int kRowThreads = 256;
+constexpr int kRowMaxDepth = 12;
+template <bool U8>
+__global__ void __launch_bounds__(kRowThreads) k_predict_rows(
+    const void* __restrict__ in, uint64_t ld, uint32_t nf, uint32_t n_trees, uint32_t depth,
+    const uint32_t* __restrict__ split8, const uint32_t* __restrict__ feat,
+    const float* __restrict__ thr, const float* __restrict__ leafval, float base,
+    float* __restrict__ out) {
+  extern __shared__ float s_val[];  // [n_trees]
+  const uint64_t r = blockIdx.x;
+  for (uint32_t t = threadIdx.x; t < n_trees; t += blockDim.x) {
+    const size_t k0 = (size_t)t * depth;
+    uint32_t bits[kRowMaxDepth];
+#pragma unroll
+    for (int d = 0; d < kRowMaxDepth; d++) {
+      bits[d] = 0u;
+      if (d < (int)depth) {
+        if (U8) {
+          const uint32_t sv = __ldg(split8 + k0 + d);
+          const uint32_t f = (sv >> 8) < nf ? (sv >> 8) : 0u;  // the host checks feature < nf
+          const uint8_t* bins = static_cast<const uint8_t*>(in);
+          bits[d] = (uint32_t)__ldg(bins + (size_t)f * ld + r) > (sv & 0xffu) ? 1u : 0u;
+        } else {
+          const uint32_t f0 = __ldg(feat + k0 + d), f = f0 < nf ? f0 : 0u;
+          const float* x = static_cast<const float*>(in);
+          bits[d] = __ldg(x + r * nf + f) > __ldg(thr + k0 + d) ? 1u : 0u;
+        }
+      }
+    }
+    uint32_t leaf = 0u;
+#pragma unroll
+    for (int d = 0; d < kRowMaxDepth; d++)
+      if (d < (int)depth) leaf = 2u * leaf + bits[d];
+    s_val[t] = __ldg(leafval + ((size_t)t << depth) + leaf);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float acc = base;
+    for (uint32_t t = 0; t < n_trees; t++) acc += s_val[t];
+    out[r] = acc;
+  }
 }
 
 __global__ void __launch_bounds__(kPredThreads) k_predict_u8_simd(
@@ -257,6 +314,18 @@ uint32_t trees_per_chunk(uint32_t n_trees, uint32_t depth, size_t per_slot_bytes
   return (uint32_t)tc;
 }
 
+// Batches of at most kRowsMax rows whose model's leaf values fit the default 48 KB of
+// shared memory go to k_predict_rows (C5's 500-tree model on B200: 12 us for one row, 19 us
+// for 1024, 77 us for 8192, 142 us for 16384, where the tiled scorer's per-thread walk over
+// the trees costs about 120 us up to 100k rows).
+#ifndef RW_PRED_ROWS_MAX
+#define RW_PRED_ROWS_MAX 12288
+#endif
+constexpr uint64_t kRowsMax = RW_PRED_ROWS_MAX;
+bool small_batch(uint64_t n, const rw_dmodel& m) {
+  return n <= kRowsMax && m.n_trees > 0 && (size_t)m.n_trees * 4 <= 48 * 1024;
+}
+
 int pred_grid(uint64_t work) {
   uint64_t b = (work + kPredThreads - 1) / kPredThreads;
   const uint64_t cap = 148ull * 8;
@@ -265,6 +334,28 @@ int pred_grid(uint64_t work) {
 }
 
 }  // namespace
+
+// Sets a kernel's dynamic shared-memory limit and returns its resident CTAs per SM, once
+// per (device, kernel, size): the two runtime calls would otherwise sit between the
+// launches of every call, which small batches feel.
+static cudaError_t tiled_prepare(int dev, const void* fn, int threads, size_t smem, int* per_sm) {
+  static std::mutex mu;
+  static std::vector<std::tuple<int, const void*, size_t, int>> done;
+  std::lock_guard<std::mutex> lock(mu);
+  for (const auto& d : done)
+    if (std::get<0>(d) == dev && std::get<1>(d) == fn && std::get<2>(d) == smem) {
+      *per_sm = std::get<3>(d);
+      return cudaSuccess;
+    }
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  int k = 1;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&k, fn, threads, smem);
+  if (e != cudaSuccess) return e;
+  *per_sm = std::max(k, 1);
+  done.emplace_back(dev, fn, smem, *per_sm);
+  return cudaSuccess;
+}
 
 // The tiled scorer for depth 1..8 when the rows' bins fit next to a tree chunk.
 static cudaError_t launch_predict_u8_tiled(const uint8_t* bins, uint64_t n, uint64_t ld,
@@ -292,12 +383,10 @@ static cudaError_t launch_predict_u8_tiled(const uint8_t* bins, uint64_t n, uint
   for (uint32_t t0 = 0; t0 < m.n_trees; t0 += tc) {
     const uint32_t c = m.n_trees - t0 < tc ? m.n_trees - t0 : tc;
     const size_t smem = ((size_t)c << m.depth) * 4 + (size_t)c * ((m.depth + 1) & ~1u) * 8 + rows_bytes;
-    cudaError_t e = cudaFuncSetAttribute(fns[m.depth], cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
-    if (e != cudaSuccess) return e;
     int per_sm = 1;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fns[m.depth], T, smem);
-    const uint64_t grid = std::max<uint64_t>(1, std::min<uint64_t>(nblk, (uint64_t)sms * std::max(per_sm, 1)));
+    cudaError_t e = tiled_prepare(dev, fns[m.depth], T, smem, &per_sm);
+    if (e != cudaSuccess) return e;
+    const uint64_t grid = std::max<uint64_t>(1, std::min<uint64_t>(nblk, (uint64_t)sms * per_sm));
     int first = t0 == 0;
     uint64_t nn = n, ll = ld;
     uint32_t nf = m.nf, tt0 = t0, cc = c;
@@ -317,6 +406,12 @@ static cudaError_t launch_predict_u8_tiled(const uint8_t* bins, uint64_t n, uint
 cudaError_t launch_predict_u8(const uint8_t* bins, uint64_t n, uint64_t ld, const rw_dmodel& m,
                               float* out, cudaStream_t s) {
   if (n == 0) return cudaSuccess;
+  if (small_batch(n, m)) {
+    k_predict_rows<true><<<(unsigned)n, kRowThreads, (size_t)m.n_trees * 4, s>>>(
+        bins, ld, m.nf, m.n_trees, m.depth, m.d_split8, nullptr, nullptr, m.d_leafval, m.base,
+        out);
+    return cudaGetLastError();
+  }
   const bool simd = m.depth <= 8 && (ld % 4) == 0 && ld >= ((n + 3) & ~3ull) &&
                     (reinterpret_cast<uintptr_t>(bins) % 4) == 0;
   if (simd && m.n_trees > 0) {
@@ -353,6 +448,11 @@ cudaError_t launch_predict_f32(const float* x, uint64_t n, uint32_t nf, const rw
                                float* out, cudaStream_t s) {
   if (n == 0) return cudaSuccess;
   (void)nf;
+  if (small_batch(n, m)) {
+    k_predict_rows<false><<<(unsigned)n, kRowThreads, (size_t)m.n_trees * 4, s>>>(
+        x, 0, m.nf, m.n_trees, m.depth, nullptr, m.d_feat, m.d_thr, m.d_leafval, m.base, out);
+    return cudaGetLastError();
+  }
   const uint32_t tc = trees_per_chunk(m.n_trees, m.depth, 8);
   for (uint32_t t0 = 0; t0 < m.n_trees; t0 += tc) {
     const uint32_t c = m.n_trees - t0 < tc ? m.n_trees - t0 : tc;

@@ -186,7 +186,7 @@ def test_fit_matches_oracle_exact(ctx, name):
 
 def test_predict_u8_random_model(ctx):
     feat, thr_bin, leafval = synth.c5_model(n_trees=500, depth=6, nf=54, seed=3)
-    n = 10_007
+    n = 20_011
     bins = synth.c5_bins(n, 54, seed=4)
     # raw-threshold twin of the same model: thr = cut[f][t] on a synthetic cut table
     cuts = np.sort(np.random.default_rng(5).standard_normal((54, 255)).astype(np.float32), axis=1)
@@ -216,14 +216,15 @@ def _raw_twin(bins, feat, thr_bin, nf, seed):
 
 
 @pytest.mark.parametrize("depth,trees,nf,n", [
-    (1, 7, 3, 1), (4, 100, 20, 4097), (6, 500, 54, 2049), (8, 1200, 10, 5000),
-    (10, 50, 30, 3000), (6, 64, 120, 2000), (6, 500, 54, 4100), (3, 33, 5, 1028),
-    (6, 251, 54, 4096), (7, 300, 64, 8200),
+    (1, 7, 3, 12289), (4, 100, 20, 16385), (6, 500, 54, 12289), (8, 1200, 10, 17000),
+    (10, 50, 30, 15000), (6, 64, 120, 14000), (6, 500, 54, 16388), (3, 33, 5, 13316),
+    (6, 251, 54, 16384), (7, 300, 64, 20488),
 ])
 def test_predict_u8_shapes(ctx, depth, trees, nf, n):
-    """The u8 scorers (tiled shared-memory kernel for depth <= 8 with tree chunks, the
-    older byte-SIMD kernel for wide rows, the scalar kernel for depth > 8 or a row stride
-    not a multiple of 4) against predict_cpu on the raw-threshold twin of the same model."""
+    """The u8 scorers for batches above 12288 rows (tiled shared-memory kernel for depth <=
+    8 with tree chunks, the older byte-SIMD kernel for wide rows, the scalar kernel for
+    depth > 8 or a row stride not a multiple of 4) against predict_cpu on the
+    raw-threshold twin of the same model."""
     feat, thr_bin, leafval = synth.c5_model(n_trees=trees, depth=depth, nf=nf, seed=depth)
     bins = synth.c5_bins(n, nf, seed=depth + 1)
     x, thr = _raw_twin(bins, feat, thr_bin, nf, seed=depth + 2)
@@ -233,6 +234,29 @@ def test_predict_u8_shapes(ctx, depth, trees, nf, n):
     b.feat, b.thr, b.thr_bin, b.leafval = feat, thr, thr_bin, leafval
     got = b.predict_bins(bins)
     np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("depth,trees,nf,n", [
+    (1, 1, 1, 1), (6, 500, 54, 1), (6, 500, 54, 1000), (12, 40, 9, 37), (9, 3000, 16, 300),
+    (4, 100, 20, 4097), (6, 500, 54, 12288), (2, 12289, 4, 64),
+])
+def test_small_batch_scoring(ctx, depth, trees, nf, n):
+    """Batches of at most 12288 rows (one CTA per row, its threads on different trees, the
+    leaf values added in tree order by one thread) against predict_cpu, through both
+    host-buffer entry points (u8 bins and raw f32 rows). 3000 trees put several trees on
+    each thread; 12,289 trees exceed the kernel's 48 KB of leaf values and take the
+    chunked scorers instead."""
+    feat, thr_bin, leafval = synth.c5_model(n_trees=trees, depth=depth, nf=nf, seed=depth + 20)
+    bins = synth.c5_bins(n, nf, seed=depth + 21)
+    x, thr = _raw_twin(bins, feat, thr_bin, nf, seed=depth + 22)
+    want = oracle.predict(x, feat, thr, leafval, 0.75, trees, depth)
+    b = rb.Booster(rb.Config(n_trees=trees, depth=depth), ctx)
+    b.n_features, b.base_score = nf, np.float32(0.75)
+    b.feat, b.thr, b.thr_bin, b.leafval = feat, thr, thr_bin, leafval
+    got = b.predict_bins(bins)
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+    got32 = b.predict(x)
+    np.testing.assert_array_equal(got32.view(np.uint32), want.view(np.uint32))
 
 
 def test_fit_vs_faithful_cpu_rs(ctx):
