@@ -6,9 +6,10 @@
 // monotone fix, or (unique mode) the midpoints of the distinct values, padded with +inf
 // or subsampled evenly. Here:
 //   k_sample_gather   the sampled rows' values, feature-major [nf][m];
-//   k_feature_sort    one CTA per feature: an LSD radix sort of the m values (4 stable
-//                     passes of 8 bits over an order-preserving key; -0.0 and +0.0 share a
-//                     key, as they compare equal) through two scratch columns;
+//   k_sort_count,     an LSD radix sort of each feature's m values (4 stable passes of 8
+//   k_sort_scatter    bits over an order-preserving key; -0.0 and +0.0 share a key, as
+//                     they compare equal) through two scratch columns, each column split
+//                     over several CTAs;
 //   k_feature_cuts    one CTA per feature: the cut table from the sorted column.
 // The sort is stable, so the zeros (-0.0 and +0.0 compare equal) stay in sample order as
 // in the reference; the cut kernel still reads a zero's sign from the sample order (a
@@ -66,62 +67,79 @@ __device__ uint32_t scan256(uint32_t v, uint32_t* s_tmp) {
   return r;
 }
 
-// One CTA sorts column f: a[f*m .. f*m+m) with b as the second buffer; 4 passes, so the
-// sorted values end in a. Each pass is a stable counting sort on one 8-bit digit (LSD
-// radix needs stable passes): the column is scattered tile by tile in index order, one
-// element per thread; within a tile an element's place is its digit's running offset,
-// plus the counts of that digit in the lower warps, plus its rank among the equal digits
-// of its own warp.
-__global__ void __launch_bounds__(kSortThreads) k_feature_sort(uint32_t* __restrict__ a,
-                                                               uint32_t* __restrict__ b,
-                                                               uint64_t m) {
+// The sort of column f (m keys) is split over P parts of the column (P CTAs per
+// feature, part p = [m*p/P, m*(p+1)/P)), 4 passes of one 8-bit digit each, two kernels per
+// pass: k_sort_count counts every part's digits; k_sort_scatter moves each part's keys to
+// their places, the digit's start over the whole column plus the same digit's count in
+// the lower parts. Within a part the keys are scattered tile by tile in index order, one
+// key per thread; within a tile a key's place is its digit's running offset, plus the
+// counts of that digit in the lower warps, plus its rank among the equal digits of its own
+// warp. So every pass is a stable counting sort, as LSD radix sorting needs.
+__global__ void __launch_bounds__(kSortThreads) k_sort_count(const uint32_t* __restrict__ src,
+                                                             uint64_t m, uint32_t parts,
+                                                             int shift,
+                                                             uint32_t* __restrict__ counts) {
+  __shared__ uint32_t s_cnt[256];
+  const uint32_t p = blockIdx.x, f = blockIdx.y;
+  const uint64_t lo = m * p / parts, hi = m * (p + 1) / parts;
+  const uint32_t* col = src + (size_t)f * m;
+  if (threadIdx.x < 256) s_cnt[threadIdx.x] = 0u;
+  __syncthreads();
+  for (uint64_t i = lo + threadIdx.x; i < hi; i += kSortThreads)
+    atomicAdd(&s_cnt[(order_key(col[i]) >> shift) & 0xffu], 1u);
+  __syncthreads();
+  if (threadIdx.x < 256) counts[((size_t)f * parts + p) * 256 + threadIdx.x] = s_cnt[threadIdx.x];
+}
+
+__global__ void __launch_bounds__(kSortThreads) k_sort_scatter(const uint32_t* __restrict__ src,
+                                                               uint32_t* __restrict__ dst,
+                                                               uint64_t m, uint32_t parts,
+                                                               int shift,
+                                                               const uint32_t* __restrict__ counts) {
   constexpr int kWarps = kSortThreads / 32;
   __shared__ uint32_t s_cnt[256];
   __shared__ uint32_t s_tmp[16];
   __shared__ uint32_t s_wc[kWarps][256];  // per tile: counts, then offsets, per warp and digit
-  uint32_t* src = a + (size_t)blockIdx.x * m;
-  uint32_t* dst = b + (size_t)blockIdx.x * m;
+  const uint32_t p = blockIdx.x, f = blockIdx.y;
+  const uint64_t lo = m * p / parts, hi = m * (p + 1) / parts;
+  const uint32_t* col = src + (size_t)f * m;
+  uint32_t* out = dst + (size_t)f * m;
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t lt = (1u << lane) - 1u;
-  for (int pass = 0; pass < 4; pass++) {
-    const int shift = 8 * pass;
-    if (threadIdx.x < 256) s_cnt[threadIdx.x] = 0u;
-    __syncthreads();
-    for (uint64_t i = threadIdx.x; i < m; i += kSortThreads)
-      atomicAdd(&s_cnt[(order_key(src[i]) >> shift) & 0xffu], 1u);
-    __syncthreads();
-    const uint32_t c = threadIdx.x < 256 ? s_cnt[threadIdx.x] : 0u;
-    const uint32_t base = scan256(c, s_tmp);
-    if (threadIdx.x < 256) s_cnt[threadIdx.x] = base;  // the digit's next free slot
-    __syncthreads();
-    for (uint64_t t0 = 0; t0 < m; t0 += kSortThreads) {
-      for (uint32_t w = threadIdx.x; w < kWarps * 256; w += kSortThreads)
-        (&s_wc[0][0])[w] = 0u;
-      const uint64_t i = t0 + threadIdx.x;
-      const bool live = i < m;
-      const uint32_t v = live ? src[i] : 0u;
-      const uint32_t d = live ? (order_key(v) >> shift) & 0xffu : 256u;  // 256: no element
-      const uint32_t peers = __match_any_sync(0xffffffffu, d);
-      const uint32_t rank = __popc(peers & lt);
-      __syncthreads();  // the counts are zero
-      if (live && rank == 0) s_wc[warp][d] = __popc(peers);
-      __syncthreads();
-      if (threadIdx.x < 256) {  // offsets of each warp's run of this digit, in warp order
-        uint32_t off = s_cnt[threadIdx.x];
-        for (int w = 0; w < kWarps; w++) {
-          const uint32_t k = s_wc[w][threadIdx.x];
-          s_wc[w][threadIdx.x] = off;
-          off += k;
-        }
-        s_cnt[threadIdx.x] = off;
-      }
-      __syncthreads();
-      if (live) dst[s_wc[warp][d] + rank] = v;
-      __syncthreads();  // s_wc is reused by the next tile
+  // this part's first place for each digit
+  uint32_t total = 0, lower = 0;
+  if (threadIdx.x < 256)
+    for (uint32_t q = 0; q < parts; q++) {
+      const uint32_t c = counts[((size_t)f * parts + q) * 256 + threadIdx.x];
+      total += c;
+      if (q < p) lower += c;
     }
-    uint32_t* t = src;
-    src = dst;
-    dst = t;
+  const uint32_t base = scan256(threadIdx.x < 256 ? total : 0u, s_tmp);
+  if (threadIdx.x < 256) s_cnt[threadIdx.x] = base + lower;  // the digit's next free slot
+  __syncthreads();
+  for (uint64_t t0 = lo; t0 < hi; t0 += kSortThreads) {
+    for (uint32_t w = threadIdx.x; w < kWarps * 256; w += kSortThreads) (&s_wc[0][0])[w] = 0u;
+    const uint64_t i = t0 + threadIdx.x;
+    const bool live = i < hi;
+    const uint32_t v = live ? col[i] : 0u;
+    const uint32_t d = live ? (order_key(v) >> shift) & 0xffu : 256u;  // 256: no element
+    const uint32_t peers = __match_any_sync(0xffffffffu, d);
+    const uint32_t rank = __popc(peers & lt);
+    __syncthreads();  // the counts are zero
+    if (live && rank == 0) s_wc[warp][d] = __popc(peers);
+    __syncthreads();
+    if (threadIdx.x < 256) {  // offsets of each warp's run of this digit, in warp order
+      uint32_t off = s_cnt[threadIdx.x];
+      for (int w = 0; w < kWarps; w++) {
+        const uint32_t k = s_wc[w][threadIdx.x];
+        s_wc[w][threadIdx.x] = off;
+        off += k;
+      }
+      s_cnt[threadIdx.x] = off;
+    }
+    __syncthreads();
+    if (live) out[s_wc[warp][d] + rank] = v;
+    __syncthreads();  // s_wc is reused by the next tile
   }
 }
 
@@ -223,21 +241,39 @@ __global__ void __launch_bounds__(kSortThreads) k_feature_cuts(
 }  // namespace
 
 cudaError_t launch_boundaries(const float* d_x, uint64_t n, uint32_t nf, uint32_t n_bins,
-                              uint64_t sample, int unique, uint32_t* scratch3, float* d_out,
-                              cudaStream_t s, uint64_t* m_out) {
+                              uint64_t sample, int unique, uint32_t* scratch, float* d_out,
+                              cudaStream_t s, uint64_t* m_out, int* nl) {
   const uint64_t stride = std::max<uint64_t>(n / std::max<uint64_t>(sample, 1), 1);
   const uint64_t m = (n - 1) / stride + 1;
   *m_out = m;
-  uint32_t* col = scratch3;                    // sample order
-  uint32_t* a = scratch3 + (size_t)nf * m;     // sorted (after 4 passes)
-  uint32_t* b = scratch3 + 2 * (size_t)nf * m;
+  uint32_t* col = scratch;                    // sample order (kept: the cut kernel reads it)
+  uint32_t* a = scratch + (size_t)nf * m;
+  uint32_t* b = scratch + 2 * (size_t)nf * m;
+  uint32_t* counts = scratch + 3 * (size_t)nf * m;  // [nf][parts][256]
   const uint64_t total = m * nf;
   const int grid = (int)std::min<uint64_t>((total + 255) / 256, 148ull * 16);
   k_sample_gather<<<grid, 256, 0, s>>>(d_x, n, nf, stride, m, col);
-  cudaError_t e = cudaMemcpyAsync(a, col, total * 4, cudaMemcpyDeviceToDevice, s);
-  if (e != cudaSuccess) return e;
-  k_feature_sort<<<nf, kSortThreads, 0, s>>>(a, b, m);
-  // b is free again: the cut kernel's compaction scratch
-  k_feature_cuts<<<nf, kSortThreads, 0, s>>>(a, col, b, m, n_bins, unique, d_out);
+  // parts per column: about two sorting CTAs per SM over all features, and at least 4096
+  // keys per part
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  uint64_t parts = std::max<uint64_t>(1, (2 * (uint64_t)sms) / nf);
+  parts = std::min<uint64_t>(parts, std::max<uint64_t>(1, m / 4096));
+  parts = std::min<uint64_t>(parts, kSortMaxParts);
+  const dim3 sg((unsigned)parts, nf);
+  // pass 0 reads the sample column; the passes then alternate a -> b -> a -> b, so the
+  // sorted keys end in b
+  const uint32_t* src = col;
+  uint32_t* dst = a;
+  for (int pass = 0; pass < 4; pass++) {
+    k_sort_count<<<sg, kSortThreads, 0, s>>>(src, m, (uint32_t)parts, 8 * pass, counts);
+    k_sort_scatter<<<sg, kSortThreads, 0, s>>>(src, dst, m, (uint32_t)parts, 8 * pass, counts);
+    src = dst;
+    dst = dst == a ? b : a;
+  }
+  // a is free again: the cut kernel's compaction scratch
+  k_feature_cuts<<<nf, kSortThreads, 0, s>>>(b, col, a, m, n_bins, unique, d_out);
+  if (nl) *nl += 2 + 8;
   return cudaGetLastError();
 }

@@ -363,12 +363,18 @@ cudaError_t launch_predict_u8(const uint8_t* bins, uint64_t n, uint64_t ld, cons
 // The sample of n row-major rows (stride max(n / sample, 1)) and its cut table
 // d_out[nf][n_bins-1]; scratch3 holds 3 * nf * m words, m = the sampled row count
 // (returned in m_out; ceil(n / stride)).
+// scratch: boundary_scratch_words(nf, m) words (three [nf][m] columns and the sort's
+// per-part digit counts); *nl counts the launches.
 cudaError_t launch_boundaries(const float* d_x, uint64_t n, uint32_t nf, uint32_t n_bins,
-                              uint64_t sample, int unique, uint32_t* scratch3, float* d_out,
-                              cudaStream_t s, uint64_t* m_out);
+                              uint64_t sample, int unique, uint32_t* scratch, float* d_out,
+                              cudaStream_t s, uint64_t* m_out, int* nl);
 inline uint64_t boundary_sample_rows(uint64_t n, uint64_t sample) {
   const uint64_t st = std::max<uint64_t>(n / std::max<uint64_t>(sample, 1), 1);
   return (n - 1) / st + 1;
+}
+constexpr uint32_t kSortMaxParts = 16;
+inline size_t boundary_scratch_words(uint32_t nf, uint64_t m) {
+  return 3 * (size_t)nf * m + (size_t)nf * kSortMaxParts * 256;
 }
 
 // ---- test hooks ------------------------------------------------------------------

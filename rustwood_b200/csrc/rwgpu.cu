@@ -1868,12 +1868,13 @@ extern "C" int rw_compute_boundaries_device(rw_ctx* ctx, const float* d_x, uint6
   const uint64_t m = boundary_sample_rows(n, sample);
   DBuf<uint32_t> scratch;
   DBuf<float> dout;
-  RW_CU(ctx, scratch.alloc(ctx, 3 * (size_t)nf * m));
+  RW_CU(ctx, scratch.alloc(ctx, boundary_scratch_words(nf, m)));
   RW_CU(ctx, dout.alloc(ctx, (size_t)nf * (n_bins - 1)));
   uint64_t mm = 0;
+  int nl = 0;
   RW_CU(ctx, launch_boundaries(d_x, n, nf, n_bins, sample, unique, scratch.p, dout.p,
-                               ctx->stream, &mm));
-  ctx->launches += 3;
+                               ctx->stream, &mm, &nl));
+  ctx->launches += nl;
   RW_CU(ctx, cudaMemcpyAsync(out, dout.p, (size_t)nf * (n_bins - 1) * 4, cudaMemcpyDeviceToHost,
                              ctx->stream));
   RW_CU(ctx, cudaStreamSynchronize(ctx->stream));
