@@ -335,25 +335,37 @@ int pred_grid(uint64_t work) {
 
 }  // namespace
 
-// Sets a kernel's dynamic shared-memory limit and returns its resident CTAs per SM, once
-// per (device, kernel, size): the two runtime calls would otherwise sit between the
-// launches of every call, which small batches feel.
+// Raises a kernel's dynamic shared-memory limit when a launch needs more than it was last
+// set to (per device; the limit only grows, so a smaller launch never lowers it under a
+// larger one) and returns the kernel's resident CTAs per SM at that size, queried once per
+// (device, kernel, size): the two runtime calls would otherwise sit between the launches
+// of every call, which small batches feel.
 static cudaError_t tiled_prepare(int dev, const void* fn, int threads, size_t smem, int* per_sm) {
   static std::mutex mu;
-  static std::vector<std::tuple<int, const void*, size_t, int>> done;
+  static std::vector<std::tuple<int, const void*, size_t>> limit;       // (dev, fn, bytes)
+  static std::vector<std::tuple<int, const void*, size_t, int>> occ;   // (dev, fn, bytes, CTAs)
   std::lock_guard<std::mutex> lock(mu);
-  for (const auto& d : done)
-    if (std::get<0>(d) == dev && std::get<1>(d) == fn && std::get<2>(d) == smem) {
-      *per_sm = std::get<3>(d);
+  size_t* lim = nullptr;
+  for (auto& l : limit)
+    if (std::get<0>(l) == dev && std::get<1>(l) == fn) lim = &std::get<2>(l);
+  if (!lim || smem > *lim) {
+    cudaError_t e =
+        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    if (lim) *lim = smem;
+    else limit.emplace_back(dev, fn, smem);
+  }
+  for (const auto& o : occ)
+    if (std::get<0>(o) == dev && std::get<1>(o) == fn && std::get<2>(o) == smem) {
+      *per_sm = std::get<3>(o);
       return cudaSuccess;
     }
-  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
   int k = 1;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&k, fn, threads, smem);
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&k, fn, threads, smem);
   if (e != cudaSuccess) return e;
   *per_sm = std::max(k, 1);
-  done.emplace_back(dev, fn, smem, *per_sm);
+  if (occ.size() >= 4096) occ.clear();  // many distinct models: keep the table bounded
+  occ.emplace_back(dev, fn, smem, *per_sm);
   return cudaSuccess;
 }
 

@@ -259,6 +259,23 @@ def test_small_batch_scoring(ctx, depth, trees, nf, n):
     np.testing.assert_array_equal(got32.view(np.uint32), want.view(np.uint32))
 
 
+def test_tiled_scorer_alternating_model_sizes(ctx):
+    """The tiled u8 scorer's shared-memory size follows the model: scoring a large model,
+    then a small one, then the large one again must not leave the kernel's limit at the
+    small size (each call bit-exact against predict_cpu)."""
+    n, nf = 13_000, 54
+    bins = synth.c5_bins(n, nf, seed=31)
+    for trees in (500, 20, 500, 120):
+        feat, thr_bin, leafval = synth.c5_model(n_trees=trees, depth=6, nf=nf, seed=trees)
+        x, thr = _raw_twin(bins, feat, thr_bin, nf, seed=32)
+        want = oracle.predict(x, feat, thr, leafval, 0.0, trees, 6)
+        b = rb.Booster(rb.Config(n_trees=trees, depth=6), ctx)
+        b.n_features, b.base_score = nf, np.float32(0.0)
+        b.feat, b.thr, b.thr_bin, b.leafval = feat, thr, thr_bin, leafval
+        got = b.predict_bins(bins)
+        np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
 def test_fit_vs_faithful_cpu_rs(ctx):
     """Against oracle_ref (faithful cpu.rs, f32 histograms, glibc expf): identical splits
     except at near-ties, and test metrics within 1e-4."""
