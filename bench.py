@@ -175,17 +175,53 @@ def reference_fit_seconds(x, y, cuts, base, trees, nt):
 def predict_cpu_baseline(rows=200_000):
     """predict_cpu (src/booster.rs:582-601) restated in oracle/, single-threaded like the
     reference, on a bounded sample of the C5 workload (the same random model; u8 bins as
-    f32 features against integer thresholds: bin > t exactly when the f32 compare holds)."""
+    f32 features against integer thresholds: bin > t exactly when the f32 compare holds);
+    beside it the same restatement over contiguous row slices on the host's threads (a
+    row-split variant the reference does not have, labelled as such)."""
+    from concurrent.futures import ThreadPoolExecutor
     import oracle
     synth = load_synth()
     feat, thr_bin, leafval = synth.c5_model(500, 6, 54, seed=0)
+    thr = thr_bin.astype(np.float32)
     rng = np.random.default_rng(2)
     x = rng.integers(0, 256, (rows, 54), dtype=np.uint8).astype(np.float32)
     t0 = time.perf_counter()
-    oracle.predict(x, feat, thr_bin.astype(np.float32), leafval, 0.0, 500, 6)
+    one = oracle.predict(x, feat, thr, leafval, 0.0, 500, 6)
     dt = time.perf_counter() - t0
+    nt = oracle.default_threads()
+    bounds = [rows * i // nt for i in range(nt + 1)]
+    with ThreadPoolExecutor(nt) as pool:  # the C scorer runs without the GIL
+        t0 = time.perf_counter()
+        parts = list(pool.map(lambda i: oracle.predict(x[bounds[i]:bounds[i + 1]], feat, thr,
+                                                       leafval, 0.0, 500, 6), range(nt)))
+        dt_mt = time.perf_counter() - t0
+    assert np.array_equal(np.concatenate(parts).view(np.uint32), one.view(np.uint32))
     return {"rows_per_s": rows / dt, "cores": 1, "kind": "port",
-            "sample": f"C5 model, {rows} rows x 54 (oracle predict_cpu, 1 thread)"}
+            "sample": f"C5 model, {rows} rows x 54 (oracle predict_cpu, 1 thread)",
+            "row_split": {"rows_per_s": rows / dt_mt, "threads": nt,
+                          "note": "the same scorer over contiguous row slices, one per thread "
+                                  "(not a reference code path)"}}
+
+
+def c4_cpu_baseline(trees=20, sample_rows=1_000_000, full_rows=10_000_000):
+    """C4's CPU leg: the first `trees` trees of oracle_ref (src/cpu.rs restated; depth 8, 16
+    bins, GOSS 0.2/0.1, L2, lr 0.1) on the reference's thread count, on a bounded
+    sample_rows-row sample of C4 (synth.c4, seed 0: the same distribution as the GPU
+    line's shards). The tree loop is timed; the figure for full_rows rows scales it by the
+    row ratio (the per-level histogram work is linear in rows) and is marked as such."""
+    import oracle
+    synth = load_synth()
+    x, y, _, _ = synth.c4(sample_rows, seed=0)
+    cuts = oracle.compute_boundaries(x, 16)
+    base = oracle.base_score(y, "l2")
+    nt = oracle.default_threads()
+    r = oracle.train(x, y, cuts, base, n_trees=trees, depth=8, n_bins=16, learning_rate=0.1,
+                     goss_top=0.2, goss_other=0.1, objective="l2", exact=False, n_threads=nt)
+    return {"seconds_sample": r.loop_seconds, "cores": nt, "kind": "port",
+            "sample": f"first {trees} trees of oracle_ref on a {sample_rows}-row C4 sample "
+                      f"(synth.c4 seed 0), tree loop timed",
+            "seconds_full_rows_extrapolated": r.loop_seconds * full_rows / sample_rows,
+            "extrapolation": f"x{full_rows / sample_rows:g} rows"}
 
 
 def run_reference(args):
@@ -283,10 +319,14 @@ def run_c4(args, ctx, rank, world, stream, flush_l2, barrier):
         ts.append(fit_dataset(ds, cfg, base).profile.total_ms)
     barrier()
     ds.close()
-    return {"workload": "C4 first %d trees: %d rows x 100 N(0,1), 16 bins 4-bit, depth 8, "
+    line = {"workload": "C4 first %d trees: %d rows x 100 N(0,1), 16 bins 4-bit, depth 8, "
                         "GOSS 0.2/0.1, L2 (8 GPU-generated shards, seeds fixed)"
                         % (args.c4_trees, args.c4_rows),
             "rows_per_gpu": n, "steps": steps, "seconds": statistics.mean(ts) / 1e3}
+    if world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = c4_cpu_baseline(args.c4_trees, min(1_000_000, args.c4_rows),
+                                               args.c4_rows)
+    return line
 
 
 def run_other_configs(args, ctx, flush_l2, barrier):

@@ -67,3 +67,12 @@ def test_predict_cpu_baseline_small_sample():
     r = bench.predict_cpu_baseline(rows=2000)
     assert r["rows_per_s"] > 0
     assert r["cores"] == 1 and r["kind"] == "port"
+    assert r["row_split"]["rows_per_s"] > 0 and r["row_split"]["threads"] >= 1
+
+
+def test_c4_cpu_baseline_small_sample():
+    sys.path.insert(0, ROOT)
+    import bench
+    r = bench.c4_cpu_baseline(trees=2, sample_rows=20_000, full_rows=200_000)
+    assert r["seconds_sample"] > 0 and r["kind"] == "port" and r["cores"] >= 1
+    assert abs(r["seconds_full_rows_extrapolated"] - 10 * r["seconds_sample"]) < 1e-9
