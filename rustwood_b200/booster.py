@@ -278,6 +278,13 @@ class Booster:
     # -- training ----------------------------------------------------------------
     def prepare(self, x: np.ndarray, y: np.ndarray):
         """fit_inner's host prep (src/booster.rs:246-285): returns (x_encoded, cuts, base)."""
+        x, y = self._encode_train(x, y)
+        cuts = compute_boundaries(x, self.cfg.n_bins, self.cfg.bin_sample, self.cfg.unique_bins)
+        return x, cuts, base_score(y, self.cfg.objective)
+
+    def _encode_train(self, x: np.ndarray, y: np.ndarray):
+        """encoding::fit_transform_train of the training rows (a C-contiguous float32 copy)
+        when the config has categorical features; y as float32."""
         cfg = self.cfg
         x = np.array(x, dtype=np.float32, order="C", copy=True)
         y = N.f32c(y)
@@ -293,21 +300,32 @@ class Booster:
                         x, y, cfg.categorical, cfg.te_smoothing, 5, cfg.cat_hash_buckets)
                 else:
                     raise
-        cuts = compute_boundaries(x, cfg.n_bins, cfg.bin_sample, cfg.unique_bins)
-        return x, cuts, base_score(y, cfg.objective)
+        return x, y
 
     def fit(self, x: np.ndarray, y: np.ndarray, profile: bool = False) -> float:
         """Booster::fit (src/booster.rs:169-181) for the GPU device; returns the tree-loop
-        time in seconds (what the reference reports as train_s)."""
-        x, cuts, base = self.prepare(x, y)
-        self.n_features = x.shape[1]
+        time in seconds (what the reference reports as train_s). One call of
+        rw_fit_with_boundaries: the rows are uploaded once and serve both the cut table
+        (compute_boundaries on the GPU, bit-identical to the host restatement) and the
+        binning; the cut table comes back in self.cuts."""
+        cfg = self.cfg
+        x, y = self._encode_train(x, y)
+        n, nf = x.shape
+        base = base_score(y, cfg.objective)
+        self.n_features = nf
         self.base_score = base
+        cuts = np.empty(nf * (cfg.n_bins - 1), dtype=np.float32)
+        r = FitResult(cfg.n_trees, cfg.depth, nf)
+        p = train_params(cfg)
+        r.profile.enable = int(profile)
+        if cfg.pgbm:
+            r.leafvar = np.zeros(cfg.n_trees << cfg.depth, dtype=np.float32)
+        self.ctx.check(N.lib.rw_fit_with_boundaries(
+            self.ctx.h, C.byref(p), N.ptr(x), N.ptr(y), n, nf, cfg.bin_sample,
+            int(cfg.unique_bins), base, N.ptr(cuts), N.ptr(r.feat), N.ptr(r.thr),
+            N.ptr(r.thr_bin), N.ptr(r.leafval), N.ptr(r.leafvar) if cfg.pgbm else None,
+            N.ptr(r.fi_gain), N.ptr(r.fi_count), C.byref(r.profile)))
         self.cuts = cuts
-        ds = Dataset(self.ctx, x, y, cuts, self.cfg.n_bins, self.cfg.pack4)
-        try:
-            r = fit_dataset(ds, self.cfg, base, profile=profile)
-        finally:
-            ds.close()
         self._take(r)
         return r.profile.total_ms / 1e3
 
