@@ -1823,38 +1823,48 @@ extern "C" void rw_compute_boundaries(const float* x, uint64_t n, uint32_t nf, u
   if (!x || !out || n_bins < 2 || n == 0) return;
   const uint32_t nbound = n_bins - 1;
   const uint64_t stride = std::max<uint64_t>(n / std::max<uint64_t>(sample, 1), 1);
-  std::vector<float> s;
-  s.reserve(n / stride + 1);
-  for (uint32_t f = 0; f < nf; f++) {
-    s.clear();
-    for (uint64_t i = 0; i < n; i += stride) s.push_back(x[i * nf + f]);
-    std::stable_sort(s.begin(), s.end(), [](float a, float b) { return a < b; });
-    float* b = out + (size_t)f * nbound;
-    if (unique) {
-      std::vector<float> u;
-      for (float v : s)
-        if (u.empty() || u.back() != v) u.push_back(v);
-      std::vector<float> cand;
-      for (size_t i = 0; i + 1 < u.size(); i++) cand.push_back(0.5f * (u[i] + u[i + 1]));
-      for (uint32_t j = 0; j < nbound; j++) {
-        if (cand.empty()) b[j] = INFINITY;
-        else if (cand.size() <= nbound) b[j] = j < cand.size() ? cand[j] : INFINITY;
-        else {
-          size_t pos = ((size_t)(j + 1) * cand.size()) / (nbound + 1);
-          b[j] = cand[std::min(pos, cand.size() - 1)];
+  // features are independent: host threads take them in turn (feature f on thread
+  // f % workers), each writing only its features' cuts
+  const uint32_t workers =
+      std::max<uint32_t>(1, std::min<uint32_t>(nf, std::thread::hardware_concurrency()));
+  auto run = [&](uint32_t w) {
+    std::vector<float> s;
+    s.reserve(n / stride + 1);
+    for (uint32_t f = w; f < nf; f += workers) {
+      s.clear();
+      for (uint64_t i = 0; i < n; i += stride) s.push_back(x[i * nf + f]);
+      std::stable_sort(s.begin(), s.end(), [](float a, float b) { return a < b; });
+      float* b = out + (size_t)f * nbound;
+      if (unique) {
+        std::vector<float> u;
+        for (float v : s)
+          if (u.empty() || u.back() != v) u.push_back(v);
+        std::vector<float> cand;
+        for (size_t i = 0; i + 1 < u.size(); i++) cand.push_back(0.5f * (u[i] + u[i + 1]));
+        for (uint32_t j = 0; j < nbound; j++) {
+          if (cand.empty()) b[j] = INFINITY;
+          else if (cand.size() <= nbound) b[j] = j < cand.size() ? cand[j] : INFINITY;
+          else {
+            size_t pos = ((size_t)(j + 1) * cand.size()) / (nbound + 1);
+            b[j] = cand[std::min(pos, cand.size() - 1)];
+          }
         }
+      } else {
+        const size_t m = s.size();
+        for (uint32_t j = 0; j < nbound; j++) {
+          const double q = (double)(j + 1) / (double)n_bins;
+          const size_t pos = (size_t)std::round(q * (double)(m - 1));
+          b[j] = s[std::min(pos, m - 1)];
+        }
+        for (uint32_t j = 1; j < nbound; j++)
+          if (b[j] <= b[j - 1]) b[j] = b[j - 1];
       }
-    } else {
-      const size_t m = s.size();
-      for (uint32_t j = 0; j < nbound; j++) {
-        const double q = (double)(j + 1) / (double)n_bins;
-        const size_t pos = (size_t)std::round(q * (double)(m - 1));
-        b[j] = s[std::min(pos, m - 1)];
-      }
-      for (uint32_t j = 1; j < nbound; j++)
-        if (b[j] <= b[j - 1]) b[j] = b[j - 1];
     }
-  }
+  };
+  std::vector<std::thread> th;
+  for (uint32_t w = 1; w < workers; w++) th.emplace_back(run, w);
+  run(0);
+  for (auto& t : th) t.join();
 }
 
 extern "C" int rw_compute_boundaries_device(rw_ctx* ctx, const float* d_x, uint64_t n,
