@@ -80,7 +80,7 @@ __global__ void __launch_bounds__(kSortThreads) k_sort_count(const uint32_t* __r
                                                              int shift,
                                                              uint32_t* __restrict__ counts) {
   __shared__ uint32_t s_cnt[256];
-  const uint32_t p = blockIdx.x, f = blockIdx.y;
+  const uint32_t f = blockIdx.x, p = blockIdx.y;
   const uint64_t lo = m * p / parts, hi = m * (p + 1) / parts;
   const uint32_t* col = src + (size_t)f * m;
   if (threadIdx.x < 256) s_cnt[threadIdx.x] = 0u;
@@ -100,7 +100,7 @@ __global__ void __launch_bounds__(kSortThreads) k_sort_scatter(const uint32_t* _
   __shared__ uint32_t s_cnt[256];
   __shared__ uint32_t s_tmp[16];
   __shared__ uint32_t s_wc[kWarps][256];  // per tile: counts, then offsets, per warp and digit
-  const uint32_t p = blockIdx.x, f = blockIdx.y;
+  const uint32_t f = blockIdx.x, p = blockIdx.y;
   const uint64_t lo = m * p / parts, hi = m * (p + 1) / parts;
   const uint32_t* col = src + (size_t)f * m;
   uint32_t* out = dst + (size_t)f * m;
@@ -261,7 +261,7 @@ cudaError_t launch_boundaries(const float* d_x, uint64_t n, uint32_t nf, uint32_
   uint64_t parts = std::max<uint64_t>(1, (2 * (uint64_t)sms) / nf);
   parts = std::min<uint64_t>(parts, std::max<uint64_t>(1, m / 4096));
   parts = std::min<uint64_t>(parts, kSortMaxParts);
-  const dim3 sg((unsigned)parts, nf);
+  const dim3 sg(nf, (unsigned)parts);  // features on x: no 65535 limit on their count
   // pass 0 reads the sample column; the passes then alternate a -> b -> a -> b, so the
   // sorted keys end in b
   const uint32_t* src = col;
