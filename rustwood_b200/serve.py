@@ -14,11 +14,12 @@ status line and a line `__END__`. `QUIT` (or end of input) stops it.
 Datasets are read from --data as src/data.rs:49-78 writes them: meta.json (n_train,
 n_test, n_features) and x_train.bin, y_train.bin, x_test.bin, y_test.bin (f32 LE,
 row-major).
-Run: python -m rustwood_b200.serve --gpu 0   (or --gpus 0,1,... for one multi-GPU context)
+Run: python -m rustwood_b200.serve --gpu 0   (or --gpus 0,1,... for one multi-GPU context);
+rustwood_b200/rustwood runs the same module with rustwood's command line, for the Python
+wrapper's RUSTWOOD_BIN.
 """
 from __future__ import annotations
 
-import argparse
 import json
 import os
 import re
@@ -138,13 +139,30 @@ def serve(gpus, inp=sys.stdin, out=sys.stdout) -> None:
 
 
 def main(argv=None) -> int:
-    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("--gpu", type=int, default=0)
-    ap.add_argument("--gpus", default="", help="comma-separated GPUs for one multi-GPU context")
-    a = ap.parse_args(argv)
-    gpus = [int(g) for g in a.gpus.split(",") if g] or [a.gpu]
-    serve(gpus)
-    return 0
+    """rustwood's command line (src/main.rs) as far as this worker goes, so the reference's
+    Python wrapper can run it as its binary (rustwood_b200/rustwood): `--serve 1`, or a
+    command line without `--data`, runs the line protocol on stdin; a command line with
+    `--data` and no `--serve` is one request (a fit, or with --load-model a scoring run)
+    whose reply goes to stdout, exit status 0 for `OK`, 1 for a failed request, 2 for a
+    bad command line. --gpu / --gpus pick the devices."""
+    from .config import Config
+    argv = list(sys.argv[1:] if argv is None else argv)
+    try:
+        cfg = Config.from_tokens(argv)
+    except Exception as e:
+        print(f"ERROR args {e}", flush=True)
+        return 2
+    gpus = list(cfg.gpus) or [cfg.gpu]
+    if cfg.serve or "--data" not in argv[0::2]:
+        serve(gpus)
+        return 0
+    w = Worker(gpus)
+    try:
+        reply = w.handle(argv)
+    finally:
+        w.close()
+    print(reply, flush=True)
+    return 0 if reply.startswith("OK") else 1
 
 
 if __name__ == "__main__":

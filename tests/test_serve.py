@@ -82,6 +82,29 @@ def test_worker_fits_then_scores_the_saved_model(tmp_path):
     b.ctx.close()
 
 
+def test_launcher_speaks_the_wrappers_protocol_without_a_gpu(tmp_path):
+    """rustwood_b200/rustwood as the reference's Python wrapper runs it (RUSTWOOD_BIN):
+    `--serve 1` answers every stdin line with a reply and __END__ and stops at QUIT; a
+    one-shot command line answers once, exit status 1 for a failed request and 2 for a bad
+    command line. Requests that fail before the GPU is needed run without one."""
+    exe = os.path.join(ROOT, "rustwood_b200", "rustwood")
+    env = dict(os.environ, RUSTWOOD_PYTHON=sys.executable)
+    missing = str(tmp_path / "missing")
+    lines = "--data\t" + missing + "\n--trees\nQUIT\n"
+    out = subprocess.run([exe, "--serve", "1"], input=lines, capture_output=True, text=True,
+                         timeout=300, env=env)
+    assert out.returncode == 0, out.stderr
+    replies = [r.strip() for r in out.stdout.split("__END__") if r.strip()]
+    assert len(replies) == 2, out.stdout
+    assert replies[0].startswith("ERROR data") and replies[1].startswith("ERROR args")
+    one = subprocess.run([exe, "--data", missing, "--trees", "5", "--device", "gpu"],
+                         capture_output=True, text=True, timeout=300, env=env)
+    assert one.returncode == 1 and one.stdout.startswith("ERROR data"), one.stdout + one.stderr
+    bad = subprocess.run([exe, "--no-such-flag", "1"], capture_output=True, text=True,
+                         timeout=300, env=env)
+    assert bad.returncode == 2 and bad.stdout.startswith("ERROR args"), bad.stdout
+
+
 def test_thr_bins_reject_a_foreign_cut_table():
     import rustwood_b200 as rb
     from rustwood_b200 import _native as N
