@@ -256,9 +256,10 @@ int rw_target_encode(rw_ctx* ctx, float* x_rowmajor, const float* y, uint64_t n,
 int rw_encoders_table(const rw_encoders* enc, uint32_t i, int64_t* key_lo, uint64_t* n_keys,
                       const float** value, const uint8_t** present);
 void rw_encoders_free(rw_encoders* enc);
-/* Encoders from maps held elsewhere (a loaded model, the caller's own fit): n_cat dense
- * tables concatenated in value/present, table i covering keys key_lo[i] .. key_lo[i] +
- * n_keys[i] - 1; gmean is the value of unseen keys. */
+/* The reference's Encoders (src/encoding.rs:16, one key -> value map per categorical
+ * feature) built from maps held elsewhere (the caller's own fit, a loaded model): n_cat
+ * dense tables concatenated in value/present, table i covering keys key_lo[i] ..
+ * key_lo[i] + n_keys[i] - 1; gmean is the value of unseen keys. */
 int rw_encoders_create(uint32_t n_cat, const int64_t* key_lo, const uint64_t* n_keys,
                        const float* value, const uint8_t* present, float gmean,
                        rw_encoders** out);
