@@ -106,23 +106,31 @@ typedef struct rw_model {
 /* ---- contexts --------------------------------------------------------------- */
 
 /* Replaces CudaContext::new(cfg.gpu) (src/booster.rs:137) and, for --serve, the
- * resident shared context (Booster::with_ctx, src/booster.rs:159). n_gpus must be 1;
- * multi-GPU training uses one process per GPU with rw_ctx_create_rank. */
+ * resident shared context (Booster::with_ctx, src/booster.rs:159). With n_gpus > 1 the
+ * one context drives every listed GPU from this process (one rank per GPU inside the
+ * library, one host thread each per call): datasets shard rows over them, fits run all
+ * ranks, host-buffer scoring shards rows, device-pointer entry points use the first
+ * GPU. */
 int rw_ctx_create(const int* gpu_ids, int n_gpus, rw_ctx** out);
 
-/* One process per GPU: rank `rank` of `world` on device gpu_id, joined by an NCCL
- * communicator built from the 128-byte id that rank 0 obtained with
- * rw_nccl_unique_id and broadcast out of band. With world == 1, id may be NULL. */
+/* No counterpart in the reference (rustwood runs one process on one GPU): one process
+ * per GPU, rank `rank` of `world` on device gpu_id, joined by an NCCL communicator built
+ * from the 128-byte id that rank 0 obtained with rw_nccl_unique_id and broadcast out of
+ * band. With world == 1, id may be NULL. */
 int rw_ctx_create_rank(int gpu_id, int rank, int world, const void* nccl_id, rw_ctx** out);
 int rw_nccl_unique_id(void* out128);
 /* Destroys the context; its datasets and uploaded models must be destroyed first (they
  * live in the context's memory pool). */
 void rw_ctx_destroy(rw_ctx* ctx);
+/* The message behind the last failing call on ctx (what rustwood's Box<dyn Error>
+ * carries, src/booster.rs:32); with ctx == NULL, the last failure on this thread of a
+ * call that had no context to record it on. */
 const char* rw_last_error(const rw_ctx* ctx);
 /* The context's CUDA stream (a cudaStream_t), for callers that order their own work
  * or CUDA events with the library's. */
 void* rw_ctx_stream(const rw_ctx* ctx);
-/* Bound (milliseconds) on each collective wait; 0 = wait forever. Default 60000. */
+/* Multi-GPU only (no counterpart in the reference): bound (milliseconds) on each
+ * collective wait; 0 = wait forever. Default 60000. */
 int rw_ctx_set_timeout(rw_ctx* ctx, int64_t ms);
 /* 1 when a wait on a peer rank expired on this context (its exchanges can no longer be
  * trusted: later fits return an error; recreate the context), else 0. */
@@ -144,7 +152,8 @@ int rw_dataset_create_device(rw_ctx* ctx, const float* d_x_rowmajor, const float
                              int32_t pack4, uint64_t n_global, uint64_t row_offset,
                              rw_dataset** out);
 void rw_dataset_destroy(rw_dataset* ds);
-/* Copy the binned matrix out, feature-major [nf][n] u8 (unpacked). */
+/* Copy out the binned matrix fit_inner builds (bin_features, src/booster.rs:255-277),
+ * feature-major [nf][n] u8 (unpacked). */
 int rw_dataset_bins(const rw_dataset* ds, uint8_t* out);
 
 /* compute_boundaries (src/data.rs:86-146) on the GPU for row-major x already in device
@@ -195,7 +204,8 @@ int rw_predict_f32(rw_ctx* ctx, const rw_model* m, const float* x_rowmajor, uint
  * leafval and base_score are not used. leafvar is rw_fit's PGBM output. */
 int rw_predict_var_f32(rw_ctx* ctx, const rw_model* m, const float* leafvar,
                        const float* x_rowmajor, uint64_t n, uint32_t nf, float* out);
-/* Same margins from pre-binned feature-major u8 rows bins[nf][n] and thr_bin. */
+/* Same margins from pre-binned feature-major u8 rows bins[nf][n] and thr_bin (the
+ * reference scores binned rows in bench_throughput, src/booster.rs:654-698). */
 int rw_predict_u8(rw_ctx* ctx, const rw_model* m, const uint8_t* bins_featmajor, uint64_t n,
                   uint32_t nf, float* out);
 
@@ -284,7 +294,7 @@ int rw_model_thr_bins(const rw_model* m, const float* cuts, uint32_t n_bins, uin
 /* base_score (src/booster.rs:201-205 / 280-284). */
 float rw_base_score(const float* y, uint64_t n, int32_t objective);
 
-/* ---- test hooks ---------------------------------------------------------------- */
+/* ---- test hooks (no counterpart in the reference) ------------------------------ */
 
 /* Runs the production histogram kernel once on caller data: node[n] (>= 0 in-sample,
  * < 0 excluded), g/h[n], scales 2^e_g / 2^e_h; odd_only keys odd nodes by node>>1.
